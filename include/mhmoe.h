@@ -1,0 +1,148 @@
+/*
+ * mhmoe.h — C ABI of the B200 (sm_100a) MAGI-2 MoE expert hot path.
+ *
+ * Drop-in replacement for the reference's `inference/flash_mh_moe` package
+ * (router top-k, global sort, fused expert FFN) plus the expert-parallel
+ * dispatch/combine.  Every entry point takes raw device pointers, shapes and a
+ * cudaStream_t (passed as void*), enqueues work on that stream and returns an
+ * mhmoe_status.  Nothing here allocates device memory: callers own every
+ * buffer, including the scratch buffers whose sizes the *_bytes queries give.
+ * No entry point synchronises the stream.
+ *
+ * Kernels that wait on on-chip barriers give up after `timeout_ns` (0 selects
+ * the default of 2 s) and record MHMOE_ERR_TIMEOUT in the optional device word
+ * `dev_status` (int32, caller-zeroed); the host reads it when convenient.
+ *
+ * Layout conventions (row-major unless stated):
+ *   x            bf16 [S, H, dh]   strides in elements; dh stride must be 1
+ *   logits       fp32 [H, S, E]
+ *   probs / idx  fp32 / int64 [H, S, K]
+ *   gather_ids   int32 [R], probs_sorted fp32 [R], expert_offsets int64 [H*E+1]
+ *   NVFP4 matrix: packed E2M1 bytes [rows, K/2] (low nibble = even k), UE4M3
+ *                 scales in 512-byte "SF atoms" (128 rows x 64 K-elements each;
+ *                 row m, scale column c at (m%32)*16 + (m/32)*4 + c; atoms
+ *                 K-fastest), one fp32 second-level scale per matrix or row.
+ */
+#ifndef MHMOE_H_
+#define MHMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MHMOE_API __attribute__((visibility("default")))
+#else
+#define MHMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MHMOE_OK = 0,
+  MHMOE_ERR_ARGS = 1,      /* bad shape, stride, alignment or null pointer */
+  MHMOE_ERR_ARCH = 2,      /* device is not sm_100 */
+  MHMOE_ERR_LAUNCH = 3,    /* CUDA launch / runtime error */
+  MHMOE_ERR_TIMEOUT = 4,   /* a bounded on-chip wait gave up (device-side) */
+  MHMOE_ERR_DRIVER = 5,    /* driver entry point / tensor-map encode failed */
+  MHMOE_ERR_PEER = 6,      /* expert-parallel peer wait gave up (device-side) */
+  MHMOE_ERR_CAPACITY = 7   /* a size exceeds a compiled-in maximum */
+} mhmoe_status;
+
+/* Library identity and diagnostics. */
+MHMOE_API int mhmoe_version(void);
+MHMOE_API const char* mhmoe_status_string(int status);
+/* Last CUDA error text recorded by a failing call on this host thread. */
+MHMOE_API const char* mhmoe_last_error(void);
+
+/* ───────────────────────── router ───────────────────────── */
+
+/* Router logits: logits[h,s,e] = sum_d x[s,h,d] * gate[h*E+e, d] in fp32.
+ * Replaces the fp32 einsum of CoreMultiHeadMoE._route
+ * (inference/model/magi2_preview.py:2588-2591).  gate is fp32 [H*E, dh]. */
+MHMOE_API int mhmoe_router_logits(const void* x, int64_t x_stride_s, int64_t x_stride_h, const float* gate, int S, int H,
+                        int dh, int E, float* logits, void* stream);
+
+/* Top-k gating from logits.  Replaces compute_topk_probs_and_indices
+ * (inference/flash_mh_moe/route.py:157-199 -> :28-148).
+ * score_func: 0 softmax, 1 sigmoid.  expert_bias fp32 [H*E] or NULL.
+ * num_virtual_group > 1 enables the two-stage group selection (route.py:61-104).
+ * route_scale multiplies the (normalised) probs, as CoreMultiHeadMoE._route does
+ * (magi2_preview.py:2600); pass 1.0 for the plain route.py contract.
+ * Outputs: probs fp32 [H,S,K]; idx int64 [H,S,K], sorted by descending score,
+ * ties to the lower expert id.  E <= 1024, K <= 32. */
+MHMOE_API int mhmoe_topk(const float* logits, const float* expert_bias, int H, int S, int E, int K, int score_func,
+               int num_virtual_group, int topk_virtual_group, int route_norm, float norm_eps, float route_scale,
+               float* probs, int64_t* idx, void* stream);
+
+/* ───────────────────────── permutation ───────────────────────── */
+
+/* Scratch bytes for mhmoe_global_sort (int32 chunk histograms). */
+MHMOE_API size_t mhmoe_global_sort_workspace_bytes(int H, int S, int K, int E);
+
+/* Stable counting sort of the flat (h,s,k) entries by global expert h*E+idx.
+ * Replaces flash_mh_moe_global_sort (inference/flash_mh_moe/route.py:209-253):
+ * gather_ids int32 [R], probs_sorted fp32 [R], expert_offsets int64 [H*E+1],
+ * bit-identical to argsort(stable=True).  row_of_flat int32 [R] (optional):
+ * the sorted position of flat entry f.  H*E <= 12288.  An expert id outside
+ * [0, E) is never used as an index: the entry is dropped and MHMOE_ERR_ARGS is
+ * recorded in dev_status. */
+MHMOE_API int mhmoe_global_sort(const float* topk_probs, const int64_t* topk_idx, int H, int S, int K, int E,
+                      void* workspace, int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
+                      int32_t* row_of_flat, int* dev_status, void* stream);
+
+/* ───────────────────────── expert FFN (NVFP4) ───────────────────────── */
+
+/* Upper bound of 128-row tiles for R routed rows over n_experts groups. */
+MHMOE_API int64_t mhmoe_max_mtiles(int64_t R, int n_experts);
+
+/* Scratch bytes of mhmoe_ffn_nvfp4 for R rows, S tokens, H heads, dh, de, H*E experts. */
+MHMOE_API size_t mhmoe_ffn_workspace_bytes(int64_t R, int S, int H, int dh, int de, int n_experts);
+
+/* Pack reference-layout weights into the NVFP4 operand layout (quantise on load).
+ *   kind 0 (gate/up): w0 = W_gate, w1 = W_up, both [n_experts, dh, de] (bf16);
+ *        out data [n_experts, 2*de, dh/2] with gate/up rows interleaved in groups
+ *        of 16, sf atoms [n_experts, 2*de*dh/16], gscale [2, n_experts] (gate, up).
+ *   kind 1 (down): w0 = W_down [n_experts, de, dh] (bf16), w1 = NULL;
+ *        out data [n_experts, dh, de/2], sf atoms [n_experts, dh*de/16], gscale [n_experts].
+ * gscale = amax(matrix)/2688.  Scratch: amax fp32 [2*n_experts] (caller-zeroed not required). */
+MHMOE_API int mhmoe_pack_weights_nvfp4(int kind, const void* w0, const void* w1, int n_experts, int dh, int de,
+                             uint8_t* data, uint8_t* sf, float* gscale, float* amax_scratch, void* stream);
+
+/* Fused expert FFN on NVFP4 operands.  Replaces flash_mh_moe_fwd / mh_moe_fwd_func
+ * (inference/flash_mh_moe/fwd.py:16-40, triton/mh_moe_fwd.py:271-373): gather ->
+ * x quantise (per row) -> grouped GEMM gate/up + SwiGLU7 + hidden quantise ->
+ * grouped GEMM down x prob -> deterministic combine into y [S,H,dh] bf16.
+ * R = number of routed rows, n_experts = H*E (flattened).  dh % 256 == 0,
+ * de % 256 == 0.  `tok_rows`/`tok_offsets` (optional) give each (s,h) its rows
+ * (row_of_flat with fixed K when tok_offsets == NULL and k_fixed > 0); when both
+ * are NULL the mapping is derived from gather_ids.  workspace: see
+ * mhmoe_ffn_workspace_bytes. */
+MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
+                    int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                    const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                    const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                    const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
+                    void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
+                    void* stream);
+
+/* ───────────────────────── building blocks (tests, EP) ───────────────────────── */
+
+/* Per-row NVFP4 quantisation of bf16 rows x[r, 0:K] (row pitch in elements):
+ * data [M, K/2], sf atoms, gscale [M] = amax(row)/2688.  K % 64 == 0. */
+MHMOE_API int mhmoe_quantize_rows_nvfp4(const void* x, int64_t row_pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
+                              float* gscale, void* stream);
+
+/* Raw block-scaled grouped GEMM for verification: acc[rows, N] fp32 =
+ * A (NVFP4, rows grouped in 128-row tiles by tile_expert) x B[e]^T (NVFP4) with
+ * no second-level scales applied.  a rows = 128 * n_mtiles. */
+MHMOE_API int mhmoe_gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
+                         const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out,
+                         int* dev_status, uint64_t timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MHMOE_H_ */

@@ -1,0 +1,221 @@
+// extern "C" entry points of libmhmoe (declared in include/mhmoe.h).
+//
+// Each entry point validates shapes, strides and alignment on the host, checks the
+// device architecture once per device, enqueues its kernels on the caller's stream and
+// maps CUDA errors to mhmoe_status.  No entry point allocates device memory.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail_cuda(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return MHMOE_ERR_LAUNCH;
+}
+
+int fail_args(const char* what) {
+  g_last_error = std::string("invalid argument: ") + what;
+  return MHMOE_ERR_ARGS;
+}
+
+// sm_100 check, cached per device ordinal.
+int check_arch() {
+  static int cached[64];   // 0 unknown, 1 ok, 2 bad
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    g_last_error = "no current CUDA device";
+    return MHMOE_ERR_ARCH;
+  }
+  if (cached[dev] == 0) {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cached[dev] = major == 10 ? 1 : 2;
+  }
+  if (cached[dev] != 1) {
+    g_last_error = "libmhmoe requires an sm_100 (B200) device";
+    return MHMOE_ERR_ARCH;
+  }
+  return MHMOE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#define MHMOE_CHECK_ARCH()          \
+  do {                              \
+    const int a_ = check_arch();    \
+    if (a_ != MHMOE_OK) return a_;  \
+  } while (0)
+
+#define MHMOE_REQUIRE(cond)                   \
+  do {                                        \
+    if (!(cond)) return fail_args(#cond);     \
+  } while (0)
+
+}  // namespace
+
+using namespace mhmoe;
+
+extern "C" {
+
+int mhmoe_version(void) { return 1; }
+
+const char* mhmoe_status_string(int status) {
+  switch (status) {
+    case MHMOE_OK: return "ok";
+    case MHMOE_ERR_ARGS: return "invalid argument";
+    case MHMOE_ERR_ARCH: return "unsupported device (sm_100 required)";
+    case MHMOE_ERR_LAUNCH: return "CUDA launch/runtime error";
+    case MHMOE_ERR_TIMEOUT: return "device-side wait timed out";
+    case MHMOE_ERR_DRIVER: return "CUDA driver entry point or tensor-map encode failed";
+    case MHMOE_ERR_PEER: return "expert-parallel peer wait timed out";
+    case MHMOE_ERR_CAPACITY: return "size exceeds a compiled-in maximum";
+    default: return "unknown status";
+  }
+}
+
+const char* mhmoe_last_error(void) { return g_last_error.c_str(); }
+
+int mhmoe_router_logits(const void* x, int64_t x_stride_s, int64_t x_stride_h, const float* gate, int S, int H,
+                        int dh, int E, float* logits, void* stream) {
+  MHMOE_REQUIRE(x && gate && logits);
+  MHMOE_REQUIRE(S >= 0 && H > 0 && E > 0 && dh > 0 && dh % 32 == 0);
+  MHMOE_CHECK_ARCH();
+  if (S == 0) return MHMOE_OK;
+  const cudaError_t e = launch_router_logits(static_cast<const __nv_bfloat16*>(x), x_stride_s, x_stride_h, gate, S,
+                                             H, dh, E, logits, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "router_logits");
+}
+
+int mhmoe_topk(const float* logits, const float* expert_bias, int H, int S, int E, int K, int score_func,
+               int num_virtual_group, int topk_virtual_group, int route_norm, float norm_eps, float route_scale,
+               float* probs, int64_t* idx, void* stream) {
+  MHMOE_REQUIRE(logits && probs && idx);
+  MHMOE_REQUIRE(H > 0 && S >= 0 && E > 0 && E <= 1024 && K > 0 && K <= 32 && K <= E);
+  MHMOE_REQUIRE(score_func == 0 || score_func == 1);
+  if (num_virtual_group > 1) {
+    MHMOE_REQUIRE(num_virtual_group <= 64 && E % num_virtual_group == 0);
+    MHMOE_REQUIRE(topk_virtual_group > 0 && topk_virtual_group <= num_virtual_group);
+  }
+  MHMOE_CHECK_ARCH();
+  if (S == 0) return MHMOE_OK;
+  const cudaError_t e = launch_topk(logits, expert_bias, H, S, E, K, score_func, num_virtual_group,
+                                    topk_virtual_group, route_norm, norm_eps, route_scale, probs, idx,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "topk");
+}
+
+size_t mhmoe_global_sort_workspace_bytes(int H, int S, int K, int E) { return global_sort_ws_bytes(H, S, K, E); }
+
+int mhmoe_global_sort(const float* topk_probs, const int64_t* topk_idx, int H, int S, int K, int E,
+                      void* workspace, int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
+                      int32_t* row_of_flat, int* dev_status, void* stream) {
+  MHMOE_REQUIRE(topk_probs && topk_idx && workspace && gather_ids && probs_sorted && expert_offsets);
+  MHMOE_REQUIRE(H > 0 && S >= 0 && K > 0 && E > 0);
+  MHMOE_REQUIRE((int64_t)H * E <= 12288);
+  MHMOE_REQUIRE((int64_t)H * S * K < (int64_t)1 << 31);
+  MHMOE_CHECK_ARCH();
+  if (S == 0) {
+    const cudaError_t e =
+        cudaMemsetAsync(expert_offsets, 0, sizeof(int64_t) * (H * E + 1), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "global_sort");
+  }
+  const cudaError_t e = launch_global_sort(topk_probs, topk_idx, H, S, K, E, workspace, gather_ids, probs_sorted,
+                                           expert_offsets, row_of_flat, dev_status,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "global_sort");
+}
+
+int64_t mhmoe_max_mtiles(int64_t R, int n_experts) { return mtiles_upper_bound(R, n_experts); }
+
+size_t mhmoe_ffn_workspace_bytes(int64_t R, int S, int H, int dh, int de, int n_experts) {
+  return ffn_workspace_bytes(R, (int64_t)S * H, dh, de, n_experts);
+}
+
+int mhmoe_pack_weights_nvfp4(int kind, const void* w0, const void* w1, int n_experts, int dh, int de,
+                             uint8_t* data, uint8_t* sf, float* gscale, float* amax_scratch, void* stream) {
+  MHMOE_REQUIRE(kind == 0 || kind == 1);
+  MHMOE_REQUIRE(w0 && data && sf && gscale && amax_scratch);
+  MHMOE_REQUIRE(kind == 1 || w1);
+  MHMOE_REQUIRE(n_experts > 0 && dh > 0 && de > 0 && dh % 128 == 0 && de % 128 == 0);
+  MHMOE_REQUIRE(aligned16(w0) && (kind == 1 || aligned16(w1)) && aligned16(data));
+  MHMOE_CHECK_ARCH();
+  const cudaError_t e = launch_pack_weights(kind, static_cast<const __nv_bfloat16*>(w0),
+                                            static_cast<const __nv_bfloat16*>(w1), n_experts, dh, de, data, sf,
+                                            gscale, amax_scratch, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "pack_weights_nvfp4");
+}
+
+int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
+                    int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                    const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                    const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                    const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
+                    void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
+                    void* stream) {
+  MHMOE_REQUIRE(x && y && expert_offsets && gu_data && gu_sf && gu_gscale && dn_data && dn_sf && dn_gscale);
+  MHMOE_REQUIRE(S >= 0 && H > 0 && n_experts > 0 && n_experts % H == 0 && R >= 0);
+  MHMOE_REQUIRE(dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
+  MHMOE_REQUIRE(R < ((int64_t)1 << 31) - 128 * (int64_t)n_experts);
+  MHMOE_REQUIRE(aligned16(x) && x_stride_s % 8 == 0 && x_stride_h % 8 == 0);
+  MHMOE_REQUIRE(aligned16(y) && y_stride_s % 8 == 0 && y_stride_h % 8 == 0);
+  MHMOE_REQUIRE(aligned16(gu_data) && aligned16(dn_data) && aligned16(gu_sf) && aligned16(dn_sf));
+  MHMOE_REQUIRE(tok_rows || !tok_offsets);
+  MHMOE_REQUIRE(!tok_rows || tok_offsets || k_fixed > 0);
+  MHMOE_CHECK_ARCH();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (S == 0) return MHMOE_OK;
+  if (R == 0) {   // no routed rows: y = 0 (reference: mh_moe_fwd.py:297-298)
+    cudaError_t e;
+    if (y_stride_h == dh && y_stride_s == (int64_t)H * dh) {
+      e = cudaMemsetAsync(y, 0, sizeof(__nv_bfloat16) * (size_t)S * H * dh, st);
+    } else {
+      e = cudaSuccess;
+      for (int64_t s = 0; s < S && e == cudaSuccess; ++s)
+        e = cudaMemset2DAsync(static_cast<__nv_bfloat16*>(y) + s * y_stride_s, sizeof(__nv_bfloat16) * y_stride_h, 0,
+                              sizeof(__nv_bfloat16) * dh, H, st);
+    }
+    return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ffn_nvfp4 (zero fill)");
+  }
+  MHMOE_REQUIRE(workspace && gather_ids && probs_sorted);
+  cudaError_t ce = cudaSuccess;
+  const int rc = ffn_nvfp4(static_cast<const __nv_bfloat16*>(x), x_stride_s, x_stride_h, S, H, dh, de, n_experts, R,
+                           gather_ids, probs_sorted, expert_offsets, gu_data, gu_sf, gu_gscale, dn_data, dn_sf,
+                           dn_gscale, tok_rows, tok_offsets, k_fixed, workspace, static_cast<__nv_bfloat16*>(y),
+                           y_stride_s, y_stride_h, dev_status, timeout_ns, st, &ce);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4");
+  if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
+  return rc;
+}
+
+int mhmoe_quantize_rows_nvfp4(const void* x, int64_t row_pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
+                              float* gscale, void* stream) {
+  MHMOE_REQUIRE(x && data && sf && gscale);
+  MHMOE_REQUIRE(M >= 0 && K > 0 && K % 64 == 0 && row_pitch % 8 == 0 && aligned16(x) && aligned16(data));
+  MHMOE_CHECK_ARCH();
+  if (M == 0) return MHMOE_OK;
+  const cudaError_t e = launch_quantize_rows(static_cast<const __nv_bfloat16*>(x), row_pitch, M, K, data, sf, gscale,
+                                             static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "quantize_rows_nvfp4");
+}
+
+int mhmoe_gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
+                         const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out,
+                         int* dev_status, uint64_t timeout_ns, void* stream) {
+  MHMOE_REQUIRE(a_data && a_sf && tile_expert && b_data && b_sf && out);
+  MHMOE_REQUIRE(n_mtiles > 0 && n_experts > 0 && N % 256 == 0 && K % 256 == 0 && N > 0 && K > 0);
+  MHMOE_REQUIRE(aligned16(a_data) && aligned16(b_data) && aligned16(a_sf) && aligned16(b_sf));
+  MHMOE_CHECK_ARCH();
+  cudaError_t ce = cudaSuccess;
+  const int rc = gemm_nvfp4_raw(a_data, a_sf, n_mtiles, tile_expert, b_data, b_sf, n_experts, N, K, out, dev_status,
+                                timeout_ns, static_cast<cudaStream_t>(stream), &ce);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "gemm_nvfp4_raw");
+  return rc;
+}
+
+}  // extern "C"

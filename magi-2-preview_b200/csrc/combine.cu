@@ -1,0 +1,108 @@
+// Deterministic weighted combine: y[s, h, :] = bf16( sum over the (token, head)'s
+// routed rows r, in ascending r, of P[r, :] ) with fp32 accumulation.
+//
+// Replaces the scatter of the reference FFN: the bf16 atomic_add of
+// _mh_moe_fwd_kernel (inference/flash_mh_moe/triton/mh_moe_fwd.py:213-221) and the
+// deterministic _scatter_back (:229-255).  P already holds bf16(y_acc * prob) per
+// sorted row, exactly the values the reference scatters; the sum is taken in fp32
+// in a fixed order, so the result is run-to-run identical.
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+constexpr int COMBINE_WARPS = 4;
+
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, int dh, int S, int H,
+                               const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
+                               int k_fixed, int64_t R, __nv_bfloat16* __restrict__ y, int64_t sy_s, int64_t sy_h) {
+  __shared__ int srt[COMBINE_WARPS][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
+  if (key >= (int64_t)H * S) return;
+  const int h = (int)(key / S), s = (int)(key % S);
+  int64_t begin;
+  int cnt;
+  if (tok_offsets) {
+    begin = tok_offsets[key];
+    cnt = tok_offsets[key + 1] - (int)begin;
+  } else {
+    begin = key * k_fixed;
+    cnt = k_fixed;
+  }
+  __nv_bfloat16* yrow = y + (int64_t)s * sy_s + (int64_t)h * sy_h;
+  const int nvec = dh / 8;
+
+  if (cnt <= 32) {
+    // rank sort of <= 32 row ids (ascending; ids are distinct)
+    int r = lane < cnt ? tok_rows[begin + lane] : 0x7fffffff;
+    if (r < 0 || r >= R) r = 0x7fffffff;            // invalid id: dropped
+    int rank = 0;
+    for (int j = 0; j < 32; ++j) {
+      const int o = __shfl_sync(0xffffffffu, r, j);
+      rank += (o < r) || (o == r && j < lane);
+    }
+    srt[warp][rank] = r;
+    __syncwarp();
+    int nvalid = 0;
+    for (int j = 0; j < cnt; ++j) nvalid += srt[warp][j] != 0x7fffffff;
+    for (int c = lane; c < nvec; c += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < nvalid; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(P + (int64_t)srt[warp][j] * dh + c * 8);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
+          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u));
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(yrow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    // rare long lists: ascending selection, one row at a time
+    for (int c = lane; c < nvec; c += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      int last = -1;
+      for (int it = 0; it < cnt; ++it) {
+        int best = 0x7fffffff;
+        for (int j = 0; j < cnt; ++j) {
+          const int rr = tok_rows[begin + j];
+          if (rr > last && rr < best && rr < R) best = rr;
+        }
+        if (best == 0x7fffffff) break;
+        last = best;
+        const uint4 u = *reinterpret_cast<const uint4*>(P + (int64_t)best * dh + c * 8);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
+          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u));
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(yrow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+cudaError_t launch_combine(const __nv_bfloat16* P, int dh, int S, int H, const int32_t* tok_rows,
+                           const int32_t* tok_offsets, int k_fixed, int64_t R, __nv_bfloat16* y, int64_t sy_s,
+                           int64_t sy_h, cudaStream_t st) {
+  const int64_t keys = (int64_t)H * S;
+  combine_kernel<<<(unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st>>>(
+      P, dh, S, H, tok_rows, tok_offsets, k_fixed, R, y, sy_s, sy_h);
+  return cudaGetLastError();
+}
+
+}  // namespace mhmoe

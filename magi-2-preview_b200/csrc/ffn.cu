@@ -1,0 +1,222 @@
+// Host orchestration of the NVFP4 expert FFN: workspace carving, TMA descriptors and
+// the launch sequence  tile tables -> gather/quantise -> gate/up GEMM (+SwiGLU7,
+// hidden quantise) -> down GEMM (x prob) -> token map -> combine.
+#include <cstring>
+#include <mutex>
+
+#include "ffn_gemm.cuh"
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+// ───────────────────────────── driver entry points ─────────────────────────────
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor map over [rows, inner_bytes] (row pitch = inner_bytes), 128-B swizzle.
+cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows,
+                              uint32_t box_inner, uint32_t box_rows) {
+  PFN_encodeTiled fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {inner_bytes, rows};
+  const cuuint64_t strides[1] = {inner_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+template <int EPI>
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const FfnGemmParams& p,
+                               int64_t max_work, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(ffn_gemm_nvfp4_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    GEMM_SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), max_work));
+  ffn_gemm_nvfp4_kernel<EPI><<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+// ───────────────────────────── workspace layout ─────────────────────────────
+
+struct FfnWorkspace {
+  int* cu_tiles;
+  int* tile_expert;
+  int* tile_row0;
+  int* tile_rows;
+  uint8_t* a_data;
+  uint8_t* a_sf;
+  float* a_gscale;
+  uint8_t* h_data;
+  uint8_t* h_sf;
+  __nv_bfloat16* P;
+  int32_t* tok_offsets;
+  int32_t* tok_rows;
+  void* tok_ws;
+  size_t bytes;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static FfnWorkspace carve(uint8_t* base, int64_t R, int64_t T, int dh, int de, int HE) {
+  FfnWorkspace w{};
+  const int64_t mt = mtiles_upper_bound(R, HE);
+  const int64_t rows = mt * 128;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 1024);
+    return p;
+  };
+  w.cu_tiles = reinterpret_cast<int*>(take(sizeof(int) * (HE + 1)));
+  w.tile_expert = reinterpret_cast<int*>(take(sizeof(int) * mt));
+  w.tile_row0 = reinterpret_cast<int*>(take(sizeof(int) * mt));
+  w.tile_rows = reinterpret_cast<int*>(take(sizeof(int) * mt));
+  w.a_data = take((size_t)rows * dh / 2);
+  w.a_sf = take((size_t)rows * dh / 16);
+  w.a_gscale = reinterpret_cast<float*>(take(sizeof(float) * rows));
+  w.h_data = take((size_t)rows * de / 2);
+  w.h_sf = take((size_t)rows * de / 16);
+  w.P = reinterpret_cast<__nv_bfloat16*>(take(sizeof(__nv_bfloat16) * (size_t)R * dh));
+  w.tok_offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (T + 1)));
+  w.tok_rows = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(R, 1)));
+  w.tok_ws = take(token_rows_ws_bytes(T));
+  w.bytes = off;
+  return w;
+}
+
+size_t ffn_workspace_bytes(int64_t R, int64_t T, int dh, int de, int HE) {
+  return carve(nullptr, R, T, dh, de, HE).bytes;
+}
+
+int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh, int de, int HE, int64_t R,
+              const int32_t* gather_ids, const float* probs_sorted, const int64_t* expert_offsets,
+              const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
+              const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
+              int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
+              uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr) {
+  const int64_t T = (int64_t)S * H;
+  FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
+  const int64_t max_mt = mtiles_upper_bound(R, HE);
+  const int64_t rows = max_mt * 128;
+  cudaError_t e;
+#define MHMOE_TRY(call)        \
+  do {                         \
+    e = (call);                \
+    if (e != cudaSuccess) {    \
+      *cerr = e;               \
+      return MHMOE_ERR_LAUNCH; \
+    }                          \
+  } while (0)
+
+  MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
+                               status, st));
+  MHMOE_TRY(launch_quant_gather(x, sx_s, sx_h, S, dh, HE / H, gather_ids, w.cu_tiles, HE, max_mt, w.tile_expert,
+                                w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale, status, st));
+
+  CUtensorMap ta1, tb1, ta2, tb2;
+  if (encode_tmap_2d_u8(&ta1, w.a_data, dh / 2, rows, 128, 128) != cudaSuccess ||
+      encode_tmap_2d_u8(&tb1, gu_data, dh / 2, (uint64_t)HE * 2 * de, 128, 256) != cudaSuccess ||
+      encode_tmap_2d_u8(&ta2, w.h_data, de / 2, rows, 128, 128) != cudaSuccess ||
+      encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess)
+    return MHMOE_ERR_DRIVER;
+
+  FfnGemmParams p1{};
+  p1.sfa = w.a_sf;
+  p1.sfb = gu_sf;
+  p1.n_mtiles_dev = w.cu_tiles + HE;
+  p1.n_mtiles_host = (int)max_mt;
+  p1.tile_expert = w.tile_expert;
+  p1.tile_row0 = w.tile_row0;
+  p1.tile_rows = w.tile_rows;
+  p1.K = dh;
+  p1.N = 2 * de;
+  p1.row_gscale = w.a_gscale;
+  p1.gs_gate = gu_gscale;
+  p1.gs_up = gu_gscale + HE;
+  p1.h_data = w.h_data;
+  p1.h_sf = w.h_sf;
+  p1.status = status;
+  p1.timeout_ns = timeout_ns;
+  MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, p1, max_mt * (2 * de / GEMM_BN), st));
+
+  FfnGemmParams p2 = p1;
+  p2.sfa = w.h_sf;
+  p2.sfb = dn_sf;
+  p2.K = de;
+  p2.N = dh;
+  p2.probs = probs_sorted;
+  p2.gs_down = dn_gscale;
+  p2.out_bf16 = w.P;
+  MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, p2, max_mt * (dh / GEMM_BN), st));
+
+  const int32_t* rows_map = tok_rows;
+  const int32_t* offs_map = tok_offsets;
+  int kf = k_fixed;
+  if (!tok_rows) {
+    MHMOE_TRY(launch_token_rows(gather_ids, max_mt, w.cu_tiles, HE, HE / H, S, H, w.tile_expert, w.tile_row0,
+                                w.tile_rows, w.tok_ws, w.tok_offsets, w.tok_rows, status, st));
+    rows_map = w.tok_rows;
+    offs_map = w.tok_offsets;
+    kf = 0;
+  }
+  MHMOE_TRY(launch_combine(w.P, dh, S, H, rows_map, offs_map, kf, R, y, sy_s, sy_h, st));
+#undef MHMOE_TRY
+  return MHMOE_OK;
+}
+
+int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
+                   const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out, int* status,
+                   uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr) {
+  CUtensorMap ta, tb;
+  if (encode_tmap_2d_u8(&ta, a_data, K / 2, (uint64_t)n_mtiles * 128, 128, 128) != cudaSuccess ||
+      encode_tmap_2d_u8(&tb, b_data, K / 2, (uint64_t)n_experts * N, 128, 256) != cudaSuccess)
+    return MHMOE_ERR_DRIVER;
+  FfnGemmParams p{};
+  p.sfa = a_sf;
+  p.sfb = b_sf;
+  p.n_mtiles_dev = nullptr;
+  p.n_mtiles_host = n_mtiles;
+  p.tile_expert = tile_expert;
+  p.K = K;
+  p.N = N;
+  p.out_f32 = out;
+  p.status = status;
+  p.timeout_ns = timeout_ns;
+  const cudaError_t e = launch_gemm<EPI_RAW>(ta, tb, p, (int64_t)n_mtiles * (N / GEMM_BN), st);
+  if (e != cudaSuccess) {
+    *cerr = e;
+    return MHMOE_ERR_LAUNCH;
+  }
+  return MHMOE_OK;
+}
+
+}  // namespace mhmoe

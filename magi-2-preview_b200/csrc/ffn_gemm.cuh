@@ -1,0 +1,298 @@
+// Block-scaled NVFP4 grouped GEMM for the MoE expert FFN (sm_100a, tcgen05).
+//
+// One persistent CTA per SM walks (m-tile, n-tile) work items of the grouped
+// problem.  A m-tile is 128 consecutive rows of the expert-padded row space (every
+// expert's rows start on a 128-row boundary); its expert comes from `tile_expert`.
+//
+//   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer: A tile (128 x 256 FP4 = 16 KB, 128-B swizzle), B tile
+//               (256 x 256 FP4 = 32 KB), and their UE4M3 scale atoms (2 KB + 4 KB,
+//               untiled bulk copies) into a 4-stage shared-memory ring.
+//   warp 1      TMEM owner + MMA issuer: per stage copies the scale atoms into TMEM
+//               (tcgen05.cp 32x128b.warpx4) and issues 4 x tcgen05.mma
+//               kind::mxf4nvf4 block16 (M128 N256 K64).
+//   warps 2-9   epilogue: drain the accumulator with tcgen05.ld into registers,
+//               release TMEM, then apply the fused epilogue and store.
+//
+// TMEM columns: [0,256) accumulator, [256 + 48*s, 256 + 48*(s+1)) the scale
+// factors of stage s (16 columns SFA = 4 MMAs x 4, 32 columns SFB = 4 MMAs x 8).
+//
+// Epilogues:
+//   EPI_SWIGLU  B = fused gate/up rows (interleaved by 16).  Each 32-column chunk
+//               gives 16 hidden values: h = swiglu7(acc_g * s_gate, acc_u * s_up),
+//               quantised to NVFP4 with the static hidden scale and written as the
+//               A operand (data + SF atoms) of the down GEMM.
+//   EPI_DOWN    y_row = bf16(acc * s_down * prob) written to the sorted-row partial
+//               buffer P[R, N].
+//   EPI_RAW     fp32 accumulator written as is (verification only).
+#pragma once
+
+#include "mhmoe_common.cuh"
+
+namespace mhmoe {
+
+enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2 };
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BN = 256;
+constexpr int GEMM_BK = 256;          // FP4 elements per stage = 128 bytes per row
+constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_THREADS = 320;
+constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK / 2;          // 16384
+constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK / 2;          // 32768
+constexpr int GEMM_SFA_BYTES = GEMM_BM * GEMM_BK / 16;       // 2048
+constexpr int GEMM_SFB_BYTES = GEMM_BN * GEMM_BK / 16;       // 4096
+constexpr int GEMM_STAGE_TX = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFA_BYTES + GEMM_SFB_BYTES;
+constexpr int GEMM_SMEM_BYTES =
+    GEMM_STAGES * GEMM_STAGE_TX + 256 /* barriers + tmem slot */ + 1024 /* alignment slack */;
+constexpr int GEMM_TMEM_COLS = 512;
+constexpr int GEMM_SF_COL0 = 256;
+constexpr int GEMM_SF_COLS_PER_STAGE = 48;
+
+// Static second-level scale of the SwiGLU7 hidden: |swiglu7| <= 7 * 8 = 56, 56 / 2688.
+constexpr float HIDDEN_GSCALE = 56.0f / 2688.0f;
+
+struct FfnGemmParams {
+  const uint8_t* sfa;        // A scale atoms (row space of 128 * n_mtiles rows)
+  const uint8_t* sfb;        // B scale atoms, per expert contiguous: N*K/16 bytes each
+  const int* n_mtiles_dev;   // device scalar: number of valid m-tiles (or nullptr)
+  int n_mtiles_host;         // m-tiles the buffers hold (caps n_mtiles_dev)
+  const int* tile_expert;    // [m-tile] -> flattened expert id
+  const int* tile_row0;      // [m-tile] -> first sorted row (EPI_DOWN)
+  const int* tile_rows;      // [m-tile] -> valid rows in the tile
+  int K;                     // reduction length in elements
+  int N;                     // B rows per expert
+  // EPI_SWIGLU
+  const float* row_gscale;   // [128 * n_mtiles] second-level scale of each A row
+  const float* gs_gate;      // [n_experts]
+  const float* gs_up;        // [n_experts]
+  uint8_t* h_data;           // [128 * n_mtiles, N/4]  (hidden has N/2 columns, 2 per byte)
+  uint8_t* h_sf;             // SF atoms of the hidden, K_hidden = N/2
+  // EPI_DOWN
+  const float* probs;        // [R] sorted probs
+  const float* gs_down;      // [n_experts]
+  __nv_bfloat16* out_bf16;   // [R, N]
+  // EPI_RAW
+  float* out_f32;            // [128 * n_mtiles, N]
+  int* status;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ float swiglu7(float g, float u) {
+  g = fminf(g, 7.0f);
+  u = fminf(fmaxf(u, -7.0f), 7.0f);
+  const float sig = __frcp_rn(1.0f + __expf(-1.702f * g));
+  return g * sig * (u + 1.0f);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const FfnGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + GEMM_STAGES * GEMM_A_BYTES;
+  uint8_t* sSFA = sB + GEMM_STAGES * GEMM_B_BYTES;
+  uint8_t* sSFB = sSFA + GEMM_STAGES * GEMM_SFA_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + GEMM_STAGES * GEMM_SFB_BYTES);
+  uint64_t* full_bar = bars;                       // [STAGES]
+  uint64_t* empty_bar = bars + GEMM_STAGES;        // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * GEMM_STAGES;    // accumulator ready
+  uint64_t* tempty_bar = tfull_bar + 1;            // accumulator drained
+  uint64_t* drain_bar = tfull_bar + 2;             // all issued tcgen05 ops retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GEMM_STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    mbar_init(smem_u32(tfull_bar), 1);
+    mbar_init(smem_u32(tempty_bar), 8);
+    mbar_init(smem_u32(drain_bar), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), GEMM_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_mtiles = p.n_mtiles_dev ? min(*p.n_mtiles_dev, p.n_mtiles_host) : p.n_mtiles_host;
+  const int n_ntiles = p.N / GEMM_BN;
+  const int n_kblk = p.K / GEMM_BK;
+  const int total = n_mtiles * n_ntiles;
+  const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
+
+  if (warp == 0) {
+    // ───────── TMA producer ─────────
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      const size_t sfa_row_atoms = (size_t)(p.K / 64);
+      const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int mt = t / n_ntiles, nt = t % n_ntiles;
+        const int e = p.tile_expert[mt];
+        const int brow = e * p.N + nt * GEMM_BN;
+        for (int kb = 0; kb < n_kblk; ++kb) {
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, GEMM_STAGE_TX);
+          tma_load_2d(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
+          tma_load_2d(smem_u32(sB + stage * GEMM_B_BYTES), &tmB, fb, kb * (GEMM_BK / 2), brow);
+          const uint8_t* sfa_src = p.sfa + ((size_t)mt * sfa_row_atoms + (size_t)kb * 4) * 512;
+          bulk_load(smem_u32(sSFA + stage * GEMM_SFA_BYTES), sfa_src, GEMM_SFA_BYTES, fb);
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb) {
+            const uint8_t* sfb_src = p.sfb + (size_t)e * sfb_expert_bytes +
+                                     ((size_t)(nt * 2 + nb) * sfa_row_atoms + (size_t)kb * 4) * 512;
+            bulk_load(smem_u32(sSFB + stage * GEMM_SFB_BYTES + nb * 2048), sfb_src, 2048, fb);
+          }
+          if (++stage == GEMM_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ───────── MMA issuer ─────────
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      constexpr uint32_t idesc = idesc_nvf4(GEMM_BM, GEMM_BN);
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        tc_fence_after();
+        for (int kb = 0; kb < n_kblk; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          tc_fence_after();
+          const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
+          const uint32_t tsfb = tsfa + 16;
+          const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
+          const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            tc_cp_32x128b_warpx4(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
+            tc_cp_32x128b_warpx4(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
+            tc_cp_32x128b_warpx4(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
+          }
+          const uint32_t a_s = smem_u32(sA + stage * GEMM_A_BYTES);
+          const uint32_t b_s = smem_u32(sB + stage * GEMM_B_BYTES);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            mma_nvf4(tmem_base, sdesc_kmajor_sw128(a_s + j * 32), sdesc_kmajor_sw128(b_s + j * 32), idesc,
+                     tsfa + j * 4, tsfb + j * 8, (kb | j) != 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == GEMM_STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc_commit(smem_u32(tfull_bar));
+        acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ───────── epilogue warps 2..9 ─────────
+    const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;       // accumulator columns [128*half, 128*half + 128)
+    const int m = q * 32 + lane;            // tile row owned by this thread
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int mt = t / n_ntiles, nt = t % n_ntiles;
+      if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 128);
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 0, (r + 0));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 32, (r + 32));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 64, (r + 64));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 96, (r + 96));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
+
+      const int e = p.tile_expert[mt];
+      const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
+      if constexpr (EPI == EPI_SWIGLU) {
+        const float gr = p.row_gscale[prow];
+        const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
+        const float s_up = __fmul_rn(gr, p.gs_up[e]);
+        const int hid_cols = p.N / 2;
+        uint32_t words[8];
+        uint32_t sfw = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float h[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float g = __fmul_rn(__uint_as_float(r[c * 32 + i]), s_gate);
+            const float u = __fmul_rn(__uint_as_float(r[c * 32 + 16 + i]), s_up);
+            h[i] = swiglu7(g, u);
+          }
+          uint32_t w2[2];
+          const uint32_t sf = quant_block16(h, HIDDEN_GSCALE, w2);
+          words[2 * c] = w2[0];
+          words[2 * c + 1] = w2[1];
+          sfw |= sf << (8 * c);
+        }
+        const int hcol0 = nt * (GEMM_BN / 2) + half * 64;          // first hidden column of this thread
+        uint4* dst = reinterpret_cast<uint4*>(p.h_data + prow * (size_t)(hid_cols / 2) + hcol0 / 2);
+        dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+        dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+        *reinterpret_cast<uint32_t*>(p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols)) =
+            sfw;
+      } else if constexpr (EPI == EPI_DOWN) {
+        if (m < p.tile_rows[mt]) {
+          const size_t row = (size_t)p.tile_row0[mt] + m;
+          const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
+          const float pr = p.probs[row];
+          uint4* dst = reinterpret_cast<uint4*>(p.out_bf16 + row * (size_t)p.N + nt * GEMM_BN + half * 128);
+#pragma unroll
+          for (int v = 0; v < 16; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[v * 8 + 2 * j]), s), pr);
+              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[v * 8 + 2 * j + 1]), s), pr);
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+              w[j] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      } else {
+        float4* dst = reinterpret_cast<float4*>(p.out_f32 + prow * (size_t)p.N + nt * GEMM_BN + half * 128);
+#pragma unroll
+        for (int v = 0; v < 32; ++v)
+          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+      }
+    }
+  }
+done:
+  if (warp == 1 && lane == 0) {
+    // Retire every tcgen05 op this thread issued before TMEM is released
+    // (matters only on an error path; on the normal path they are done already).
+    tc_commit(smem_u32(drain_bar));
+    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, timeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, GEMM_TMEM_COLS);
+  }
+}
+
+}  // namespace mhmoe

@@ -1,0 +1,64 @@
+// Internal launcher declarations shared by the .cu files of libmhmoe.
+#pragma once
+
+#include <algorithm>
+#include <cstdint>
+
+#include "mhmoe_common.cuh"
+
+namespace mhmoe {
+
+// Upper bound of 128-row tiles for R rows spread over n_experts groups.
+inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts) { return (R + 127) / 128 + n_experts; }
+
+// permute.cu
+int sort_chunk_size(int64_t R);
+size_t global_sort_ws_bytes(int H, int S, int K, int E);
+cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, int S, int K, int E, void* ws,
+                               int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
+                               int32_t* row_of_flat, int* status, cudaStream_t st);
+cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
+                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st);
+size_t token_rows_ws_bytes(int64_t T);
+cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, const int* cu_tiles, int HE, int E,
+                              int S, int H, const int* tile_expert, const int* tile_row0, const int* tile_rows,
+                              void* ws, int32_t* tok_offsets, int32_t* tok_rows, int* status, cudaStream_t st);
+
+// quant.cu
+cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int dh, int E_per_head,
+                                const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
+                                const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
+                                uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
+cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
+                                 float* gscale, cudaStream_t st);
+cudaError_t launch_pack_weights(int kind, const __nv_bfloat16* w0, const __nv_bfloat16* w1, int n_experts, int dh,
+                                int de, uint8_t* data, uint8_t* sf, float* gscale, float* amax, cudaStream_t st);
+
+// route.cu
+cudaError_t launch_router_logits(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, const float* gate, int S, int H,
+                                 int dh, int E, float* logits, cudaStream_t st);
+cudaError_t launch_topk(const float* logits, const float* bias, int H, int S, int E, int K, int score_func, int nvg,
+                        int tvg, int route_norm, float norm_eps, float route_scale, float* probs, int64_t* idx,
+                        cudaStream_t st);
+
+// combine.cu
+cudaError_t launch_combine(const __nv_bfloat16* P, int dh, int S, int H, const int32_t* tok_rows,
+                           const int32_t* tok_offsets, int k_fixed, int64_t R, __nv_bfloat16* y, int64_t sy_s,
+                           int64_t sy_h, cudaStream_t st);
+
+// ffn.cu
+int num_sms();
+size_t ffn_workspace_bytes(int64_t R, int64_t T, int dh, int de, int HE);
+int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh, int de, int HE, int64_t R,
+              const int32_t* gather_ids, const float* probs_sorted, const int64_t* expert_offsets,
+              const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
+              const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
+              int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
+              uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);
+int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
+                   const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out, int* status,
+                   uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);
+cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows,
+                              uint32_t box_inner, uint32_t box_rows);
+
+}  // namespace mhmoe

@@ -1,0 +1,293 @@
+// Shared device helpers for the MAGI-2 MoE hot path on sm_100a.
+//
+// Inline-PTX wrappers for mbarriers, TMA, bulk copies and the tcgen05 tensor-core
+// family, plus the NVFP4 scalar conversions.  Every wait on an mbarrier is bounded:
+// after `timeout_ns` of %globaltimer it records an error code in the caller's
+// device flag and returns false, so a broken pipeline ends the kernel with a
+// status the host reads instead of hanging the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/mhmoe.h"
+
+namespace mhmoe {
+
+// ───────────────────────────── basic helpers ─────────────────────────────
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_volatile_i32(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// ───────────────────────────── mbarriers ─────────────────────────────
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and records `code`) on timeout or when another
+// role of this grid already recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code,
+                                          uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (err && ld_volatile_i32(err) != 0) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        record_error(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ───────────────────────────── TMA / bulk copies ─────────────────────────────
+
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// 2-D tiled TMA load (no multicast). c0 = innermost coordinate (bytes for uint8 maps).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0,
+                                            int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(tmap), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared; both addresses 16-B aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// ───────────────────────────── tcgen05 ─────────────────────────────
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Arrive on `bar` once every tcgen05 op issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 inputs, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= (A .* SFA) * (B .* SFB)^T, E2M1 inputs with UE4M3 scales per 16 K-elements.
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Copy 32 rows x 16 bytes from shared memory into TMEM (4 columns), replicated to
+// all four 32-lane quadrants.
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+#define MHMOE_TMEM_LD_32x32b_X32(taddr, r)                                                                     \
+  asm volatile(                                                                                                \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"  \
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                        \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),         \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),   \
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), \
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])  \
+      : "r"(taddr))
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 "version 1" format).
+//   bits [0,14)  start address >> 4
+//   bits [16,30) leading-dimension byte offset >> 4
+//   bits [32,46) stride-dimension byte offset >> 4
+//   bits [46,48) version = 1
+//   bits [49,52) base offset (0: operands start on 1024-B swizzle-atom boundaries)
+//   bits [61,64) layout: 0 = no swizzle, 2 = 128-B swizzle
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                               uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(layout & 7u) << 61;
+  return d;
+}
+
+// K-major operand, rows of 128 B in 128-B swizzle atoms of 8 rows (1024 B).
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+  return make_sdesc(saddr, 16, 1024, 2);
+}
+
+// Scale-factor chunk for tcgen05.cp 32x128b: 32 rows of 16 B, no swizzle,
+// 8-row core matrices 128 B apart.
+__device__ __forceinline__ uint64_t sdesc_sf_chunk(uint32_t saddr) { return make_sdesc(saddr, 0, 128, 0); }
+
+// Instruction descriptor, kind::mxf4nvf4: A/B = E2M1, scales = UE4M3, K = 64, both K-major.
+__host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
+  return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f16: A/B = bf16, D = f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ───────────────────────────── NVFP4 conversions ─────────────────────────────
+
+// RNE + saturate of eight fp32 values to E2M1, packed little-endian: value i goes to
+// nibble i (the first of each pair in the low nibble of its byte).
+__device__ __forceinline__ uint32_t cvt_e2m1x8(float a0, float a1, float a2, float a3, float a4, float a5,
+                                               float a6, float a7) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(a0), "f"(a1), "f"(a2), "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7));
+  return out;
+}
+
+// RNE + saturate (448) of a non-negative fp32 to E4M3; returns the byte.
+__device__ __forceinline__ uint32_t cvt_e4m3(float a) {
+  uint16_t out;
+  asm volatile("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(out) : "f"(a), "f"(0.0f));
+  return out & 0xFFu;
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  const uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+  if (e == 0) return __uint_as_float(0) + (float)m * 0.001953125f;  // m * 2^-9
+  return __uint_as_float(((e + 120u) << 23) | (m << 20));            // (1 + m/8) * 2^(e-7)
+}
+
+// Quantise 16 fp32 values with second-level scale g (see oracle/nvfp4_ref.py for the
+// exact op sequence).  Writes 8 packed bytes to out[0..1] (little-endian words) and
+// returns the E4M3 scale byte.
+__device__ __forceinline__ uint32_t quant_block16(const float* v, float g, uint32_t out[2]) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float t = __fdiv_rn(amax, __fmul_rn(6.0f, g));
+  const uint32_t sf = cvt_e4m3(t);
+  const float sfv = e4m3_to_f32(sf);
+  if (sfv == 0.f) {
+    out[0] = out[1] = 0u;
+    return sf;
+  }
+  const float inv = __fdiv_rn(1.0f, __fmul_rn(sfv, g));
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const float* p = v + 8 * w;
+    out[w] = cvt_e2m1x8(__fmul_rn(p[0], inv), __fmul_rn(p[1], inv), __fmul_rn(p[2], inv), __fmul_rn(p[3], inv),
+                        __fmul_rn(p[4], inv), __fmul_rn(p[5], inv), __fmul_rn(p[6], inv), __fmul_rn(p[7], inv));
+  }
+  return sf;
+}
+
+// Byte offset of scale (row, sf column) in the SF-atom layout of a [rows, K] matrix.
+__host__ __device__ __forceinline__ uint64_t sf_atom_offset(uint64_t row, uint32_t sfcol, uint32_t K) {
+  const uint64_t atom = (row >> 7) * (uint64_t)(K >> 6) + (sfcol >> 2);
+  const uint32_t m = (uint32_t)(row & 127u);
+  return atom * 512u + (m & 31u) * 16u + (m >> 5) * 4u + (sfcol & 3u);
+}
+
+}  // namespace mhmoe

@@ -1,0 +1,332 @@
+// Token permutation for the MoE hot path: stable counting sort by expert, CSR
+// offsets, 128-row tile tables, and the inverse (token -> rows) map.
+//
+// Replaces flash_mh_moe_global_sort (inference/flash_mh_moe/route.py:209-253) and the
+// tile-count prep of mh_moe_fwd_func (inference/flash_mh_moe/triton/mh_moe_fwd.py:315-322).
+//
+// Stable sort = argsort(stable=True) over the flat (h, s, k) order:
+//   1. chunk histograms   hist[c][g]  (one CTA per chunk, shared-memory counters)
+//   2. column scan        hist[c][g] <- sum_{c' < c} hist[c'][g];  total[g]
+//   3. key scan           expert_offsets = exclusive scan of total; tile tables
+//   4. ordered scatter    one warp per chunk walks its entries in order; lanes that
+//                         share a key get consecutive slots via __match_any_sync, so
+//                         equal keys keep their flat order (stability).
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+__global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int SK, int E, int HE, int chunk,
+                                 int* __restrict__ hist, int* __restrict__ status) {
+  extern __shared__ int sh[];
+  for (int g = threadIdx.x; g < HE; g += blockDim.x) sh[g] = 0;
+  __syncthreads();
+  const int64_t f0 = (int64_t)blockIdx.x * chunk;
+  const int64_t f1 = min(f0 + chunk, R);
+  for (int64_t f = f0 + threadIdx.x; f < f1; f += blockDim.x) {
+    const int64_t e = idx[f];
+    if (e < 0 || e >= E) {            // out-of-range expert id: record, never index with it
+      record_error(status, MHMOE_ERR_ARGS);
+      continue;
+    }
+    const int h = (int)(f / SK);
+    atomicAdd(&sh[h * E + (int)e], 1);
+  }
+  __syncthreads();
+  int* row = hist + (size_t)blockIdx.x * HE;
+  for (int g = threadIdx.x; g < HE; g += blockDim.x) row[g] = sh[g];
+}
+
+__global__ void sort_colscan_kernel(int* __restrict__ hist, int nchunks, int HE, int* __restrict__ total) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= HE) return;
+  int run = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    int* p = hist + (size_t)c * HE + g;
+    const int v = *p;
+    *p = run;
+    run += v;
+  }
+  total[g] = run;
+}
+
+// Single CTA: expert_offsets / tile tables from per-expert counts (counts != nullptr)
+// or from given expert_offsets (counts == nullptr).
+__global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t* __restrict__ offsets_in,
+                                   int HE, int64_t* __restrict__ offsets_out, int* __restrict__ cu_tiles,
+                                   int* __restrict__ tile_expert, int* __restrict__ tile_row0,
+                                   int* __restrict__ tile_rows, int64_t max_mtiles, int* __restrict__ status) {
+  __shared__ int64_t s_carry_rows;
+  __shared__ int s_carry_tiles;
+  __shared__ int64_t s_rows[1024];
+  __shared__ int s_tiles[1024];
+  if (threadIdx.x == 0) {
+    s_carry_rows = 0;
+    s_carry_tiles = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < HE; base += 1024) {
+    const int g = base + threadIdx.x;
+    int64_t cnt = 0;
+    if (g < HE) cnt = counts ? (int64_t)counts[g] : (offsets_in[g + 1] - offsets_in[g]);
+    if (cnt < 0) {                    // non-monotonic offsets from a caller
+      record_error(status, MHMOE_ERR_ARGS);
+      cnt = 0;
+    }
+    const int nt = (int)((cnt + 127) / 128);
+    s_rows[threadIdx.x] = cnt;
+    s_tiles[threadIdx.x] = nt;
+    __syncthreads();
+    // Hillis-Steele inclusive scan over 1024 entries (two arrays)
+    for (int off = 1; off < 1024; off <<= 1) {
+      int64_t vr = 0;
+      int vt = 0;
+      if (threadIdx.x >= off) {
+        vr = s_rows[threadIdx.x - off];
+        vt = s_tiles[threadIdx.x - off];
+      }
+      __syncthreads();
+      s_rows[threadIdx.x] += vr;
+      s_tiles[threadIdx.x] += vt;
+      __syncthreads();
+    }
+    const int64_t row_excl = s_carry_rows + s_rows[threadIdx.x] - cnt;
+    const int tile_excl = s_carry_tiles + s_tiles[threadIdx.x] - nt;
+    if (g < HE) {
+      const int64_t row0 = counts ? row_excl : offsets_in[g];
+      if (offsets_out) offsets_out[g] = row0;
+      cu_tiles[g] = tile_excl;
+      for (int j = 0; j < nt; ++j) {
+        if (tile_excl + j >= max_mtiles) {   // more rows than the caller sized for
+          record_error(status, MHMOE_ERR_ARGS);
+          break;
+        }
+        tile_expert[tile_excl + j] = g;
+        tile_row0[tile_excl + j] = (int)(row0 + 128 * j);
+        tile_rows[tile_excl + j] = (int)(cnt - 128 * j < 128 ? cnt - 128 * j : 128);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 1023) {
+      s_carry_rows += s_rows[1023];
+      s_carry_tiles += s_tiles[1023];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (offsets_out) offsets_out[HE] = counts ? s_carry_rows : offsets_in[HE];
+    cu_tiles[HE] = (int)((int64_t)s_carry_tiles < max_mtiles ? (int64_t)s_carry_tiles : max_mtiles);
+  }
+}
+
+// One warp per chunk; entries of the chunk are visited in flat order, 32 at a time.
+__global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float* __restrict__ probs, int64_t R,
+                                    int S, int K, int E, int HE, int chunk, const int* __restrict__ hist,
+                                    const int64_t* __restrict__ offsets, int32_t* __restrict__ gather_ids,
+                                    float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat) {
+  // Entries with an out-of-range expert id were rejected (and recorded) by
+  // sort_hist_kernel; they get no slot here either.
+  extern __shared__ int cursor[];
+  const int lane = threadIdx.x;
+  const int* row = hist + (size_t)blockIdx.x * HE;
+  for (int g = lane; g < HE; g += 32) cursor[g] = (int)offsets[g] + row[g];
+  __syncwarp();
+  const int SK = S * K;
+  const int64_t f0 = (int64_t)blockIdx.x * chunk;
+  const int64_t f1 = min(f0 + chunk, R);
+  for (int64_t fb = f0; fb < f1; fb += 32) {
+    const int64_t f = fb + lane;
+    int g = -1 - lane;   // distinct sentinel per invalid lane
+    bool ok = false;
+    if (f < f1) {
+      const int64_t e = idx[f];
+      ok = e >= 0 && e < E;
+      if (ok) g = (int)(f / SK) * E + (int)e;
+    }
+    const bool valid_key = ok;
+    const unsigned peers = __match_any_sync(0xffffffffu, g);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    int base = 0;
+    if (valid_key) base = cursor[g];
+    __syncwarp();
+    if (valid_key && rank == 0) cursor[g] = base + __popc(peers);
+    __syncwarp();
+    if (valid_key) {
+      const int pos = base + rank;
+      gather_ids[pos] = (int32_t)((f / K) % S);
+      probs_sorted[pos] = probs[f];
+      if (row_of_flat) row_of_flat[f] = pos;
+    }
+  }
+}
+
+// ───────────── token -> rows map for arbitrary (gather_ids, expert_offsets) ─────────────
+
+// counts[h*S + s] += 1 for every row; one CTA per m-tile of the tile tables.
+__global__ void tok_count_kernel(const int32_t* __restrict__ gather_ids, const int* __restrict__ cu_tiles,
+                                 int HE, int E, int S, const int* __restrict__ tile_expert,
+                                 const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
+                                 int* __restrict__ tok_count, int* __restrict__ status) {
+  const int mt = blockIdx.x;
+  if (mt >= cu_tiles[HE]) return;
+  const int m = threadIdx.x;
+  if (m >= tile_rows[mt]) return;
+  const int h = tile_expert[mt] / E;
+  const int r = tile_row0[mt] + m;
+  const int s = gather_ids[r];
+  if (s < 0 || s >= S) {
+    record_error(status, MHMOE_ERR_ARGS);
+    return;
+  }
+  atomicAdd(&tok_count[h * S + s], 1);
+}
+
+// Exclusive scan, pass 1: per-block scan of 4096 entries, block sums out.
+__global__ void scan_block_kernel(const int* __restrict__ in, int n, int* __restrict__ out,
+                                  int* __restrict__ block_sums) {
+  __shared__ int sh[1024];
+  const int base = blockIdx.x * 4096 + threadIdx.x * 4;
+  int v[4], s = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = (base + i < n) ? in[base + i] : 0;
+    s += v[i];
+  }
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int t = threadIdx.x >= off ? sh[threadIdx.x - off] : 0;
+    __syncthreads();
+    sh[threadIdx.x] += t;
+    __syncthreads();
+  }
+  int run = sh[threadIdx.x] - s;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (base + i < n) out[base + i] = run;
+    run += v[i];
+  }
+  if (threadIdx.x == 1023) block_sums[blockIdx.x] = sh[1023];
+}
+
+// Pass 2: exclusive scan of the block sums in place (single CTA, serial carry) and
+// the grand total into out_total.
+__global__ void scan_sums_kernel(int* __restrict__ block_sums, int nblocks, int* __restrict__ out_total) {
+  __shared__ int sh[1024];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < nblocks; base += 1024) {
+    const int i = base + threadIdx.x;
+    const int v = i < nblocks ? block_sums[i] : 0;
+    sh[threadIdx.x] = v;
+    __syncthreads();
+    for (int off = 1; off < 1024; off <<= 1) {
+      const int t = threadIdx.x >= off ? sh[threadIdx.x - off] : 0;
+      __syncthreads();
+      sh[threadIdx.x] += t;
+      __syncthreads();
+    }
+    if (i < nblocks) block_sums[i] = carry + sh[threadIdx.x] - v;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry += sh[1023];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out_total = carry;
+}
+
+// Pass 3: add block offsets.
+__global__ void scan_add_kernel(int* __restrict__ out, int n, const int* __restrict__ block_sums) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] += block_sums[i / 4096];
+}
+
+__global__ void tok_fill_kernel(const int32_t* __restrict__ gather_ids, const int* __restrict__ cu_tiles, int HE,
+                                int E, int S, const int* __restrict__ tile_expert,
+                                const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
+                                const int* __restrict__ tok_offsets, int* __restrict__ tok_cursor,
+                                int32_t* __restrict__ tok_rows) {
+  const int mt = blockIdx.x;
+  if (mt >= cu_tiles[HE]) return;
+  const int m = threadIdx.x;
+  if (m >= tile_rows[mt]) return;
+  const int h = tile_expert[mt] / E;
+  const int r = tile_row0[mt] + m;
+  const int s = gather_ids[r];
+  if (s < 0 || s >= S) return;      // recorded by tok_count_kernel
+  const int t = h * S + s;
+  const int pos = tok_offsets[t] + atomicAdd(&tok_cursor[t], 1);
+  tok_rows[pos] = r;
+}
+
+// ───────────────────────────── host launchers ─────────────────────────────
+
+int sort_chunk_size(int64_t R) {
+  int64_t c = (R + 1023) / 1024;
+  c = (c + 31) / 32 * 32;
+  return (int)std::max<int64_t>(1024, c);
+}
+
+cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, int S, int K, int E, void* ws,
+                               int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
+                               int32_t* row_of_flat, int* status, cudaStream_t st) {
+  const int64_t R = (int64_t)H * S * K;
+  const int HE = H * E;
+  const int chunk = sort_chunk_size(R);
+  const int nchunks = (int)((R + chunk - 1) / chunk);
+  const int64_t mt = mtiles_upper_bound(R, HE);
+  int* hist = static_cast<int*>(ws);
+  int* total = hist + (size_t)nchunks * HE;
+  int* cu_tiles = total + HE;
+  int* tile_expert = cu_tiles + HE + 1;
+  int* tile_row0 = tile_expert + mt;
+  int* tile_rows = tile_row0 + mt;
+  const size_t shb = (size_t)HE * sizeof(int);
+  sort_hist_kernel<<<nchunks, 256, shb, st>>>(idx, R, S * K, E, HE, chunk, hist, status);
+  sort_colscan_kernel<<<(HE + 255) / 256, 256, 0, st>>>(hist, nchunks, HE, total);
+  tile_tables_kernel<<<1, 1024, 0, st>>>(total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
+                                         tile_rows, mtiles_upper_bound(R, HE), status);
+  sort_scatter_kernel<<<nchunks, 32, shb, st>>>(idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
+                                                gather_ids, probs_sorted, row_of_flat);
+  return cudaGetLastError();
+}
+
+size_t global_sort_ws_bytes(int H, int S, int K, int E) {
+  const int64_t R = (int64_t)H * S * K;
+  const int chunk = sort_chunk_size(R);
+  const int64_t nchunks = (R + chunk - 1) / chunk;
+  const int64_t mt = mtiles_upper_bound(R, (int64_t)H * E);
+  return ((size_t)(nchunks + 2) * (size_t)(H * E) + 1 + 3 * (size_t)mt) * sizeof(int) + 256;
+}
+
+cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
+                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st) {
+  tile_tables_kernel<<<1, 1024, 0, st>>>(nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert, tile_row0,
+                                         tile_rows, max_tiles, status);
+  return cudaGetLastError();
+}
+
+size_t token_rows_ws_bytes(int64_t T) {
+  const int64_t nblk = (T + 4095) / 4096;
+  return (size_t)(2 * T + nblk + 64) * sizeof(int);
+}
+
+cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, const int* cu_tiles, int HE, int E,
+                              int S, int H, const int* tile_expert, const int* tile_row0, const int* tile_rows,
+                              void* ws, int32_t* tok_offsets, int32_t* tok_rows, int* status, cudaStream_t st) {
+  const int64_t T = (int64_t)H * S;
+  int* cnt = static_cast<int*>(ws);
+  int* cursor = cnt + T;
+  int* bsums = cursor + T;
+  const int nblk = (int)((T + 4095) / 4096);
+  cudaMemsetAsync(cnt, 0, (size_t)(2 * T) * sizeof(int), st);
+  tok_count_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
+                                                         tile_rows, cnt, status);
+  scan_block_kernel<<<nblk, 1024, 0, st>>>(cnt, (int)T, tok_offsets, bsums);
+  scan_sums_kernel<<<1, 1024, 0, st>>>(bsums, nblk, tok_offsets + T);
+  scan_add_kernel<<<(unsigned)((T + 255) / 256), 256, 0, st>>>(tok_offsets, (int)T, bsums);
+  tok_fill_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
+                                                        tile_rows, tok_offsets, cursor, tok_rows);
+  return cudaGetLastError();
+}
+
+}  // namespace mhmoe

@@ -1,0 +1,195 @@
+// NVFP4 quantisers: activation gather+quantise for the gate/up GEMM, generic per-row
+// quantisation, and the weight packer (quantise on load).
+//
+// The exact fp32 op sequence of a 16-element block is quant_block16() in
+// mhmoe_common.cuh; oracle/nvfp4_ref.py states the same sequence for the CPU.
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+// Load 8 bf16 (16 B) and widen to fp32.
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float* f) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Quantise one bf16 row of K elements (K % 64 == 0) with a warp: amax -> g, then
+// lanes take 64-element groups (4 blocks), write 32 packed bytes + one 4-byte SF word.
+__device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, uint64_t out_row, uint8_t* data,
+                                               uint8_t* sf, float* gscale, int lane) {
+  float amax = 0.f;
+  if (src) {
+    for (int i = lane; i < K / 8; i += 32) {
+      float f[8];
+      load8_bf16(src + i * 8, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float g = amax > 0.f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  if (lane == 0 && gscale) gscale[out_row] = g;
+  uint8_t* drow = data + out_row * (uint64_t)(K / 2);
+  for (int grp = lane; grp < K / 64; grp += 32) {
+    uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint32_t sfw = 0;
+    if (src) {
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        float v[16];
+        load8_bf16(src + grp * 64 + b * 16, v);
+        load8_bf16(src + grp * 64 + b * 16 + 8, v + 8);
+        uint32_t w2[2];
+        const uint32_t s = quant_block16(v, g, w2);
+        words[2 * b] = w2[0];
+        words[2 * b + 1] = w2[1];
+        sfw |= s << (8 * b);
+      }
+    }
+    uint4* d = reinterpret_cast<uint4*>(drow + grp * 32);
+    d[0] = make_uint4(words[0], words[1], words[2], words[3]);
+    d[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(out_row, (uint32_t)(grp * 4), (uint32_t)K)) = sfw;
+  }
+}
+
+// One warp per padded row of the expert-grouped row space; padding rows are zeroed.
+__global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int dh,
+                                    int E_per_head, const int32_t* __restrict__ gather_ids,
+                                    const int* __restrict__ cu_tiles, int HE, const int* __restrict__ tile_expert,
+                                    const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
+                                    uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf,
+                                    float* __restrict__ a_gscale, int* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t prow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int mt = (int)(prow >> 7);
+  if (mt >= cu_tiles[HE]) return;
+  const int m = (int)(prow & 127);
+  const __nv_bfloat16* src = nullptr;
+  if (m < tile_rows[mt]) {
+    const int e = tile_expert[mt];
+    const int s = gather_ids[tile_row0[mt] + m];
+    if (s >= 0 && s < S) {
+      src = x + (int64_t)s * sx_s + (int64_t)(e / E_per_head) * sx_h;
+    } else if (lane == 0) {
+      record_error(status, MHMOE_ERR_ARGS);
+    }
+  }
+  warp_quant_row(src, dh, (uint64_t)prow, a_data, a_sf, a_gscale, lane);
+}
+
+__global__ void quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t pitch, int64_t M, int K,
+                                     uint8_t* __restrict__ data, uint8_t* __restrict__ sf,
+                                     float* __restrict__ gscale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= M) return;
+  warp_quant_row(x + row * pitch, K, (uint64_t)row, data, sf, gscale, lane);
+}
+
+// ───────────────────────────── weight packer ─────────────────────────────
+
+// amax[mat] over each [rows x cols] matrix; grid (chunks, n_mats).  Non-negative
+// floats order like their bit patterns, so an integer atomicMax is exact.
+__global__ void amax_kernel(const __nv_bfloat16* __restrict__ w, int64_t mat_elems, float* __restrict__ amax) {
+  const __nv_bfloat16* base = w + (int64_t)blockIdx.y * mat_elems;
+  float a = 0.f;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; i < mat_elems;
+       i += (int64_t)gridDim.x * blockDim.x * 8) {
+    float f[8];
+    load8_bf16(base + i, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a = fmaxf(a, fabsf(f[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(amax) + blockIdx.y, __float_as_int(a));
+}
+
+__global__ void gscale_kernel(const float* __restrict__ amax, int n, float* __restrict__ g) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) g[i] = amax[i] > 0.f ? __fdiv_rn(amax[i], 2688.0f) : 1.0f;
+}
+
+// Transposing quantiser: source matrix w[e] is [Kdim, Ndim] (N contiguous, the
+// reference layout); the packed operand is K-major [Nrows, Kdim/2].  One CTA handles a
+// 64(k) x 64(n) tile; thread (n, kq) quantises the 16-element k-block kq of column n.
+// For kind 0 the source column n of matrix `which` (0 gate, 1 up) lands on fused row
+// 32*(n/16) + 16*which + n%16 of a 2*Ndim-row operand.
+__global__ void pack_tile_kernel(const __nv_bfloat16* __restrict__ w, int Kdim, int Ndim, int which, int fused,
+                                 const float* __restrict__ gscale, uint8_t* __restrict__ data,
+                                 uint8_t* __restrict__ sf) {
+  __shared__ float tile[64][65];
+  const int e = blockIdx.z;
+  const int k0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const __nv_bfloat16* src = w + (int64_t)e * Kdim * Ndim;
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) {
+    const int kk = i / 64, nn = i % 64;
+    tile[kk][nn] = __bfloat162float(src[(int64_t)(k0 + kk) * Ndim + n0 + nn]);
+  }
+  __syncthreads();
+  const int nn = threadIdx.x & 63, kq = threadIdx.x >> 6;   // 256 threads: 64 columns x 4 k-blocks
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = tile[kq * 16 + i][nn];
+  const int Nrows = fused ? 2 * Ndim : Ndim;
+  const float g = gscale[(fused ? which * gridDim.z : 0) + e];
+  uint32_t w2[2];
+  const uint32_t s = quant_block16(v, g, w2);
+  const int n = n0 + nn;
+  const int64_t row = fused ? (int64_t)32 * (n / 16) + 16 * which + (n % 16) : n;
+  const int k = k0 + kq * 16;
+  uint8_t* drow = data + ((int64_t)e * Nrows + row) * (Kdim / 2);
+  *reinterpret_cast<uint2*>(drow + k / 2) = make_uint2(w2[0], w2[1]);
+  uint8_t* sfe = sf + (int64_t)e * Nrows * (Kdim / 16);
+  sfe[sf_atom_offset((uint64_t)row, (uint32_t)(k / 16), (uint32_t)Kdim)] = (uint8_t)s;
+}
+
+// ───────────────────────────── launchers ─────────────────────────────
+
+cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int dh, int E_per_head,
+                                const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
+                                const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
+                                uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
+  const int64_t rows = max_mtiles * 128;
+  quant_gather_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(x, sx_s, sx_h, S, dh, E_per_head, gather_ids, cu_tiles,
+                                                            HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
+                                                            a_gscale, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
+                                 float* gscale, cudaStream_t st) {
+  quantize_rows_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(x, pitch, M, K, data, sf, gscale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_weights(int kind, const __nv_bfloat16* w0, const __nv_bfloat16* w1, int n_experts, int dh,
+                                int de, uint8_t* data, uint8_t* sf, float* gscale, float* amax, cudaStream_t st) {
+  // kind 0: w0 = W_gate, w1 = W_up, each [E, dh, de]; operand [E, 2de, dh/2]
+  // kind 1: w0 = W_down [E, de, dh];                     operand [E, dh, de/2]
+  const int nmat = kind == 0 ? 2 : 1;
+  const int64_t elems = (int64_t)dh * de;
+  cudaMemsetAsync(amax, 0, sizeof(float) * nmat * n_experts, st);
+  const dim3 ag(64, n_experts);
+  amax_kernel<<<ag, 256, 0, st>>>(w0, elems, amax);
+  if (kind == 0) amax_kernel<<<ag, 256, 0, st>>>(w1, elems, amax + n_experts);
+  gscale_kernel<<<(nmat * n_experts + 255) / 256, 256, 0, st>>>(amax, nmat * n_experts, gscale);
+  if (kind == 0) {
+    const dim3 grid(de / 64, dh / 64, n_experts);
+    pack_tile_kernel<<<grid, 256, 0, st>>>(w0, dh, de, 0, 1, gscale, data, sf);
+    pack_tile_kernel<<<grid, 256, 0, st>>>(w1, dh, de, 1, 1, gscale, data, sf);
+  } else {
+    const dim3 grid(dh / 64, de / 64, n_experts);
+    pack_tile_kernel<<<grid, 256, 0, st>>>(w0, de, dh, 0, 0, gscale, data, sf);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mhmoe

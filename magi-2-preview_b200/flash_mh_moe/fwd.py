@@ -1,0 +1,118 @@
+"""Expert FFN forward — same call signature as the reference's ``inference/flash_mh_moe/fwd.py``.
+
+``flash_mh_moe_fwd(x, gather_ids, probs, expert_offsets, W_gate, W_up, W_down)``
+(reference ``fwd.py:16-40`` -> ``triton/mh_moe_fwd.py:271-373``): gather ->
+gate/up GEMM -> SwiGLU7 -> down GEMM -> weighted scatter, here as the NVFP4 B200 path:
+
+    per-row NVFP4 quantise of the gathered x  ->  tcgen05 block-scaled grouped GEMM
+    (gate|up) with SwiGLU7 and NVFP4 re-quantise fused in its epilogue  ->  grouped
+    GEMM (down) x prob  ->  deterministic combine (fp32 sum in sorted-row order).
+
+Weights may be the reference's bf16 parameters (packed to NVFP4 on first use and
+cached per parameter version) or already-packed ``NVFP4GateUp`` / ``NVFP4Down``.
+The combine is deterministic by construction, so ``MAGI2_DETERMINISTIC`` (read by the
+reference to pick its scatter) changes nothing here; it is still honoured as a name.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+from .nvfp4 import NVFP4Down, NVFP4GateUp, pack_down, pack_gate_up
+
+
+def _is_deterministic() -> bool:
+    return os.environ.get("MAGI2_DETERMINISTIC", "0") == "1"
+
+
+_pack_cache: dict[tuple, tuple] = {}
+
+
+def _key(t: torch.Tensor) -> tuple:
+    return (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device)
+
+
+def packed_weights(W_gate, W_up, W_down) -> tuple[NVFP4GateUp, NVFP4Down]:
+    """Return NVFP4 operands for the given weights, packing (and caching) bf16 ones."""
+    if isinstance(W_gate, NVFP4GateUp):
+        gu = W_gate
+    else:
+        k = ("gu",) + _key(W_gate) + _key(W_up)
+        hit = _pack_cache.get(k)
+        if hit is None:
+            hit = (pack_gate_up(W_gate, W_up),)
+            _pack_cache[k] = hit
+        gu = hit[0]
+    if isinstance(W_down, NVFP4Down):
+        dn = W_down
+    else:
+        k = ("dn",) + _key(W_down)
+        hit = _pack_cache.get(k)
+        if hit is None:
+            hit = (pack_down(W_down),)
+            _pack_cache[k] = hit
+        dn = hit[0]
+    return gu, dn
+
+
+def clear_pack_cache() -> None:
+    _pack_cache.clear()
+
+
+def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tensor, expert_offsets: torch.Tensor,
+              gu: NVFP4GateUp, dn: NVFP4Down, tok_rows: torch.Tensor | None = None,
+              tok_offsets: torch.Tensor | None = None, k_fixed: int = 0,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """NVFP4 expert FFN on x_heads [S, H, dh] bf16 -> y [S, H, dh] bf16."""
+    _lib.require_cuda(x_heads, expert_offsets)
+    S, H, dh = x_heads.shape
+    n = expert_offsets.numel() - 1
+    if gu.num_experts != n or dn.num_experts != n:
+        raise ValueError(f"weights hold {gu.num_experts}/{dn.num_experts} experts, expert_offsets {n}")
+    if gu.d_head != dh or dn.d_head != dh or gu.d_expert != dn.d_expert:
+        raise ValueError("weight shapes do not match x")
+    de = gu.d_expert
+    assert dh % 256 == 0, f"d_head={dh} must be divisible by 256"
+    assert de % 256 == 0, f"d_expert={de} must be divisible by 256"
+    x = x_heads if x_heads.dtype == torch.bfloat16 else x_heads.to(torch.bfloat16)
+    if x.stride(2) != 1 or x.stride(0) % 8 or x.stride(1) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    dev = x.device
+    R = int(gather_ids.numel())
+    y = out if out is not None else torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
+    gids = gather_ids.to(torch.int32).contiguous()
+    ps = probs.float().contiguous()
+    offs = expert_offsets.to(torch.int64).contiguous()
+    L = _lib.lib()
+    ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, S, H, dh, de, n)), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.mhmoe_ffn_nvfp4(
+            x.data_ptr(), x.stride(0), x.stride(1), S, H, dh, de, n, R, gids.data_ptr(), ps.data_ptr(),
+            offs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(),
+            dn.sf.data_ptr(), dn.gscale.data_ptr(), _lib.ptr(tok_rows), _lib.ptr(tok_offsets), int(k_fixed),
+            ws.data_ptr(), y.data_ptr(), y.stride(0), y.stride(1), _lib.device_status(dev).data_ptr(), 0,
+            _lib.stream_ptr(dev)), "flash_mh_moe_fwd")
+    return y
+
+
+def flash_mh_moe_fwd(
+    x: torch.Tensor,
+    gather_ids: torch.Tensor,
+    probs: torch.Tensor,
+    expert_offsets: torch.Tensor,
+    W_gate,
+    W_up,
+    W_down,
+) -> torch.Tensor:
+    """Flash-MH-MoE forward: gather -> gate/up GEMM -> SwiGLU7 -> down GEMM -> scatter.
+
+    x [S, H, d_head]; gather_ids int32 [T]; probs fp32 [T]; expert_offsets [H*E+1];
+    W_gate/W_up [H*E, d_head, d_expert], W_down [H*E, d_expert, d_head] (bf16, packed
+    on first use) or their packed ``NVFP4GateUp`` (as W_gate; W_up ignored) and
+    ``NVFP4Down`` forms.  Returns y like x (bf16).
+    """
+    gu, dn = packed_weights(W_gate, W_up, W_down)
+    y = ffn_nvfp4(x, gather_ids, probs, expert_offsets, gu, dn)
+    return y if x.dtype == torch.bfloat16 else y.to(x.dtype)

@@ -1,0 +1,122 @@
+"""Generate golden fixtures by running the reference implementation itself.
+
+Run once, in a container that has the reference checkout (default
+``/root/reference``; override with ``MAGI2_REFERENCE``).  The fixtures are
+committed; nothing at test time reads the reference.
+
+    python tests/golden/make_golden.py
+
+Produces:
+* ``route_cases.npz`` — inputs/outputs of ``compute_topk_probs_and_indices``
+  (``inference/flash_mh_moe/route.py:157``) and ``flash_mh_moe_global_sort``
+  (``route.py:209``) on seeded logits: softmax/sigmoid, expert_bias, virtual
+  groups, route_norm off, a Zipf-skewed bias, the production head shape.
+* ``ffn_fp32.npz`` — the reference Triton kernel ``_mh_moe_fwd_kernel``
+  (``inference/flash_mh_moe/triton/mh_moe_fwd.py:90``) run under
+  ``TRITON_INTERPRET=1`` on fp32 tensors (the interpreter does not support bf16),
+  atomic and deterministic variants.
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("MAGI2_REFERENCE", "/root/reference"))
+
+
+def _import_reference():
+    sys.path.insert(0, str(REF))
+    import torch  # noqa: F401
+    from inference.flash_mh_moe import route  # type: ignore
+    return route
+
+
+ROUTE_CASES = [
+    # name, H, S, E, K, score_func, bias, nvg, tvg, route_norm, seed
+    ("cfg0_softmax", 1, 512, 8, 2, "softmax", False, 1, 0, True, 0),
+    ("sigmoid_bias", 2, 64, 16, 4, "sigmoid", True, 1, 0, True, 11),
+    ("softmax_vgroup", 2, 64, 16, 4, "softmax", False, 4, 2, True, 12),
+    ("softmax_nonorm", 1, 128, 32, 8, "softmax", False, 1, 0, False, 13),
+    ("zipf_logit_bias", 1, 256, 128, 8, "softmax", False, 1, 0, True, 2),
+    ("prod_heads_sigmoid", 12, 16, 256, 6, "sigmoid", True, 1, 0, True, 14),
+    ("sigmoid_vgroup_bias", 1, 96, 64, 6, "sigmoid", True, 8, 3, True, 15),
+]
+
+
+def make_route(route):
+    import torch
+    out = {}
+    for name, H, S, E, K, sf, use_bias, nvg, tvg, rn, seed in ROUTE_CASES:
+        g = torch.Generator().manual_seed(seed)
+        if name == "cfg0_softmax":
+            # config 0 router: x bf16 N(0,1) [S,1,1024]; gate bf16 N(0,0.02) stored fp32 (magi2_preview.py:2588-2591)
+            x = torch.randn(S, 1, 1024, generator=g).to(torch.bfloat16)
+            gate = (torch.randn(E, 1024, generator=g) * 0.02).to(torch.bfloat16).float()
+            logits = torch.einsum("shd,hed->hse", x.float(), gate.view(1, E, 1024))
+        else:
+            logits = torch.randn(H, S, E, generator=g) * 1.5
+        if name == "zipf_logit_bias":
+            e = torch.arange(E, dtype=torch.float32)
+            logits = logits + 2.0 * torch.log((e + 1.0) ** -1.2)
+        bias = (torch.randn(H, E, generator=g) * 0.05) if use_bias else None
+        probs, idx = route.compute_topk_probs_and_indices(
+            logits, K, score_func=sf, expert_bias=bias, num_virtual_group=nvg,
+            topk_virtual_group=tvg, route_norm=rn)
+        gids, psorted, offs = route.flash_mh_moe_global_sort(probs, idx, E)
+        p = f"{name}/"
+        out[p + "meta"] = np.array([H, S, E, K, nvg, tvg, int(rn), int(use_bias)], np.int64)
+        out[p + "score_func"] = np.array(sf)
+        out[p + "logits"] = logits.numpy().astype(np.float32)
+        if bias is not None:
+            out[p + "bias"] = bias.numpy().astype(np.float32)
+        out[p + "probs"] = probs.numpy()
+        out[p + "idx"] = idx.numpy()
+        out[p + "gather_ids"] = gids.numpy()
+        out[p + "probs_sorted"] = psorted.numpy()
+        out[p + "expert_offsets"] = offs.numpy()
+    np.savez_compressed(HERE / "route_cases.npz", **out)
+    print("route_cases.npz:", len(ROUTE_CASES), "cases")
+
+
+def make_ffn(route):
+    os.environ["TRITON_INTERPRET"] = "1"
+    import torch
+    torch.cuda.get_device_capability = lambda *a, **k: (10, 0)    # mh_moe_fwd.py:265 on a CPU box
+    from inference.flash_mh_moe.triton import mh_moe_fwd as mk  # type: ignore
+    out = {}
+    cases = [("small", 32, 2, 64, 4, 2, 64, 21), ("ragged", 40, 1, 128, 8, 3, 96, 22)]
+    for name, S, H, dh, E, K, de, seed in cases:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(S, H, dh, generator=g)
+        logits = torch.randn(H, S, E, generator=g)
+        if name == "ragged":
+            logits[:, :, 0] += 4.0          # one crowded expert, some empty ones
+            logits[:, :, E - 1] -= 8.0
+        probs, idx = route.compute_topk_probs_and_indices(logits, K, score_func="softmax")
+        gids, ps, offs = route.flash_mh_moe_global_sort(probs, idx, E)
+        Wg = torch.randn(H * E, dh, de, generator=g) * 0.05
+        Wu = torch.randn(H * E, dh, de, generator=g) * 0.05
+        Wd = torch.randn(H * E, de, dh, generator=g) * 0.05
+        p = f"{name}/"
+        for det in (False, True):
+            y = mk.mh_moe_fwd_func(x, gids, ps, offs, Wg, Wu, Wd, deterministic=det)
+            out[p + ("y_det" if det else "y_atomic")] = y.numpy()
+        out[p + "x"] = x.numpy()
+        out[p + "gather_ids"] = gids.numpy()
+        out[p + "probs_sorted"] = ps.numpy()
+        out[p + "expert_offsets"] = offs.numpy()
+        out[p + "W_gate"] = Wg.numpy()
+        out[p + "W_up"] = Wu.numpy()
+        out[p + "W_down"] = Wd.numpy()
+    np.savez_compressed(HERE / "ffn_fp32.npz", **out)
+    print("ffn_fp32.npz:", len(cases), "cases")
+
+
+if __name__ == "__main__":
+    r = _import_reference()
+    make_route(r)
+    make_ffn(r)
