@@ -305,5 +305,5 @@ def quantize_rows(x: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     """
     x = f32(x)
     g = global_scale(np.abs(x).max(axis=1))
-    codes, sf = quantize_blocks(x, g[:, None])
+    codes, sf = quantize_blocks(x, g)
     return codes, sf, g
