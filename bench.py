@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""bench.py — MAGI-2 routed MoE layer (NVFP4) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward of the MoE layer (router logits -> top-k -> global sort ->
+NVFP4 expert FFN -> combine) over the BASELINE config-1 batch: S=16384 tokens,
+d=3072 (H=1), E=128 experts, top-8 softmax routing, SwiGLU7 expert FFN dim 1024.
+Synthetic seeded data with the config's distributions (x ~ N(0,1) bf16, router
+weight ~ N(0,0.02) bf16-valued fp32, expert weights ~ N(0,0.02) cast to bf16, then
+packed to NVFP4 at load).  Inputs are larger than L2 (0.68 GB of NVFP4 weights and
+0.1 GB of x are streamed every step), so no explicit flush is needed.
+
+Rank 0 prints one JSON line.  Under torchrun (N>1) every rank runs an independent
+replica of the config-1 layer on its own tokens (weak scaling); the expert-parallel
+layer is exercised by the multi-GPU tests.
+
+`--impl reference` times the reference's CPU path for the same layer (router fp32
+einsum, route.py top-k and global sort, and the bf16 FFN of mh_moe_fwd.py restated in
+numpy — the oracle port, because the reference is Python/Triton and cannot travel to
+the GPU box) on a bounded token sample, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "magi-2-preview_b200"
+for p in (str(ROOT), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+CFG1 = dict(name="config1", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=1, score_func="softmax")
+METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
+KERNELS_PER_STEP = 11   # logits, topk, sort x4, tile tables, quant, gate/up GEMM, down GEMM, combine
+CPU_SAMPLE_TOKENS = 512
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clk", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for ln in self.path.read_text().splitlines():
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def make_layer(cfg, device, rank):
+    import torch
+    from flash_mh_moe.moe import CoreMultiHeadMoE, CoreMultiHeadMoEConfig, init_moe_params_
+    mc = CoreMultiHeadMoEConfig(hidden_size=cfg["d"], num_heads=cfg["H"], num_experts=cfg["E"], top_k=cfg["K"],
+                                expert_intermediate_size=cfg["de"], num_layers=1, params_dtype=torch.bfloat16,
+                                score_func=cfg["score_func"], route_norm=True, route_scale=1.0)
+    m = CoreMultiHeadMoE(mc).to(device)
+    init_moe_params_(m, seed=cfg["seed"], device=device)
+    g = torch.Generator().manual_seed(cfg["seed"] * 1000 + rank)
+    x_host = torch.randn(cfg["S"], cfg["d"], generator=g).to(torch.bfloat16)
+    return m, x_host
+
+
+def step_explicit(m, x, ev):
+    """The module forward spelled out, with events between the stages (same kernels)."""
+    from flash_mh_moe.fwd import ffn_nvfp4
+    from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse
+    x_heads = x.view(-1, m.num_heads, m.d_head)
+    ev[0].record()
+    probs, idx = m._route(x_heads)
+    ev[1].record()
+    gids, ps, offs, inv = flash_mh_moe_global_sort_with_inverse(probs, idx, m.num_experts)
+    gu, dn = m.packed_weights()
+    return ffn_nvfp4(x_heads, gids, ps, offs, gu, dn, tok_rows=inv, k_fixed=m.topk, stage_events=ev[2:7])
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+    from flash_mh_moe import _lib
+    cfg = CFG1
+    dev = torch.device("cuda", local if world > 1 else 0)
+    m, x_host = make_layer(cfg, dev, rank)
+    x = x_host.to(dev)
+    m.packed_weights()
+    torch.cuda.synchronize()
+
+    nev = 7
+    for _ in range(args.warmup):
+        step_explicit(m, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
+    if world > 1:
+        dist.barrier()
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nev)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device() if world == 1 else local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0.record()
+        for k in range(args.steps):
+            step_explicit(m, x, evs[k])
+        t1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    _lib.check_device_status(dev)
+    ms_total = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+
+    def avg(i, j):
+        return sum(e[i].elapsed_time(e[j]) for e in evs) / len(evs)
+
+    stages = {"route_ms": avg(0, 1), "sort_ms": avg(1, 2), "quant_tables_ms": avg(2, 3),
+              "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "combine_ms": avg(5, 6)}
+
+    # end-to-end through the public module API, host buffers, copies inside the timed region
+    e2e_ms = float("nan")
+    if not args.no_e2e:
+        e2e_ms = _e2e(args, m, x_host, dev, world)
+    return _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host)
+
+
+def _e2e(args, m, x_host, dev, world):
+    import torch
+    import torch.distributed as dist
+    xh = x_host.pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(m(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(m(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    return e2e_ms
+
+
+def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
+    S, d, de, K = cfg["S"], cfg["d"], cfg["de"], cfg["K"]
+    R = S * K * cfg["H"]
+    flop_gate_up = 2.0 * R * (d // cfg["H"]) * (2 * de)
+    flop_total = 6.0 * R * (d // cfg["H"]) * de
+    peaks = load_peaks()
+    fp4_peak = 4.0 * peaks["bf16_tflops_sustained"]
+    achieved = flop_gate_up / (stages["gemm_gate_up_ms"] * 1e-3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "gemm_gate_up_config1_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    layer_tflops = flop_total / (ms_step * 1e-3) / 1e12
+    value = world * S / (ms_step * 1e-3)
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
+        "data": "synthetic (seeded, config-1 distributions)",
+        "config": {"workload": "config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024",
+                   "tokens_per_gpu": S, "global_batch": world * S, "parallelism":
+                       f"{world} independent replicas" if world > 1 else "1 GPU",
+                   "l2": "inputs larger than L2 (0.68 GB NVFP4 weights + 0.1 GB x per step)"},
+        "tokens_per_s_per_gpu": round(value / world, 1),
+        "layer_tflops": round(layer_tflops, 1),
+        "nvfp4_util_pct": {"vs_4x_measured_bf16_sustained": round(100 * layer_tflops / fp4_peak, 2),
+                           "vs_datasheet_9pf": round(100 * layer_tflops / 9000.0, 2)},
+        "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+        "roofline": {"kernel": "ffn_gemm_nvfp4_kernel<EPI_SWIGLU> (gate/up GEMM)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": round(fp4_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp4_peak, 4), "traffic": traffic,
+                     "peak_note": f"4 x {peaks['source']} bf16 sustained (FP4 dense = 4x bf16); "
+                                  f"datasheet dense FP4 9000 TFLOP/s -> frac {achieved / 9000.0:.4f}",
+                     "algorithmic_flop_per_launch": flop_gate_up},
+        "e2e": None if e2e_ms != e2e_ms else {"value": round(world * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": S * d * 2, "d2h_bytes_per_step": S * d * 2,
+                "ms_per_step": round(e2e_ms, 4), "api": "CoreMultiHeadMoE.forward (custom op magi2_b200::mh_moe)"},
+        "gpu_launches": KERNELS_PER_STEP * args.steps,   # kernels of libmhmoe inside the device-timed region
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
+    return out
+
+
+# ───────────────────────────── CPU reference path (oracle port) ─────────────────────────────
+
+def _host_weights(m):
+    import numpy as np
+    import torch
+    with torch.no_grad():
+        Wg = m.W_gate.detach().float().cpu().numpy()
+        Wu = m.W_up.detach().float().cpu().numpy()
+        Wd = m.W_down.detach().float().cpu().numpy()
+        gate = m.gate.detach().float().cpu().numpy()
+    return gate, Wg, Wu, Wd
+
+
+def cpu_layer_sample(gate, Wg, Wu, Wd, x_np, cfg):
+    """Reference CPU path on x_np [n, d]: fp32 einsum router, route.py top-k + sort, bf16 FFN."""
+    from oracle import ffn_ref, route_ref
+    n = x_np.shape[0]
+    H, E = cfg["H"], cfg["E"]
+    xh = x_np.reshape(n, H, -1)
+    logits = route_ref.router_logits(xh, gate, E)
+    p, i = route_ref.compute_topk_probs_and_indices(logits, cfg["K"], cfg["score_func"])
+    g, ps, o = route_ref.flash_mh_moe_global_sort(p, i, E)
+    return ffn_ref.mh_moe_fwd_ref(xh, g, ps, o, Wg, Wu, Wd, dtype="bf16", round_weights=False)
+
+
+def _cores():
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((d.get("num_threads", 0) for d in threadpool_info()), default=0)
+        return int(n) or os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def cpu_baseline(m, x_host, reps=2, host=None):
+    host = host or _host_weights(m)
+    x_np = x_host[:CPU_SAMPLE_TOKENS].float().numpy()
+    times = []
+    for _ in range(reps + 1):
+        t = time.perf_counter()
+        cpu_layer_sample(*host, x_np, CFG1)
+        times.append(time.perf_counter() - t)
+    best = min(times[1:]) if len(times) > 1 else times[0]
+    return {"value": round(CPU_SAMPLE_TOKENS / best, 1), "unit": "tokens/s", "cores": _cores(), "kind": "port",
+            "sample": f"first {CPU_SAMPLE_TOKENS} tokens of the config-1 batch through the full layer "
+                      f"(all 128 experts' bf16 weights), best of {reps} after 1 warm-up; numpy/BLAS threads"}
+
+
+def run_reference(args, world, rank):
+    import torch
+    if rank != 0:
+        return None
+    cfg = CFG1
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    m, x_host = make_layer(cfg, dev, 0) if dev.type == "cuda" else (None, None)
+    host = _host_weights(m)
+    x_np = x_host[:CPU_SAMPLE_TOKENS].float().numpy()
+    for _ in range(args.warmup):
+        cpu_layer_sample(*host, x_np, cfg)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_layer_sample(*host, x_np, cfg)
+    dt = (time.perf_counter() - t) / args.steps
+    v = CPU_SAMPLE_TOKENS / dt
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
+            "data": "synthetic (seeded, config-1 distributions)",
+            "config": {"workload": "config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024",
+                       "sample_tokens_per_step": CPU_SAMPLE_TOKENS, "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": _cores(), "kind": "port",
+                             "sample": f"{CPU_SAMPLE_TOKENS} tokens of the config-1 batch per step"},
+            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per GPU (default: config 1's 16384; smaller only for profiler captures)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.tokens:
+        CFG1["S"] = args.tokens
+    world, rank, local = dist_setup()
+    try:
+        out = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)
+        if rank == 0 and out is not None:
+            print(json.dumps(out), flush=True)
+    finally:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -118,14 +118,16 @@ MHMOE_API int mhmoe_pack_weights_nvfp4(int kind, const void* w0, const void* w1,
  * de % 256 == 0.  `tok_rows`/`tok_offsets` (optional) give each (s,h) its rows
  * (row_of_flat with fixed K when tok_offsets == NULL and k_fixed > 0); when both
  * are NULL the mapping is derived from gather_ids.  workspace: see
- * mhmoe_ffn_workspace_bytes. */
+ * mhmoe_ffn_workspace_bytes.  stage_events (optional): 5 cudaEvent_t recorded on
+ * `stream` before the tile tables, before the gate/up GEMM, before the down GEMM,
+ * before the combine and at the end (per-stage timing without a profiler). */
 MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
                     int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
                     const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
                     const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
                     const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
-                    void* stream);
+                    void* const* stage_events, void* stream);
 
 /* ───────────────────────── building blocks (tests, EP) ───────────────────────── */
 

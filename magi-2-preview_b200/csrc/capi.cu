@@ -157,7 +157,7 @@ int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S
                     const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
                     const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
-                    void* stream) {
+                    void* const* stage_events, void* stream) {
   MHMOE_REQUIRE(x && y && expert_offsets && gu_data && gu_sf && gu_gscale && dn_data && dn_sf && dn_gscale);
   MHMOE_REQUIRE(S >= 0 && H > 0 && n_experts > 0 && n_experts % H == 0 && R >= 0);
   MHMOE_REQUIRE(dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
@@ -187,7 +187,8 @@ int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S
   const int rc = ffn_nvfp4(static_cast<const __nv_bfloat16*>(x), x_stride_s, x_stride_h, S, H, dh, de, n_experts, R,
                            gather_ids, probs_sorted, expert_offsets, gu_data, gu_sf, gu_gscale, dn_data, dn_sf,
                            dn_gscale, tok_rows, tok_offsets, k_fixed, workspace, static_cast<__nv_bfloat16*>(y),
-                           y_stride_s, y_stride_h, dev_status, timeout_ns, st, &ce);
+                           y_stride_s, y_stride_h, dev_status, timeout_ns,
+                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce);
   if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4");
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
   return rc;

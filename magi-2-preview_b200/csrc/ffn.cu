@@ -122,7 +122,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
-              uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr) {
+              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr) {
   const int64_t T = (int64_t)S * H;
   FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
   const int64_t max_mt = mtiles_upper_bound(R, HE);
@@ -137,6 +137,10 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     }                          \
   } while (0)
 
+  auto mark = [&](int i) {
+    if (events && events[i]) cudaEventRecord(events[i], st);
+  };
+  mark(0);
   MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
                                status, st));
   MHMOE_TRY(launch_quant_gather(x, sx_s, sx_h, S, dh, HE / H, gather_ids, w.cu_tiles, HE, max_mt, w.tile_expert,
@@ -149,6 +153,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
       encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess)
     return MHMOE_ERR_DRIVER;
 
+  mark(1);
   FfnGemmParams p1{};
   p1.sfa = w.a_sf;
   p1.sfb = gu_sf;
@@ -168,6 +173,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p1.timeout_ns = timeout_ns;
   MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, p1, max_mt * (2 * de / GEMM_BN), st));
 
+  mark(2);
   FfnGemmParams p2 = p1;
   p2.sfa = w.h_sf;
   p2.sfb = dn_sf;
@@ -178,6 +184,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p2.out_bf16 = w.P;
   MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, p2, max_mt * (dh / GEMM_BN), st));
 
+  mark(3);
   const int32_t* rows_map = tok_rows;
   const int32_t* offs_map = tok_offsets;
   int kf = k_fixed;
@@ -189,6 +196,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     kf = 0;
   }
   MHMOE_TRY(launch_combine(w.P, dh, S, H, rows_map, offs_map, kf, R, y, sy_s, sy_h, st));
+  mark(4);
 #undef MHMOE_TRY
   return MHMOE_OK;
 }

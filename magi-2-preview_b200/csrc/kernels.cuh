@@ -54,7 +54,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
-              uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);
+              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr);
 int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
                    const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out, int* status,
                    uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);

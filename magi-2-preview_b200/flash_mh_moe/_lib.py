@@ -34,7 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_ffn_workspace_bytes": (sz, [i64, i32, i32, i32, i32, i32]),
     "mhmoe_pack_weights_nvfp4": (i32, [i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]),
     "mhmoe_ffn_nvfp4": (i32, [vp, i64, i64, i32, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                              vp, vp, i32, vp, vp, i64, i64, vp, u64, vp]),
+                              vp, vp, i32, vp, vp, i64, i64, vp, u64, vp, vp]),
     "mhmoe_quantize_rows_nvfp4": (i32, [vp, i64, i64, i32, vp, vp, vp, vp]),
     "mhmoe_gemm_nvfp4_raw": (i32, [vp, vp, i32, vp, vp, vp, i32, i32, i32, vp, vp, u64, vp]),
 }

@@ -64,8 +64,12 @@ def clear_pack_cache() -> None:
 def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tensor, expert_offsets: torch.Tensor,
               gu: NVFP4GateUp, dn: NVFP4Down, tok_rows: torch.Tensor | None = None,
               tok_offsets: torch.Tensor | None = None, k_fixed: int = 0,
-              out: torch.Tensor | None = None) -> torch.Tensor:
-    """NVFP4 expert FFN on x_heads [S, H, dh] bf16 -> y [S, H, dh] bf16."""
+              out: torch.Tensor | None = None, stage_events=None) -> torch.Tensor:
+    """NVFP4 expert FFN on x_heads [S, H, dh] bf16 -> y [S, H, dh] bf16.
+
+    ``stage_events``: optional 5 ``torch.cuda.Event`` recorded on the current stream
+    before the tile tables, gate/up GEMM, down GEMM, combine, and at the end.
+    """
     _lib.require_cuda(x_heads, expert_offsets)
     S, H, dh = x_heads.shape
     n = expert_offsets.numel() - 1
@@ -93,8 +97,18 @@ def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tens
             offs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(),
             dn.sf.data_ptr(), dn.gscale.data_ptr(), _lib.ptr(tok_rows), _lib.ptr(tok_offsets), int(k_fixed),
             ws.data_ptr(), y.data_ptr(), y.stride(0), y.stride(1), _lib.device_status(dev).data_ptr(), 0,
-            _lib.stream_ptr(dev)), "flash_mh_moe_fwd")
+            _events(stage_events), _lib.stream_ptr(dev)), "flash_mh_moe_fwd")
     return y
+
+
+def _events(evs):
+    if not evs:
+        return None
+    import ctypes
+    arr = (ctypes.c_void_p * 5)()
+    for i, e in enumerate(evs):
+        arr[i] = e.cuda_event
+    return ctypes.cast(arr, ctypes.c_void_p)
 
 
 def flash_mh_moe_fwd(

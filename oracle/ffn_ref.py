@@ -59,13 +59,15 @@ def _sequential_add(y_flat: np.ndarray, idx: np.ndarray, vals: np.ndarray, rnd) 
 
 
 def mh_moe_fwd_ref(x, gather_ids, probs, expert_offsets, W_gate, W_up, W_down,
-                   dtype: str = "bf16", deterministic: bool = True) -> np.ndarray:
+                   dtype: str = "bf16", deterministic: bool = True, round_weights: bool = True) -> np.ndarray:
     """Reference FFN restatement.  x [S,H,dh]; W_gate/W_up [H*E,dh,de]; W_down [H*E,de,dh].
 
     ``dtype`` is the operand / output dtype: "bf16" rounds operands, hidden and
     output to bf16; "fp32" keeps everything fp32 (the Triton-interpreter check).
     The bf16 atomic path adds in an unspecified order, so only the sequential
     (deterministic) order is restated; both round after every add.
+    ``round_weights=False`` skips re-rounding weights the caller already holds as
+    bf16 values (same result, less work for large layers).
     """
     rnd = nv.bf16_round if dtype == "bf16" else (lambda a: np.asarray(a, np.float32))
     x = rnd(np.asarray(x, np.float32))
@@ -73,7 +75,10 @@ def mh_moe_fwd_ref(x, gather_ids, probs, expert_offsets, W_gate, W_up, W_down,
     R = int(np.asarray(gather_ids).size)
     if R == 0:                                                     # mh_moe_fwd.py:257-258
         return np.zeros_like(x)
-    Wg, Wu, Wd = (rnd(np.asarray(w, np.float32)) for w in (W_gate, W_up, W_down))
+    if round_weights:
+        Wg, Wu, Wd = (rnd(np.asarray(w, np.float32)) for w in (W_gate, W_up, W_down))
+    else:
+        Wg, Wu, Wd = W_gate, W_up, W_down
     expert, head = _row_meta(gather_ids, expert_offsets, H)
     tok = np.asarray(gather_ids, np.int64)
     p = np.asarray(probs, np.float32)

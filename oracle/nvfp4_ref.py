@@ -115,11 +115,10 @@ def e4m3_decode(b: np.ndarray) -> np.ndarray:
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
     """fp32 -> nearest bf16 (RNE), returned as fp32 values."""
-    x = f32(x)
-    u = x.view(np.uint32).astype(np.uint64)
-    r = ((u >> 16) & 1) + 0x7FFF
-    u = ((u + r) >> 16) << 16
-    out = u.astype(np.uint32).view(np.float32)
+    x = np.ascontiguousarray(f32(x))
+    u = x.view(np.uint32)
+    r = ((u >> np.uint32(16)) & np.uint32(1)) + np.uint32(0x7FFF)
+    out = ((u + r) & np.uint32(0xFFFF0000)).view(np.float32)   # wraps only for NaN payloads
     return np.where(np.isnan(x), x, out).astype(np.float32)
 
 
