@@ -107,6 +107,7 @@ def _events(evs):
     import ctypes
     arr = (ctypes.c_void_p * 5)()
     for i, e in enumerate(evs):
+        e.record()            # torch creates the CUDA event lazily; the library re-records it in place
         arr[i] = e.cuda_event
     return ctypes.cast(arr, ctypes.c_void_p)
 
