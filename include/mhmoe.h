@@ -92,6 +92,18 @@ MHMOE_API int mhmoe_global_sort(const float* topk_probs, const int64_t* topk_idx
                       void* workspace, int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
                       int32_t* row_of_flat, int* dev_status, void* stream);
 
+/* Same contract and outputs as mhmoe_global_sort, for callers that cannot allocate
+ * device memory: it takes no workspace and allocates nothing.  No counterpart in the
+ * reference (the reference sort allocates through PyTorch).  Its scratch is a fixed
+ * ~1.05 MB array inside the library, held by every GPU that loads it; limits:
+ * H*S*K <= 262144 routed rows and H*E <= 1024 experts, else MHMOE_ERR_CAPACITY with
+ * nothing launched.  The first call on a device (with it current) resolves the
+ * array's device address; make that call before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU race, so order them. */
+MHMOE_API int mhmoe_global_sort_noalloc(const float* topk_probs, const int64_t* topk_idx, int H, int S, int K, int E,
+                                        int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
+                                        int32_t* row_of_flat, int* dev_status, void* stream);
+
 /* ───────────────────────── expert FFN (NVFP4) ───────────────────────── */
 
 /* Upper bound of 128-row tiles for R routed rows over n_experts groups. */

@@ -59,6 +59,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
+namespace mhmoe {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace mhmoe
+
 using namespace mhmoe;
 
 extern "C" {

@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <string>
 
 #include "mhmoe_common.cuh"
 
@@ -45,6 +46,9 @@ cudaError_t launch_topk(const float* logits, const float* bias, int H, int S, in
 cudaError_t launch_combine(const __nv_bfloat16* P, int dh, int S, int H, const int32_t* tok_rows,
                            const int32_t* tok_offsets, int k_fixed, int64_t R, __nv_bfloat16* y, int64_t sy_s,
                            int64_t sy_h, cudaStream_t st);
+
+// capi.cu: text returned by mhmoe_last_error() on this host thread
+void set_last_error(const std::string& msg);
 
 // ffn.cu
 int num_sms();

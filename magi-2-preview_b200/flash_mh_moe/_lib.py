@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_topk": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, f32, vp, vp, vp]),
     "mhmoe_global_sort_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "mhmoe_global_sort": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]),
+    "mhmoe_global_sort_noalloc": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp]),
     "mhmoe_max_mtiles": (i64, [i64, i32]),
     "mhmoe_ffn_workspace_bytes": (sz, [i64, i32, i32, i32, i32, i32]),
     "mhmoe_pack_weights_nvfp4": (i32, [i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]),
