@@ -64,6 +64,26 @@ MHMOE_API const char* mhmoe_last_error(void);
 MHMOE_API int mhmoe_router_logits(const void* x, int64_t x_stride_s, int64_t x_stride_h, const float* gate, int S, int H,
                         int dh, int E, float* logits, void* stream);
 
+/* Router weight preparation (at load, not per step): split the fp32 gate [H*E, dh]
+ * into nsplit (1..3) bf16 planes hi, lo, lo2 (g = hi + lo + lo2 exactly for nsplit 3),
+ * stored interleaved per 64-column block: planes [H*E, nsplit*dh] bf16.
+ * flags (optional, int32[3], caller-zeroed): flags[1] / flags[2] set when the lo / lo2
+ * plane is non-zero, i.e. the smallest exact nsplit is 1 + flags[1]|flags[2] + flags[2]. */
+MHMOE_API int mhmoe_router_prepare(const float* gate, int n_experts, int dh, int nsplit, void* planes, int* flags,
+                                   void* stream);
+
+/* Fused router on the tensor cores.  Replaces CoreMultiHeadMoE._route
+ * (inference/model/magi2_preview.py:2588-2601): fp32-accurate logits (bf16 tcgen05 MMAs
+ * over the prepared planes) followed, in the same kernel, by softmax/sigmoid, +expert_bias
+ * for selection, top-k (sorted desc, ties to the lower id), L1 normalisation and
+ * route_scale (route.py:28-148 without virtual groups).  x bf16 [S, H, dh] with heads
+ * contiguous (x_stride_h == dh).  E <= 256, K <= 16, dh % 64 == 0.
+ * logits (optional) receives fp32 [H, S, E]. */
+MHMOE_API int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const void* planes, int nsplit,
+                          int S, int H, int dh, int E, int K, int score_func, const float* expert_bias,
+                          int route_norm, float norm_eps, float route_scale, float* probs, int64_t* idx,
+                          float* logits, int* dev_status, void* stream);
+
 /* Top-k gating from logits.  Replaces compute_topk_probs_and_indices
  * (inference/flash_mh_moe/route.py:157-199 -> :28-148).
  * score_func: 0 softmax, 1 sigmoid.  expert_bias fp32 [H*E] or NULL.

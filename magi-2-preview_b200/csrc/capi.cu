@@ -96,6 +96,34 @@ int mhmoe_router_logits(const void* x, int64_t x_stride_s, int64_t x_stride_h, c
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "router_logits");
 }
 
+int mhmoe_router_prepare(const float* gate, int n_experts, int dh, int nsplit, void* planes, int* flags,
+                         void* stream) {
+  MHMOE_REQUIRE(gate && planes && n_experts > 0 && dh > 0 && dh % 64 == 0 && nsplit >= 1 && nsplit <= 3);
+  MHMOE_CHECK_ARCH();
+  const cudaError_t e = launch_split_gate(gate, n_experts, dh, nsplit, static_cast<__nv_bfloat16*>(planes), flags,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "router_prepare");
+}
+
+int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const void* planes, int nsplit, int S, int H,
+                int dh, int E, int K, int score_func, const float* expert_bias, int route_norm, float norm_eps,
+                float route_scale, float* probs, int64_t* idx, float* logits, int* dev_status, void* stream) {
+  MHMOE_REQUIRE(x && planes && probs && idx);
+  MHMOE_REQUIRE(S >= 0 && H > 0 && dh > 0 && dh % 64 == 0 && E > 0 && E <= 256 && K > 0 && K <= 16 && K <= E);
+  MHMOE_REQUIRE(nsplit >= 1 && nsplit <= 3 && (score_func == 0 || score_func == 1));
+  MHMOE_REQUIRE(x_stride_h == dh && x_stride_s % 8 == 0 && x_stride_s >= (int64_t)H * dh && aligned16(x));
+  MHMOE_REQUIRE(aligned16(planes));
+  MHMOE_CHECK_ARCH();
+  if (S == 0) return MHMOE_OK;
+  cudaError_t ce = cudaSuccess;
+  const int rc = router_tc(static_cast<const __nv_bfloat16*>(x), x_stride_s, static_cast<const __nv_bfloat16*>(planes),
+                           nsplit, S, H, dh, E, K, score_func, expert_bias, route_norm, norm_eps, route_scale, probs,
+                           idx, logits, dev_status, static_cast<cudaStream_t>(stream), &ce);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "route");
+  if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed (route)";
+  return rc;
+}
+
 int mhmoe_topk(const float* logits, const float* expert_bias, int H, int S, int E, int K, int score_func,
                int num_virtual_group, int topk_virtual_group, int route_norm, float norm_eps, float route_scale,
                float* probs, int64_t* idx, void* stream) {

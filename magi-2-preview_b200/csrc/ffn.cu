@@ -28,19 +28,28 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
+// 2-D tensor map over [rows, inner] elements with the given row stride, 128-B swizzle.
+cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                           uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                           uint32_t box_rows) {
+  PFN_encodeTiled fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // 2-D uint8 tensor map over [rows, inner_bytes] (row pitch = inner_bytes), 128-B swizzle.
 cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows,
                               uint32_t box_inner, uint32_t box_rows) {
-  PFN_encodeTiled fn = get_encode_fn();
-  if (!fn) return cudaErrorNotSupported;
-  const cuuint64_t dims[2] = {inner_bytes, rows};
-  const cuuint64_t strides[1] = {inner_bytes};
-  const cuuint32_t box[2] = {box_inner, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, inner_bytes, rows, inner_bytes, box_inner,
+                        box_rows);
 }
 
 int num_sms() {

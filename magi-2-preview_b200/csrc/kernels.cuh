@@ -64,5 +64,16 @@ int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, con
                    uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);
 cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows,
                               uint32_t box_inner, uint32_t box_rows);
+cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                           uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
+                           uint32_t box_rows);
+
+// router_tc.cu
+cudaError_t launch_split_gate(const float* gate, int64_t HE, int dh, int nsplit, __nv_bfloat16* out, int* flags,
+                              cudaStream_t st);
+int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_planes, int nsplit, int S, int H,
+              int dh, int E, int K, int score_func, const float* bias, int route_norm, float norm_eps,
+              float route_scale, float* probs, int64_t* idx, float* logits, int* status, cudaStream_t st,
+              cudaError_t* cerr);
 
 }  // namespace mhmoe

@@ -1,0 +1,340 @@
+// Fused router on the tensor cores: fp32-accurate logits from bf16 tcgen05 MMAs, with
+// scoring, top-k, normalisation and route_scale in the epilogue.
+//
+// Replaces CoreMultiHeadMoE._route (inference/model/magi2_preview.py:2588-2601): the
+// fp32 einsum("shd,hed->hse") and compute_topk_probs_and_indices
+// (inference/flash_mh_moe/route.py:28-148, no virtual groups — MAGI-2 does not use them).
+//
+// Precision: x is bf16, so x * g for an fp32 gate weight g = hi + lo + lo2 (three bf16
+// planes, hi = bf16(g), lo = bf16(g - hi), lo2 = bf16(g - hi - lo)) is the sum of three
+// exactly representable products; the MMA accumulates them in fp32.  The logits match an
+// fp32 GEMM to fp32 rounding.  Gate planes that are all zero are skipped (nsplit < 3),
+// e.g. a bf16-valued gate needs one plane.
+//
+// GEMM shape per tile: M = 128 tokens (one head), N = E rounded up to 16 (<= 256),
+// K' = nsplit * dh, iterated as (dh block of 64, plane) so each x tile is re-read from L2
+// right after its first load.  Warp 0: TMA producer (x tile 128x64 bf16, gate tile
+// Nx64 bf16, 128-B swizzle, 4 stages); warp 1: TMEM owner + MMA issuer
+// (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-5: epilogue, one token row per thread.
+#include <mutex>
+
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+constexpr int RT_BM = 128;
+constexpr int RT_BK = 64;                // bf16 elements per stage row (128 B)
+constexpr int RT_STAGES = 4;
+constexpr int RT_THREADS = 192;
+constexpr int RT_MAXK = 16;
+
+struct RouterParams {
+  const float* bias;       // [H*E] or null
+  float* probs;            // [H, S, K]
+  int64_t* idx;            // [H, S, K]
+  float* logits;           // [H, S, E] or null
+  int S, H, dh, E, Npad, K, nsplit, score_func, route_norm;
+  float norm_eps, route_scale;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+// Insert (v, e, sc) into the descending list tv[0..K) (ties keep the earlier, lower
+// index first).  All indices are compile-time after unrolling, so the lists stay in
+// registers; `thr` caches tv[K-1] so most candidates are rejected by one compare.
+__device__ __forceinline__ void topk_insert(float v, int e, float sc, float* tv, int* ti, float* ts, int K,
+                                            float& thr) {
+  if (!(v > thr)) return;
+#pragma unroll
+  for (int j = RT_MAXK - 1; j >= 0; --j) {
+    if (j < K) {
+      if (j > 0 && v > tv[j > 0 ? j - 1 : 0]) {
+        tv[j] = tv[j > 0 ? j - 1 : 0];
+        ti[j] = ti[j > 0 ? j - 1 : 0];
+        ts[j] = ts[j > 0 ? j - 1 : 0];
+      } else if (v > tv[j]) {
+        tv[j] = v;
+        ti[j] = e;
+        ts[j] = sc;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RT_MAXK; ++j)
+    if (j == K - 1) thr = tv[j];
+}
+
+__global__ void __launch_bounds__(RT_THREADS, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
+                     const RouterParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int a_bytes = RT_BM * RT_BK * 2;
+  const int b_bytes = p.Npad * RT_BK * 2;
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + RT_STAGES * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + RT_STAGES * b_bytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + RT_STAGES;
+  uint64_t* tfull_bar = bars + 2 * RT_STAGES;
+  uint64_t* tempty_bar = tfull_bar + 1;
+  uint64_t* drain_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t tcols = p.Npad <= 32 ? 32 : p.Npad <= 64 ? 64 : p.Npad <= 128 ? 128 : 256;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RT_STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    mbar_init(smem_u32(tfull_bar), 1);
+    mbar_init(smem_u32(tempty_bar), 4);
+    mbar_init(smem_u32(drain_bar), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmG);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), tcols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int mtiles = (p.S + RT_BM - 1) / RT_BM;
+  const int total = mtiles * p.H;
+  const int nkb = p.dh / RT_BK;
+  const int nk = nkb * p.nsplit;
+  const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const int h = t / mtiles, mt = t % mtiles;
+        for (int k = 0; k < nk; ++k) {
+          const int kb = k / p.nsplit, sp = k % p.nsplit;
+          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, (uint32_t)(a_bytes + b_bytes));
+          tma_load_2d(smem_u32(sA + stage * a_bytes), &tmX, fb, h * p.dh + kb * RT_BK, mt * RT_BM);
+          tma_load_2d(smem_u32(sB + stage * b_bytes), &tmG, fb, (kb * p.nsplit + sp) * RT_BK, h * p.E);
+          if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      const uint32_t idesc = idesc_bf16(RT_BM, p.Npad);
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        tc_fence_after();
+        for (int k = 0; k < nk; ++k) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          tc_fence_after();
+          const uint32_t a_s = smem_u32(sA + stage * a_bytes);
+          const uint32_t b_s = smem_u32(sB + stage * b_bytes);
+#pragma unroll
+          for (int j = 0; j < RT_BK / 16; ++j)
+            mma_bf16(tmem_base, sdesc_kmajor_sw128(a_s + j * 32), sdesc_kmajor_sw128(b_s + j * 32), idesc,
+                     (k | j) != 0 ? 1u : 0u);
+          tc_commit(smem_u32(&empty_bar[stage]));
+          if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc_commit(smem_u32(tfull_bar));
+        acc_phase ^= 1;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int h = t / mtiles, mt = t % mtiles;
+      if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+      const int s = mt * RT_BM + m;
+      const bool valid = s < p.S;
+      const int64_t row = (int64_t)h * p.S + s;
+      const int nchunk = p.Npad / 32 + (p.Npad % 32 ? 1 : 0);
+      uint32_t r[32];
+      // pass 1: max (softmax) and optional logits output
+      float mx = -INFINITY;
+      for (int c = 0; c < nchunk; ++c) {
+        MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int e = c * 32 + i;
+          if (e < p.E) {
+            const float l = __uint_as_float(r[i]);
+            mx = fmaxf(mx, l);
+            if (valid && p.logits) p.logits[row * p.E + e] = l;
+          }
+        }
+      }
+      float sum = 0.f;
+      if (p.score_func == 0) {
+        for (int c = 0; c < nchunk; ++c) {
+          MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < p.E) sum += expf(__uint_as_float(r[i]) - mx);
+        }
+      }
+      float tv[RT_MAXK], ts[RT_MAXK], thr = -INFINITY;
+      int ti[RT_MAXK];
+#pragma unroll
+      for (int j = 0; j < RT_MAXK; ++j) {
+        tv[j] = -INFINITY;
+        ts[j] = 0.f;
+        ti[j] = 0;
+      }
+      for (int c = 0; c < nchunk; ++c) {
+        MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int e = c * 32 + i;
+          if (e < p.E) {
+            const float l = __uint_as_float(r[i]);
+            const float sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
+            const float v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
+            topk_insert(v, e, sc, tv, ti, ts, p.K, thr);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
+      if (valid) {
+        float nrm = 1.f;
+        if (p.route_norm) {
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < RT_MAXK; ++j)
+            if (j < p.K) a += fabsf(ts[j]);
+          nrm = fmaxf(a, p.norm_eps);
+        }
+#pragma unroll
+        for (int j = 0; j < RT_MAXK; ++j) {
+          if (j < p.K) {
+            const float pr = p.route_norm ? __fdiv_rn(ts[j], nrm) : ts[j];
+            p.probs[row * p.K + j] = __fmul_rn(pr, p.route_scale);
+            p.idx[row * p.K + j] = ti[j];
+          }
+        }
+      }
+    }
+  }
+done:
+  if (warp == 1 && lane == 0) {
+    tc_commit(smem_u32(drain_bar));
+    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, timeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tcols);
+  }
+}
+
+// gate fp32 [HE, dh] -> planes bf16 [HE, nsplit*dh], interleaved per 64-column block:
+// out[r, (kb*nsplit + s)*64 + j] = plane_s[r, kb*64 + j].  flags[s] |= plane s non-zero.
+__global__ void split_gate_kernel(const float* __restrict__ gate, int64_t HE, int dh, int nsplit,
+                                  __nv_bfloat16* __restrict__ out, int* __restrict__ flags) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= HE * dh) return;
+  const int64_t r = i / dh;
+  const int d = (int)(i % dh);
+  const float g = gate[i];
+  const __nv_bfloat16 hi = __float2bfloat16_rn(g);
+  const float rem1 = g - __bfloat162float(hi);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(rem1);
+  const float rem2 = rem1 - __bfloat162float(lo);
+  const __nv_bfloat16 lo2 = __float2bfloat16_rn(rem2);
+  const __nv_bfloat16 planes[3] = {hi, lo, lo2};
+  const int kb = d / 64, j = d % 64;
+  for (int s = 0; s < nsplit; ++s) {
+    out[r * (int64_t)nsplit * dh + (int64_t)(kb * nsplit + s) * 64 + j] = planes[s];
+  }
+  if (flags) {
+    if (__bfloat162float(lo) != 0.f) atomicOr(&flags[1], 1);
+    if (__bfloat162float(lo2) != 0.f) atomicOr(&flags[2], 1);
+  }
+}
+
+// 2-D bf16 tensor map [rows, inner] with the given row stride, 128-B swizzle.
+static cudaError_t encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                                  uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows) {
+  return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, rows, row_stride_bytes, box_inner,
+                        box_rows);
+}
+
+cudaError_t launch_split_gate(const float* gate, int64_t HE, int dh, int nsplit, __nv_bfloat16* out, int* flags,
+                              cudaStream_t st) {
+  const int64_t n = HE * dh;
+  split_gate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gate, HE, dh, nsplit, out, flags);
+  return cudaGetLastError();
+}
+
+int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_planes, int nsplit, int S, int H,
+              int dh, int E, int K, int score_func, const float* bias, int route_norm, float norm_eps,
+              float route_scale, float* probs, int64_t* idx, float* logits, int* status, cudaStream_t st,
+              cudaError_t* cerr) {
+  const int Npad = std::max(16, (E + 15) / 16 * 16);
+  CUtensorMap tx, tg;
+  if (encode_bf16_2d(&tx, x, (uint64_t)H * dh, (uint64_t)S, (uint64_t)sx_s * 2, RT_BK, RT_BM) != cudaSuccess ||
+      encode_bf16_2d(&tg, gate_planes, (uint64_t)nsplit * dh, (uint64_t)H * E, (uint64_t)nsplit * dh * 2, RT_BK,
+                     (uint32_t)Npad) != cudaSuccess)
+    return MHMOE_ERR_DRIVER;
+  RouterParams p{};
+  p.bias = bias;
+  p.probs = probs;
+  p.idx = idx;
+  p.logits = logits;
+  p.S = S;
+  p.H = H;
+  p.dh = dh;
+  p.E = E;
+  p.Npad = Npad;
+  p.K = K;
+  p.nsplit = nsplit;
+  p.score_func = score_func;
+  p.route_norm = route_norm;
+  p.norm_eps = norm_eps;
+  p.route_scale = route_scale;
+  p.status = status;
+  const int smem = RT_STAGES * (RT_BM * RT_BK * 2 + Npad * RT_BK * 2) + 256 + 1024;
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                RT_STAGES * (RT_BM * RT_BK * 2 + 256 * RT_BK * 2) + 256 + 1024);
+  });
+  if (attr != cudaSuccess) {
+    *cerr = attr;
+    return MHMOE_ERR_LAUNCH;
+  }
+  const int tiles = ((S + RT_BM - 1) / RT_BM) * H;
+  const int grid = std::max(1, std::min(tiles, num_sms()));
+  router_tc_kernel<<<grid, RT_THREADS, smem, st>>>(tx, tg, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *cerr = e;
+    return MHMOE_ERR_LAUNCH;
+  }
+  return MHMOE_OK;
+}
+
+}  // namespace mhmoe

@@ -25,7 +25,8 @@ import torch.nn as nn
 
 from .fwd import ffn_nvfp4
 from .nvfp4 import NVFP4Down, NVFP4GateUp, pack_down, pack_gate_up
-from .route import compute_topk_probs_and_indices, flash_mh_moe_global_sort_with_inverse, router_logits
+from .route import (compute_topk_probs_and_indices, flash_mh_moe_global_sort_with_inverse,
+                    fused_router_supported, route_fused, router_logits, router_prepare)
 
 
 @dataclass
@@ -79,6 +80,8 @@ class CoreMultiHeadMoE(nn.Module):
         self.router.register_buffer("expert_bias_ema", torch.zeros(self.flatten_num_experts, dtype=torch.float32))
         self._packed: tuple | None = None
         self._packed_key: tuple | None = None
+        self._router_planes: tuple | None = None
+        self._router_key: tuple | None = None
 
     # ── NVFP4 weights (quantise on load) ──
     def _weights_key(self):
@@ -97,13 +100,25 @@ class CoreMultiHeadMoE(nn.Module):
         self._packed = (gu, dn)
         self._packed_key = self._weights_key()
 
+    def router_planes(self) -> tuple[torch.Tensor, int]:
+        key = (self.gate.data_ptr(), self.gate._version)
+        if self._router_planes is None or self._router_key != key:
+            self._router_planes = router_prepare(self.gate)
+            self._router_key = key
+        return self._router_planes
+
     # ── reference structure ──
     def _route(self, x_heads: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """magi2_preview.py:2588-2601: fp32 logits -> top-k -> x route_scale."""
+        bias = self.router.expert_bias.view(self.num_heads, self.num_experts)
+        if fused_router_supported(self.num_experts, self.topk, self.d_head):
+            planes, nsplit = self.router_planes()
+            return route_fused(x_heads, planes, nsplit, self.num_experts, self.topk,
+                               score_func=self.config.score_func, expert_bias=bias,
+                               route_norm=self.config.route_norm, route_scale=float(self.config.route_scale))
         logits = router_logits(x_heads, self.gate, self.num_experts)
         return compute_topk_probs_and_indices(
-            logits, self.topk, score_func=self.config.score_func,
-            expert_bias=self.router.expert_bias.view(self.num_heads, self.num_experts),
+            logits, self.topk, score_func=self.config.score_func, expert_bias=bias,
             route_norm=self.config.route_norm, route_scale=float(self.config.route_scale))
 
     def _flash_forward(self, x_heads, topk_probs, topk_indices) -> torch.Tensor:

@@ -122,3 +122,62 @@ def router_logits(x_heads: torch.Tensor, gate: torch.Tensor, num_experts: int) -
                                                    int(num_experts), out.data_ptr(), _lib.stream_ptr(dev)),
                    "router_logits")
     return out
+
+
+# ───────────────────────── fused tensor-core router ─────────────────────────
+
+def router_prepare(gate: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """Split the fp32 router weight [H*E, dh] into the fewest exact bf16 planes (1..3)
+    the fused router needs (load-time work; reads back three flags)."""
+    _lib.require_cuda(gate)
+    g = gate.detach().float().contiguous()
+    n, dh = g.shape
+    dev = g.device
+    L = _lib.lib()
+    flags = torch.zeros(3, dtype=torch.int32, device=dev)
+    full = torch.empty(n, 3 * dh, dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.mhmoe_router_prepare(g.data_ptr(), n, dh, 3, full.data_ptr(), flags.data_ptr(),
+                                           _lib.stream_ptr(dev)), "router_prepare")
+        f = flags.tolist()
+        nsplit = 3 if f[2] else (2 if f[1] else 1)
+        if nsplit == 3:
+            return full, 3
+        planes = torch.empty(n, nsplit * dh, dtype=torch.bfloat16, device=dev)
+        _lib.check(L.mhmoe_router_prepare(g.data_ptr(), n, dh, nsplit, planes.data_ptr(), None,
+                                           _lib.stream_ptr(dev)), "router_prepare")
+    return planes, nsplit
+
+
+def fused_router_supported(E: int, K: int, dh: int) -> bool:
+    return E <= 256 and K <= 16 and dh % 64 == 0
+
+
+def route_fused(x_heads: torch.Tensor, planes: torch.Tensor, nsplit: int, num_experts: int, top_k: int,
+                score_func: str = "softmax", expert_bias: torch.Tensor | None = None, route_norm: bool = True,
+                norm_eps: float = 1e-12, route_scale: float = 1.0, return_logits: bool = False):
+    """Router logits + top-k in one tcgen05 kernel (``CoreMultiHeadMoE._route``).
+
+    x_heads [S, H, dh] bf16 (heads contiguous).  Returns (probs fp32 [H,S,K], idx int64
+    [H,S,K]) and, with ``return_logits``, the fp32 logits [H,S,E] as a third item.
+    """
+    if score_func not in score_func_name2id_map:
+        raise ValueError(f"Unknown score_func: {score_func}")
+    _lib.require_cuda(x_heads, planes)
+    S, H, dh = x_heads.shape
+    E, K = int(num_experts), int(top_k)
+    x = x_heads if x_heads.dtype == torch.bfloat16 else x_heads.to(torch.bfloat16)
+    if x.stride(2) != 1 or x.stride(1) != dh or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    dev = x.device
+    probs = torch.empty(H, S, K, dtype=torch.float32, device=dev)
+    idx = torch.empty(H, S, K, dtype=torch.int64, device=dev)
+    logits = torch.empty(H, S, E, dtype=torch.float32, device=dev) if return_logits else None
+    bias = None if expert_bias is None else expert_bias.reshape(-1).float().contiguous()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().mhmoe_route(
+            x.data_ptr(), x.stride(0), x.stride(1), planes.data_ptr(), int(nsplit), S, H, dh, E, K,
+            score_func_name2id_map[score_func], _lib.ptr(bias), int(bool(route_norm)), float(norm_eps),
+            float(route_scale), probs.data_ptr(), idx.data_ptr(), _lib.ptr(logits),
+            _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)), "route")
+    return (probs, idx, logits) if return_logits else (probs, idx)

@@ -89,3 +89,35 @@ def test_router_logits_fp32(S, H, dh, E):
     ref = route_ref.router_logits(x.float().numpy(), gate.numpy(), E)
     assert rel_l2(to_np(out), ref) < 1e-6
     np.testing.assert_allclose(to_np(out), ref, rtol=1e-4, atol=1e-5)
+
+
+FUSED = [
+    # S, H, dh, E, K, score, bias, route_scale, bf16_gate
+    (512, 1, 1024, 8, 2, "softmax", False, 1.0, True),      # config-0 router
+    (1000, 1, 3072, 128, 8, "softmax", False, 1.0, True),   # config-1 router (partial batch)
+    (300, 2, 256, 64, 4, "sigmoid", True, 2.5, False),      # fp32 gate -> 3 planes
+    (130, 12, 256, 256, 6, "sigmoid", True, 4.9, False),    # production head split
+    (77, 1, 128, 40, 16, "softmax", True, 1.0, False),      # ragged E, K = 16
+]
+
+
+@pytest.mark.parametrize("S,H,dh,E,K,score,use_bias,scale,bf16_gate", FUSED)
+def test_fused_router_matches_reference(S, H, dh, E, K, score, use_bias, scale, bf16_gate):
+    from flash_mh_moe.route import route_fused, router_prepare
+    g = torch.Generator().manual_seed(S * 7 + E)
+    x = torch.randn(S, H, dh, generator=g).to(torch.bfloat16)
+    gate = torch.randn(H * E, dh, generator=g) * 0.02
+    if bf16_gate:
+        gate = gate.to(torch.bfloat16).float()
+    bias = (torch.randn(H, E, generator=g) * 0.01) if use_bias else None
+    planes, nsplit = router_prepare(gate.cuda())
+    assert nsplit == (1 if bf16_gate else 3)
+    probs, idx, logits = route_fused(x.cuda(), planes, nsplit, E, K, score, None if bias is None else bias.cuda(),
+                                     True, 1e-12, scale, return_logits=True)
+    ref_logits = route_ref.router_logits(x.float().numpy(), gate.numpy(), E)
+    gl = to_np(logits)
+    assert rel_l2(gl, ref_logits) < 1e-6
+    # routing parity on the GPU's own logits (the reference contract is route.py on the logits)
+    rp, ri = route_ref.compute_topk_probs_and_indices(gl, K, score, None if bias is None else bias.numpy())
+    np.testing.assert_array_equal(to_np(idx), ri)
+    np.testing.assert_allclose(to_np(probs), rp * np.float32(scale), rtol=3e-6, atol=1e-7)
