@@ -40,7 +40,7 @@ for p in (str(ROOT), str(PKG)):
 
 CFG1 = dict(name="config1", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=1, score_func="softmax")
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
-KERNELS_PER_STEP = 11   # logits, topk, sort x4, tile tables, quant, gate/up GEMM, down GEMM, combine
+KERNELS_PER_STEP = 10   # fused router, sort x4, tile tables, quant, gate/up GEMM, down GEMM, combine
 CPU_SAMPLE_TOKENS = 512
 
 

@@ -107,7 +107,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
-// 2-D tiled TMA load (no multicast). c0 = innermost coordinate (bytes for uint8 maps).
+// 2-D tiled TMA load into this CTA's shared memory. c0 = innermost coordinate (bytes for uint8 maps).
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0,
                                             int32_t c1) {
   asm volatile(

@@ -116,8 +116,18 @@ def test_fused_router_matches_reference(S, H, dh, E, K, score, use_bias, scale, 
                                      True, 1e-12, scale, return_logits=True)
     ref_logits = route_ref.router_logits(x.float().numpy(), gate.numpy(), E)
     gl = to_np(logits)
-    assert rel_l2(gl, ref_logits) < 1e-6
+    # Products are exact (x is bf16, the gate is split into exact bf16 planes); the
+    # tensor core's fp32 accumulation is coarser than an IEEE FMA chain: measured
+    # 3.3e-6 relative L2 at dh = 3072.  Bound: 1e-5.
+    assert rel_l2(gl, ref_logits) < 1e-5
     # routing parity on the GPU's own logits (the reference contract is route.py on the logits)
-    rp, ri = route_ref.compute_topk_probs_and_indices(gl, K, score, None if bias is None else bias.numpy())
+    b = None if bias is None else bias.numpy()
+    rp, ri = route_ref.compute_topk_probs_and_indices(gl, K, score, b)
     np.testing.assert_array_equal(to_np(idx), ri)
     np.testing.assert_allclose(to_np(probs), rp * np.float32(scale), rtol=3e-6, atol=1e-7)
+    # near-tie flips against fp64 logits: only tokens whose k-th / (k+1)-th scores are
+    # within the logit error may choose a different set
+    _, ri64 = route_ref.compute_topk_probs_and_indices(ref_logits, K, score, b)
+    flips = int((np.sort(ri, -1) != np.sort(ri64, -1)).any(-1).sum())
+    print(f"logit rel L2 {rel_l2(gl, ref_logits):.2e}; top-{K} set flips vs fp64 logits: {flips}/{H * S}")
+    assert flips <= max(1, H * S // 200)
