@@ -155,6 +155,9 @@ def run_ours(args, world, rank, local):
     m, x_host = make_layer(cfg, dev, rank)
     x = x_host.to(dev)
     m.packed_weights()
+    if args.release_master:
+        m.release_master_weights()
+        torch.cuda.empty_cache()
     torch.cuda.synchronize()
 
     nev = 7
@@ -265,7 +268,7 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "gpu_launches": KERNELS_PER_STEP * args.steps,   # kernels of libmhmoe inside the device-timed region
         "clocks": clk.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not args.release_master:
         out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
     return out
 
@@ -354,6 +357,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--release-master", action="store_true",
+                    help="free the bf16 expert weights after NVFP4 packing (profiler captures)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default: config 1's 16384; smaller only for profiler captures)")
     args = ap.parse_args()

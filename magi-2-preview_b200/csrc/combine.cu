@@ -12,9 +12,20 @@ namespace mhmoe {
 
 constexpr int COMBINE_WARPS = 4;
 
-__global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, int dh, int S, int H,
+// pad_of_row[r] = padded row of sorted row r: mt * 128 + m for tile rows m < tile_rows[mt].
+__global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const int* __restrict__ tile_row0,
+                                const int* __restrict__ tile_rows, int32_t* __restrict__ pad_of_row) {
+  const int mt = blockIdx.x;
+  if (mt >= cu_tiles[HE]) return;
+  const int m = threadIdx.x;
+  if (m < tile_rows[mt]) pad_of_row[tile_row0[mt] + m] = mt * 128 + m;
+}
+
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row, int dh,
+                               int S, int H,
                                const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
-                               int k_fixed, int64_t R, __nv_bfloat16* __restrict__ y, int64_t sy_s, int64_t sy_h) {
+                               int k_fixed, int64_t R, int64_t P_rows, __nv_bfloat16* __restrict__ y, int64_t sy_s,
+                               int64_t sy_h) {
   __shared__ int srt[COMBINE_WARPS][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
@@ -36,12 +47,17 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, int dh, int 
     // rank sort of <= 32 row ids (ascending; ids are distinct)
     int r = lane < cnt ? tok_rows[begin + lane] : 0x7fffffff;
     if (r < 0 || r >= R) r = 0x7fffffff;            // invalid id: dropped
+    int prow = r == 0x7fffffff ? 0x7fffffff : (pad_of_row ? pad_of_row[r] : r);
+    if (prow < 0 || prow >= P_rows) {               // never read outside P
+      prow = 0x7fffffff;
+      r = 0x7fffffff;
+    }
     int rank = 0;
     for (int j = 0; j < 32; ++j) {
       const int o = __shfl_sync(0xffffffffu, r, j);
       rank += (o < r) || (o == r && j < lane);
     }
-    srt[warp][rank] = r;
+    srt[warp][rank] = prow;   // ascending sorted row <=> ascending padded row
     __syncwarp();
     int nvalid = 0;
     for (int j = 0; j < cnt; ++j) nvalid += srt[warp][j] != 0x7fffffff;
@@ -77,7 +93,9 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, int dh, int 
         }
         if (best == 0x7fffffff) break;
         last = best;
-        const uint4 u = *reinterpret_cast<const uint4*>(P + (int64_t)best * dh + c * 8);
+        const int64_t prow = pad_of_row ? pad_of_row[best] : best;
+        if (prow < 0 || prow >= P_rows) continue;
+        const uint4 u = *reinterpret_cast<const uint4*>(P + prow * dh + c * 8);
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -96,12 +114,18 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, int dh, int 
   }
 }
 
-cudaError_t launch_combine(const __nv_bfloat16* P, int dh, int S, int H, const int32_t* tok_rows,
-                           const int32_t* tok_offsets, int k_fixed, int64_t R, __nv_bfloat16* y, int64_t sy_s,
-                           int64_t sy_h, cudaStream_t st) {
+cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
+                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st) {
+  pad_rows_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(cu_tiles, HE, tile_row0, tile_rows, pad_of_row);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh, int S, int H,
+                           const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
+                           int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
   const int64_t keys = (int64_t)H * S;
   combine_kernel<<<(unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st>>>(
-      P, dh, S, H, tok_rows, tok_offsets, k_fixed, R, y, sy_s, sy_h);
+      P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
   return cudaGetLastError();
 }
 

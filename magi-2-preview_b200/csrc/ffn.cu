@@ -60,17 +60,17 @@ int num_sms() {
 }
 
 template <int EPI>
-static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const FfnGemmParams& p,
-                               int64_t max_work, cudaStream_t st) {
+static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                               const FfnGemmParams& p, int64_t max_work, cudaStream_t st) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(ffn_gemm_nvfp4_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    GEMM_SMEM_BYTES);
+                                    gemm_smem_bytes(EPI));
   });
   if (attr_err != cudaSuccess) return attr_err;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), max_work));
-  ffn_gemm_nvfp4_kernel<EPI><<<grid, GEMM_THREADS, GEMM_SMEM_BYTES, st>>>(ta, tb, p);
+  ffn_gemm_nvfp4_kernel<EPI><<<grid, GEMM_THREADS, gemm_smem_bytes(EPI), st>>>(ta, tb, tc, p);
   return cudaGetLastError();
 }
 
@@ -81,12 +81,13 @@ struct FfnWorkspace {
   int* tile_expert;
   int* tile_row0;
   int* tile_rows;
-  uint8_t* a_data;
-  uint8_t* a_sf;
-  float* a_gscale;
-  uint8_t* h_data;
-  uint8_t* h_sf;
-  __nv_bfloat16* P;
+  int32_t* pad_of_row;   // [R] sorted row -> padded row
+  uint8_t* xq;           // [T, dh/2]  per-token quantised x (T = S*H rows, row = s*H + h)
+  uint8_t* xsf;          // [T, dh/16] row-major scales
+  float* xg;             // [T]
+  uint8_t* h_data;       // [rows_pad, de/2] quantised SwiGLU hidden
+  uint8_t* h_sf;         // SF atoms of the hidden
+  __nv_bfloat16* P;      // [rows_pad, dh] bf16(y_acc * prob) per padded row
   int32_t* tok_offsets;
   int32_t* tok_rows;
   void* tok_ws;
@@ -109,12 +110,13 @@ static FfnWorkspace carve(uint8_t* base, int64_t R, int64_t T, int dh, int de, i
   w.tile_expert = reinterpret_cast<int*>(take(sizeof(int) * mt));
   w.tile_row0 = reinterpret_cast<int*>(take(sizeof(int) * mt));
   w.tile_rows = reinterpret_cast<int*>(take(sizeof(int) * mt));
-  w.a_data = take((size_t)rows * dh / 2);
-  w.a_sf = take((size_t)rows * dh / 16);
-  w.a_gscale = reinterpret_cast<float*>(take(sizeof(float) * rows));
+  w.pad_of_row = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(R, 1)));
+  w.xq = take((size_t)T * dh / 2);
+  w.xsf = take((size_t)T * dh / 16);
+  w.xg = reinterpret_cast<float*>(take(sizeof(float) * T));
   w.h_data = take((size_t)rows * de / 2);
   w.h_sf = take((size_t)rows * de / 16);
-  w.P = reinterpret_cast<__nv_bfloat16*>(take(sizeof(__nv_bfloat16) * (size_t)R * dh));
+  w.P = reinterpret_cast<__nv_bfloat16*>(take(sizeof(__nv_bfloat16) * (size_t)rows * dh));
   w.tok_offsets = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * (T + 1)));
   w.tok_rows = reinterpret_cast<int32_t*>(take(sizeof(int32_t) * std::max<int64_t>(R, 1)));
   w.tok_ws = take(token_rows_ws_bytes(T));
@@ -152,19 +154,20 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   mark(0);
   MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
                                status, st));
-  MHMOE_TRY(launch_quant_gather(x, sx_s, sx_h, S, dh, HE / H, gather_ids, w.cu_tiles, HE, max_mt, w.tile_expert,
-                                w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale, status, st));
+  MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
+  MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
 
-  CUtensorMap ta1, tb1, ta2, tb2;
-  if (encode_tmap_2d_u8(&ta1, w.a_data, dh / 2, rows, 128, 128) != cudaSuccess ||
+  CUtensorMap ta1, tb1, ta2, tb2, tc2;
+  if (encode_tmap_2d_u8(&ta1, w.xq, dh / 2, (uint64_t)T, 128, 1) != cudaSuccess ||
       encode_tmap_2d_u8(&tb1, gu_data, dh / 2, (uint64_t)HE * 2 * de, 128, 256) != cudaSuccess ||
       encode_tmap_2d_u8(&ta2, w.h_data, de / 2, rows, 128, 128) != cudaSuccess ||
-      encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess)
+      encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess ||
+      encode_tmap_2d(&tc2, w.P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dh, rows, (uint64_t)dh * 2, 64, 32) !=
+          cudaSuccess)
     return MHMOE_ERR_DRIVER;
 
   mark(1);
   FfnGemmParams p1{};
-  p1.sfa = w.a_sf;
   p1.sfb = gu_sf;
   p1.n_mtiles_dev = w.cu_tiles + HE;
   p1.n_mtiles_host = (int)max_mt;
@@ -173,14 +176,19 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p1.tile_rows = w.tile_rows;
   p1.K = dh;
   p1.N = 2 * de;
-  p1.row_gscale = w.a_gscale;
+  p1.gather_ids = gather_ids;
+  p1.xsf = w.xsf;
+  p1.xg = w.xg;
+  p1.H = H;
+  p1.E_per_head = HE / H;
+  p1.T = (int)T;
   p1.gs_gate = gu_gscale;
   p1.gs_up = gu_gscale + HE;
   p1.h_data = w.h_data;
   p1.h_sf = w.h_sf;
   p1.status = status;
   p1.timeout_ns = timeout_ns;
-  MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, p1, max_mt * (2 * de / GEMM_BN), st));
+  MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, ta1, p1, max_mt * (2 * de / GEMM_BN), st));
 
   mark(2);
   FfnGemmParams p2 = p1;
@@ -190,8 +198,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p2.N = dh;
   p2.probs = probs_sorted;
   p2.gs_down = dn_gscale;
-  p2.out_bf16 = w.P;
-  MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, p2, max_mt * (dh / GEMM_BN), st));
+  MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
 
   mark(3);
   const int32_t* rows_map = tok_rows;
@@ -204,7 +211,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     offs_map = w.tok_offsets;
     kf = 0;
   }
-  MHMOE_TRY(launch_combine(w.P, dh, S, H, rows_map, offs_map, kf, R, y, sy_s, sy_h, st));
+  MHMOE_TRY(launch_combine(w.P, w.pad_of_row, dh, S, H, rows_map, offs_map, kf, R, rows, y, sy_s, sy_h, st));
   mark(4);
 #undef MHMOE_TRY
   return MHMOE_OK;
@@ -228,7 +235,7 @@ int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, con
   p.out_f32 = out;
   p.status = status;
   p.timeout_ns = timeout_ns;
-  const cudaError_t e = launch_gemm<EPI_RAW>(ta, tb, p, (int64_t)n_mtiles * (N / GEMM_BN), st);
+  const cudaError_t e = launch_gemm<EPI_RAW>(ta, tb, ta, p, (int64_t)n_mtiles * (N / GEMM_BN), st);
   if (e != cudaSuccess) {
     *cerr = e;
     return MHMOE_ERR_LAUNCH;

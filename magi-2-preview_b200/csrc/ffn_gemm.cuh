@@ -7,9 +7,13 @@
 //   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
 //
 // Warp roles (320 threads):
-//   warp 0      TMA producer: A tile (128 x 256 FP4 = 16 KB, 128-B swizzle), B tile
-//               (256 x 256 FP4 = 32 KB), and their UE4M3 scale atoms (2 KB + 4 KB,
-//               untiled bulk copies) into a 4-stage shared-memory ring.
+//   warp 0      producer into a shared-memory stage ring (one stage = 256 K-elements):
+//               B tile (256 x 256 FP4 = 32 KB, TMA, 128-B swizzle) and its UE4M3 scale
+//               atoms (4 KB, untiled bulk copies);
+//               A tile (128 x 256 FP4 = 16 KB): for EPI_SWIGLU gathered straight from the
+//               per-token quantised x with TMA tile::gather4 (each lane fetches its 4 rows)
+//               while the lanes place the rows' scale bytes into the atom layout; for the
+//               other epilogues a tiled TMA load of an already grouped operand.
 //   warp 1      TMEM owner + MMA issuer: per stage copies the scale atoms into TMEM
 //               (tcgen05.cp 32x128b.warpx4) and issues 4 x tcgen05.mma
 //               kind::mxf4nvf4 block16 (M128 N256 K64).
@@ -24,8 +28,8 @@
 //               gives 16 hidden values: h = swiglu7(acc_g * s_gate, acc_u * s_up),
 //               quantised to NVFP4 with the static hidden scale and written as the
 //               A operand (data + SF atoms) of the down GEMM.
-//   EPI_DOWN    y_row = bf16(acc * s_down * prob) written to the sorted-row partial
-//               buffer P[R, N].
+//   EPI_DOWN    bf16(acc * s_down * prob) staged in swizzled shared memory and written
+//               with TMA stores into the padded partial buffer P[rows_pad, N].
 //   EPI_RAW     fp32 accumulator written as is (verification only).
 #pragma once
 
@@ -38,34 +42,44 @@ enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2 };
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
 constexpr int GEMM_BK = 256;          // FP4 elements per stage = 128 bytes per row
-constexpr int GEMM_STAGES = 4;
 constexpr int GEMM_THREADS = 320;
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK / 2;          // 16384
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK / 2;          // 32768
 constexpr int GEMM_SFA_BYTES = GEMM_BM * GEMM_BK / 16;       // 2048
 constexpr int GEMM_SFB_BYTES = GEMM_BN * GEMM_BK / 16;       // 4096
 constexpr int GEMM_STAGE_TX = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFA_BYTES + GEMM_SFB_BYTES;
-constexpr int GEMM_SMEM_BYTES =
-    GEMM_STAGES * GEMM_STAGE_TX + 256 /* barriers + tmem slot */ + 1024 /* alignment slack */;
+constexpr int GEMM_STAGE_BYTES = GEMM_STAGE_TX;
+constexpr int GEMM_STAGE_TMA = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFB_BYTES;   // gather mode: SFA by threads
+constexpr int GEMM_STG_BYTES = 8 * 32 * 128;                 // EPI_DOWN: 4 KB store staging per epilogue warp
 constexpr int GEMM_TMEM_COLS = 512;
 constexpr int GEMM_SF_COL0 = 256;
 constexpr int GEMM_SF_COLS_PER_STAGE = 48;
+
+__host__ __device__ constexpr int gemm_stages(int epi) { return epi == EPI_DOWN ? 3 : 4; }
+__host__ __device__ constexpr int gemm_smem_bytes(int epi) {
+  return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
+}
 
 // Static second-level scale of the SwiGLU7 hidden: |swiglu7| <= 7 * 8 = 56, 56 / 2688.
 constexpr float HIDDEN_GSCALE = 56.0f / 2688.0f;
 
 struct FfnGemmParams {
-  const uint8_t* sfa;        // A scale atoms (row space of 128 * n_mtiles rows)
+  const uint8_t* sfa;        // A scale atoms (tiled A modes)
   const uint8_t* sfb;        // B scale atoms, per expert contiguous: N*K/16 bytes each
   const int* n_mtiles_dev;   // device scalar: number of valid m-tiles (or nullptr)
   int n_mtiles_host;         // m-tiles the buffers hold (caps n_mtiles_dev)
   const int* tile_expert;    // [m-tile] -> flattened expert id
-  const int* tile_row0;      // [m-tile] -> first sorted row (EPI_DOWN)
+  const int* tile_row0;      // [m-tile] -> first sorted row
   const int* tile_rows;      // [m-tile] -> valid rows in the tile
   int K;                     // reduction length in elements
   int N;                     // B rows per expert
-  // EPI_SWIGLU
-  const float* row_gscale;   // [128 * n_mtiles] second-level scale of each A row
+  // EPI_SWIGLU (A gathered from the per-token quantised x)
+  const int32_t* gather_ids; // [R] token of each sorted row
+  const uint8_t* xsf;        // [T, K/16] row-major UE4M3 scales of the quantised tokens
+  const float* xg;           // [T] second-level scale of each quantised token row
+  int H;                     // heads: token row = gather_id * H + head
+  int E_per_head;
+  int T;                     // quantised token rows (S * H)
   const float* gs_gate;      // [n_experts]
   const float* gs_up;        // [n_experts]
   uint8_t* h_data;           // [128 * n_mtiles, N/4]  (hidden has N/2 columns, 2 per byte)
@@ -73,7 +87,6 @@ struct FfnGemmParams {
   // EPI_DOWN
   const float* probs;        // [R] sorted probs
   const float* gs_down;      // [n_experts]
-  __nv_bfloat16* out_bf16;   // [R, N]
   // EPI_RAW
   float* out_f32;            // [128 * n_mtiles, N]
   int* status;
@@ -87,20 +100,27 @@ __device__ __forceinline__ float swiglu7(float g, float u) {
   return g * sig * (u + 1.0f);
 }
 
+// tmA: EPI_SWIGLU -> quantised tokens [T, K/2] with a 128 x 1 box (gather4);
+//      otherwise  -> grouped A operand [128 * n_mtiles, K/2], box 128 x 128.
+// tmB: B operand [n_experts * N, K/2], box 128 x 256.
+// tmC: EPI_DOWN -> P [128 * n_mtiles, N] bf16, box 64 x 32 (store); unused otherwise.
 template <int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                          const FfnGemmParams p) {
+                          const __grid_constant__ CUtensorMap tmC, const FfnGemmParams p) {
+  constexpr int STAGES = gemm_stages(EPI);
+  constexpr bool GATHER = EPI == EPI_SWIGLU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = sA + GEMM_STAGES * GEMM_A_BYTES;
-  uint8_t* sSFA = sB + GEMM_STAGES * GEMM_B_BYTES;
-  uint8_t* sSFB = sSFA + GEMM_STAGES * GEMM_SFA_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSFB + GEMM_STAGES * GEMM_SFB_BYTES);
+  uint8_t* sB = sA + STAGES * GEMM_A_BYTES;
+  uint8_t* sSFA = sB + STAGES * GEMM_B_BYTES;
+  uint8_t* sSFB = sSFA + STAGES * GEMM_SFA_BYTES;
+  uint8_t* sSTG = sSFB + STAGES * GEMM_SFB_BYTES;                     // EPI_DOWN staging (1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSTG + (EPI == EPI_DOWN ? GEMM_STG_BYTES : 0));
   uint64_t* full_bar = bars;                       // [STAGES]
-  uint64_t* empty_bar = bars + GEMM_STAGES;        // [STAGES]
-  uint64_t* tfull_bar = bars + 2 * GEMM_STAGES;    // accumulator ready
+  uint64_t* empty_bar = bars + STAGES;             // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * STAGES;         // accumulator ready
   uint64_t* tempty_bar = tfull_bar + 1;            // accumulator drained
   uint64_t* drain_bar = tfull_bar + 2;             // all issued tcgen05 ops retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
@@ -109,8 +129,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GEMM_STAGES; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), GATHER ? 2 : 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     mbar_init(smem_u32(tfull_bar), 1);
@@ -119,6 +139,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (EPI == EPI_DOWN) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), GEMM_TMEM_COLS);
@@ -136,32 +157,78 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
 
   if (warp == 0) {
-    // ───────── TMA producer ─────────
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      const size_t sfa_row_atoms = (size_t)(p.K / 64);
-      const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const int mt = t / n_ntiles, nt = t % n_ntiles;
-        const int e = p.tile_expert[mt];
-        const int brow = e * p.N + nt * GEMM_BN;
-        for (int kb = 0; kb < n_kblk; ++kb) {
-          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
-          const uint32_t fb = smem_u32(&full_bar[stage]);
-          mbar_arrive_expect_tx(fb, GEMM_STAGE_TX);
-          tma_load_2d(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
+    // ───────── producer ─────────
+    int stage = 0;
+    uint32_t phase = 0;
+    const size_t k_atoms = (size_t)(p.K / 64);
+    const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int mt = t / n_ntiles, nt = t % n_ntiles;
+      const int e = p.tile_expert[mt];
+      const int brow = e * p.N + nt * GEMM_BN;
+      int trow[4] = {0, 0, 0, 0};   // gather mode: quantised token row of tile rows 4*lane + j
+      if constexpr (GATHER) {
+        const int nrows = p.tile_rows[mt], row0 = p.tile_row0[mt];
+        const int h = e / p.E_per_head;
+        int fallback = p.gather_ids[row0] * p.H + h;            // padding rows re-read a real row
+        if (fallback < 0 || fallback >= p.T) fallback = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int m = 4 * lane + j;
+          int r = fallback;
+          if (m < nrows) {
+            const int s = p.gather_ids[row0 + m];
+            r = s * p.H + h;
+            if (s < 0 || r >= p.T) {            // out-of-range token id: never dereference it
+              record_error(p.status, MHMOE_ERR_ARGS);
+              r = fallback;
+            }
+          }
+          trow[j] = r;
+        }
+      }
+      for (int kb = 0; kb < n_kblk; ++kb) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) goto done;
+        const uint32_t fb = smem_u32(&full_bar[stage]);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(fb, GATHER ? GEMM_STAGE_TMA : GEMM_STAGE_TX);
           tma_load_2d(smem_u32(sB + stage * GEMM_B_BYTES), &tmB, fb, kb * (GEMM_BK / 2), brow);
-          const uint8_t* sfa_src = p.sfa + ((size_t)mt * sfa_row_atoms + (size_t)kb * 4) * 512;
-          bulk_load(smem_u32(sSFA + stage * GEMM_SFA_BYTES), sfa_src, GEMM_SFA_BYTES, fb);
 #pragma unroll
           for (int nb = 0; nb < 2; ++nb) {
-            const uint8_t* sfb_src = p.sfb + (size_t)e * sfb_expert_bytes +
-                                     ((size_t)(nt * 2 + nb) * sfa_row_atoms + (size_t)kb * 4) * 512;
+            const uint8_t* sfb_src =
+                p.sfb + (size_t)e * sfb_expert_bytes + ((size_t)(nt * 2 + nb) * k_atoms + (size_t)kb * 4) * 512;
             bulk_load(smem_u32(sSFB + stage * GEMM_SFB_BYTES + nb * 2048), sfb_src, 2048, fb);
           }
-          if (++stage == GEMM_STAGES) { stage = 0; phase ^= 1; }
+          if constexpr (!GATHER) {
+            tma_load_2d(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
+            const uint8_t* sfa_src = p.sfa + ((size_t)mt * k_atoms + (size_t)kb * 4) * 512;
+            bulk_load(smem_u32(sSFA + stage * GEMM_SFA_BYTES), sfa_src, GEMM_SFA_BYTES, fb);
+          }
         }
+        if constexpr (GATHER) {
+          __syncwarp();
+          tma_gather4(smem_u32(sA + stage * GEMM_A_BYTES + lane * 512), &tmA, fb, kb * (GEMM_BK / 2), trow[0],
+                      trow[1], trow[2], trow[3]);
+          // this stage's 16 scale bytes of each of the lane's rows -> 4 atoms x 4 bytes
+          uint8_t* sfa_s = sSFA + stage * GEMM_SFA_BYTES;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int m = 4 * lane + j;
+            const uint4 v = *reinterpret_cast<const uint4*>(p.xsf + (size_t)trow[j] * (size_t)(p.K / 16) + kb * 16);
+            const uint32_t off = (uint32_t)((m & 31) * 16 + (m >> 5) * 4);
+            *reinterpret_cast<uint32_t*>(sfa_s + 0 * 512 + off) = v.x;
+            *reinterpret_cast<uint32_t*>(sfa_s + 1 * 512 + off) = v.y;
+            *reinterpret_cast<uint32_t*>(sfa_s + 2 * 512 + off) = v.z;
+            *reinterpret_cast<uint32_t*>(sfa_s + 3 * 512 + off) = v.w;
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(fb);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
@@ -194,7 +261,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                      tsfa + j * 4, tsfb + j * 8, (kb | j) != 0 ? 1u : 0u);
           }
           tc_commit(smem_u32(&empty_bar[stage]));
-          if (++stage == GEMM_STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         tc_commit(smem_u32(tfull_bar));
         acc_phase ^= 1;
@@ -225,7 +292,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int e = p.tile_expert[mt];
       const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
       if constexpr (EPI == EPI_SWIGLU) {
-        const float gr = p.row_gscale[prow];
+        float gr = 1.0f;
+        if (m < p.tile_rows[mt]) {
+          const int s = p.gather_ids[p.tile_row0[mt] + m];
+          const int tr = s * p.H + e / p.E_per_head;
+          if (s >= 0 && tr < p.T) gr = p.xg[tr];
+        }
         const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
         const float s_up = __fmul_rn(gr, p.gs_up[e]);
         const int hid_cols = p.N / 2;
@@ -233,15 +305,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         uint32_t sfw = 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float h[16];
+          float hv[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float g = __fmul_rn(__uint_as_float(r[c * 32 + i]), s_gate);
             const float u = __fmul_rn(__uint_as_float(r[c * 32 + 16 + i]), s_up);
-            h[i] = swiglu7(g, u);
+            hv[i] = swiglu7(g, u);
           }
           uint32_t w2[2];
-          const uint32_t sf = quant_block16(h, HIDDEN_GSCALE, w2);
+          const uint32_t sf = quant_block16(hv, HIDDEN_GSCALE, w2);
           words[2 * c] = w2[0];
           words[2 * c + 1] = w2[1];
           sfw |= sf << (8 * c);
@@ -253,22 +325,35 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         *reinterpret_cast<uint32_t*>(p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols)) =
             sfw;
       } else if constexpr (EPI == EPI_DOWN) {
-        if (m < p.tile_rows[mt]) {
-          const size_t row = (size_t)p.tile_row0[mt] + m;
-          const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
-          const float pr = p.probs[row];
-          uint4* dst = reinterpret_cast<uint4*>(p.out_bf16 + row * (size_t)p.N + nt * GEMM_BN + half * 128);
+        const int nrows = p.tile_rows[mt];
+        const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
+        const float pr = m < nrows ? p.probs[p.tile_row0[mt] + m] : 0.0f;
+        uint8_t* stg = sSTG + (warp - 2) * (32 * 128);
+        const uint32_t stg_s = smem_u32(stg);
 #pragma unroll
-          for (int v = 0; v < 16; ++v) {
+        for (int box = 0; box < 2; ++box) {
+          // the previous box's TMA store must have finished reading the staging buffer
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {            // 16-B chunk c of this row: columns box*64 + 8c .. +7
             uint32_t w[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[v * 8 + 2 * j]), s), pr);
-              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[v * 8 + 2 * j + 1]), s), pr);
+              const int col = box * 64 + c * 8 + 2 * j;
+              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
+              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
               __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
               w[j] = *reinterpret_cast<uint32_t*>(&h2);
             }
-            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+            // 128-B swizzle: chunk c of row `lane` sits at chunk c ^ (lane & 7)
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg_s, nt * GEMM_BN + half * 128 + box * 64, mt * GEMM_BM + q * 32);
+            bulk_commit();
           }
         }
       } else {
@@ -278,6 +363,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
                                __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
       }
+    }
+    if constexpr (EPI == EPI_DOWN) {
+      if (lane == 0) bulk_wait_all();     // stores complete before the CTA exits
     }
   }
 done:

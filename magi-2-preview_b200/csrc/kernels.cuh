@@ -30,6 +30,8 @@ cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx
                                 const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
                                 const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
                                 uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
+cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
+                                uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st);
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
                                  float* gscale, cudaStream_t st);
 cudaError_t launch_pack_weights(int kind, const __nv_bfloat16* w0, const __nv_bfloat16* w1, int n_experts, int dh,
@@ -43,9 +45,11 @@ cudaError_t launch_topk(const float* logits, const float* bias, int H, int S, in
                         cudaStream_t st);
 
 // combine.cu
-cudaError_t launch_combine(const __nv_bfloat16* P, int dh, int S, int H, const int32_t* tok_rows,
-                           const int32_t* tok_offsets, int k_fixed, int64_t R, __nv_bfloat16* y, int64_t sy_s,
-                           int64_t sy_h, cudaStream_t st);
+cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
+                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st);
+cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh, int S, int H,
+                           const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
+                           int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st);
 
 // capi.cu: text returned by mhmoe_last_error() on this host thread
 void set_last_error(const std::string& msg);

@@ -21,7 +21,7 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float* f) {
 // Quantise one bf16 row of K elements (K % 64 == 0) with a warp: amax -> g, then
 // lanes take 64-element groups (4 blocks), write 32 packed bytes + one 4-byte SF word.
 __device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, uint64_t out_row, uint8_t* data,
-                                               uint8_t* sf, float* gscale, int lane) {
+                                               uint8_t* sf, float* gscale, int lane, bool sf_rowmajor = false) {
   float amax = 0.f;
   if (src) {
     for (int i = lane; i < K / 8; i += 32) {
@@ -55,7 +55,9 @@ __device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, 
     uint4* d = reinterpret_cast<uint4*>(drow + grp * 32);
     d[0] = make_uint4(words[0], words[1], words[2], words[3]);
     d[1] = make_uint4(words[4], words[5], words[6], words[7]);
-    *reinterpret_cast<uint32_t*>(sf + sf_atom_offset(out_row, (uint32_t)(grp * 4), (uint32_t)K)) = sfw;
+    const uint64_t so = sf_rowmajor ? out_row * (uint64_t)(K / 16) + (uint64_t)grp * 4
+                                    : sf_atom_offset(out_row, (uint32_t)(grp * 4), (uint32_t)K);
+    *reinterpret_cast<uint32_t*>(sf + so) = sfw;
   }
 }
 
@@ -82,6 +84,18 @@ __global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t
     }
   }
   warp_quant_row(src, dh, (uint64_t)prow, a_data, a_sf, a_gscale, lane);
+}
+
+// Per-token quantisation for the gathered gate/up GEMM: row t = s * H + h of x
+// [S, H, dh]; scales row-major [T, dh/16] so a stage's 16 bytes of a row are contiguous.
+__global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
+                                    int dh, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf,
+                                    float* __restrict__ xg) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= (int64_t)S * H) return;
+  const int64_t s = t / H, h = t % H;
+  warp_quant_row(x + s * sx_s + h * sx_h, dh, (uint64_t)t, xq, xsf, xg, lane, true);
 }
 
 __global__ void quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t pitch, int64_t M, int K,
@@ -161,6 +175,13 @@ cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx
   quant_gather_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(x, sx_s, sx_h, S, dh, E_per_head, gather_ids, cu_tiles,
                                                             HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
                                                             a_gscale, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
+                                uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st) {
+  const int64_t T = (int64_t)S * H;
+  quant_tokens_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, xq, xsf, xg);
   return cudaGetLastError();
 }
 

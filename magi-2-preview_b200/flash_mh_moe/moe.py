@@ -82,12 +82,15 @@ class CoreMultiHeadMoE(nn.Module):
         self._packed_key: tuple | None = None
         self._router_planes: tuple | None = None
         self._router_key: tuple | None = None
+        self._masters_released = False
 
     # ── NVFP4 weights (quantise on load) ──
     def _weights_key(self):
         return tuple((p.data_ptr(), p._version) for p in (self.W_gate, self.W_up, self.W_down))
 
     def packed_weights(self) -> tuple[NVFP4GateUp, NVFP4Down]:
+        if self._masters_released:
+            return self._packed
         key = self._weights_key()
         if self._packed is None or self._packed_key != key:
             with torch.no_grad():
@@ -95,10 +98,24 @@ class CoreMultiHeadMoE(nn.Module):
             self._packed_key = key
         return self._packed
 
+    def release_master_weights(self) -> None:
+        """Pack (if needed), then free the params_dtype expert weights: inference only needs
+        the NVFP4 operands (0.56 B/weight instead of 2).  The parameters stay registered
+        with zero elements; load a state dict again to restore them."""
+        self.packed_weights()
+        with torch.no_grad():
+            for p in (self.W_gate, self.W_up, self.W_down):
+                p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+        self._masters_released = True
+
     def load_packed(self, gu: NVFP4GateUp, dn: NVFP4Down) -> None:
         """Install pre-packed NVFP4 operands (e.g. produced offline); skips packing."""
         self._packed = (gu, dn)
         self._packed_key = self._weights_key()
+
+    def _load_from_state_dict(self, *args, **kwargs):
+        super()._load_from_state_dict(*args, **kwargs)
+        self._masters_released = False       # new masters: pack again at first use
 
     def router_planes(self) -> tuple[torch.Tensor, int]:
         key = (self.gate.data_ptr(), self.gate._version)
