@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), GATHER ? 2 : 1);
+      mbar_init(smem_u32(&full_bar[s]), GATHER ? 33 : 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     mbar_init(smem_u32(tfull_bar), 1);
@@ -157,35 +157,45 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
 
   if (warp == 0) {
-    // ───────── producer ─────────
+    // ───────── producer (whole warp; lane 0 issues the TMA / bulk copies) ─────────
     int stage = 0;
     uint32_t phase = 0;
     const size_t k_atoms = (size_t)(p.K / 64);
     const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
+    // gather mode: quantised token rows of this lane's tile rows 4*lane + j, for the current
+    // tile and (prefetched one tile ahead) the next one
+    int trow[4] = {0, 0, 0, 0}, trow_next[4] = {0, 0, 0, 0};
+    auto tile_token_rows = [&](int t, int* out) {
+      const int mt = t / n_ntiles;
+      const int e = p.tile_expert[mt];
+      const int nrows = p.tile_rows[mt], row0 = p.tile_row0[mt];
+      const int h = e / p.E_per_head;
+      int fallback = p.gather_ids[row0] * p.H + h;            // padding rows re-read a real row
+      if (fallback < 0 || fallback >= p.T) fallback = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int m = 4 * lane + j;
+        int r = fallback;
+        if (m < nrows) {
+          const int s = p.gather_ids[row0 + m];
+          r = s * p.H + h;
+          if (s < 0 || r >= p.T) {            // out-of-range token id: never dereference it
+            record_error(p.status, MHMOE_ERR_ARGS);
+            r = fallback;
+          }
+        }
+        out[j] = r;
+      }
+    };
+    if constexpr (GATHER) {
+      if (blockIdx.x < total) tile_token_rows(blockIdx.x, trow);
+    }
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
       const int e = p.tile_expert[mt];
       const int brow = e * p.N + nt * GEMM_BN;
-      int trow[4] = {0, 0, 0, 0};   // gather mode: quantised token row of tile rows 4*lane + j
       if constexpr (GATHER) {
-        const int nrows = p.tile_rows[mt], row0 = p.tile_row0[mt];
-        const int h = e / p.E_per_head;
-        int fallback = p.gather_ids[row0] * p.H + h;            // padding rows re-read a real row
-        if (fallback < 0 || fallback >= p.T) fallback = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = 4 * lane + j;
-          int r = fallback;
-          if (m < nrows) {
-            const int s = p.gather_ids[row0 + m];
-            r = s * p.H + h;
-            if (s < 0 || r >= p.T) {            // out-of-range token id: never dereference it
-              record_error(p.status, MHMOE_ERR_ARGS);
-              r = fallback;
-            }
-          }
-          trow[j] = r;
-        }
+        if (t + (int)gridDim.x < total) tile_token_rows(t + gridDim.x, trow_next);
       }
       for (int kb = 0; kb < n_kblk; ++kb) {
         int ok = 1;
@@ -212,37 +222,40 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           __syncwarp();
           tma_gather4(smem_u32(sA + stage * GEMM_A_BYTES + lane * 512), &tmA, fb, kb * (GEMM_BK / 2), trow[0],
                       trow[1], trow[2], trow[3]);
-          // this stage's 16 scale bytes of each of the lane's rows -> 4 atoms x 4 bytes
-          uint8_t* sfa_s = sSFA + stage * GEMM_SFA_BYTES;
+          // this stage's 16 scale bytes of each of the lane's rows -> 4 atoms x 4 bytes,
+          // copied asynchronously; the lane's noinc arrive fires once they have landed
+          const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int m = 4 * lane + j;
-            const uint4 v = *reinterpret_cast<const uint4*>(p.xsf + (size_t)trow[j] * (size_t)(p.K / 16) + kb * 16);
+            const uint8_t* src = p.xsf + (size_t)trow[j] * (size_t)(p.K / 16) + kb * 16;
             const uint32_t off = (uint32_t)((m & 31) * 16 + (m >> 5) * 4);
-            *reinterpret_cast<uint32_t*>(sfa_s + 0 * 512 + off) = v.x;
-            *reinterpret_cast<uint32_t*>(sfa_s + 1 * 512 + off) = v.y;
-            *reinterpret_cast<uint32_t*>(sfa_s + 2 * 512 + off) = v.z;
-            *reinterpret_cast<uint32_t*>(sfa_s + 3 * 512 + off) = v.w;
+#pragma unroll
+            for (int a = 0; a < 4; ++a) cp_async_4(sfa_s + a * 512 + off, src + 4 * a);
           }
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(fb);
+          cp_async_arrive_noinc(fb);
         }
+        __syncwarp();
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if constexpr (GATHER) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) trow[j] = trow_next[j];
       }
     }
   } else if (warp == 1) {
-    // ───────── MMA issuer ─────────
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      constexpr uint32_t idesc = idesc_nvf4(GEMM_BM, GEMM_BN);
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+    // ───────── MMA issuer (whole warp waits; lane 0 issues) ─────────
+    int stage = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    constexpr uint32_t idesc = idesc_nvf4(GEMM_BM, GEMM_BN);
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+      tc_fence_after();
+      for (int kb = 0; kb < n_kblk; ++kb) {
+        if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
         tc_fence_after();
-        for (int kb = 0; kb < n_kblk; ++kb) {
-          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
-          tc_fence_after();
+        if (lane == 0) {
+          if constexpr (GATHER) fence_proxy_async_shared();   // scale bytes arrived through cp.async
           const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
           const uint32_t tsfb = tsfa + 16;
           const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
@@ -261,11 +274,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                      tsfa + j * 4, tsfb + j * 8, (kb | j) != 0 ? 1u : 0u);
           }
           tc_commit(smem_u32(&empty_bar[stage]));
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        tc_commit(smem_u32(tfull_bar));
-        acc_phase ^= 1;
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
+      if (lane == 0) tc_commit(smem_u32(tfull_bar));
+      __syncwarp();
+      acc_phase ^= 1;
     }
   } else {
     // ───────── epilogue warps 2..9 ─────────

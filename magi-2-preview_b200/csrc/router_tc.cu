@@ -111,33 +111,36 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
   const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const int h = t / mtiles, mt = t % mtiles;
-        for (int k = 0; k < nk; ++k) {
-          const int kb = k / p.nsplit, sp = k % p.nsplit;
-          if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+    // producer: the whole warp loops and waits, lane 0 issues
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const int h = t / mtiles, mt = t % mtiles;
+      for (int k = 0; k < nk; ++k) {
+        const int kb = k / p.nsplit, sp = k % p.nsplit;
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        if (lane == 0) {
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, (uint32_t)(a_bytes + b_bytes));
           tma_load_2d(smem_u32(sA + stage * a_bytes), &tmX, fb, h * p.dh + kb * RT_BK, mt * RT_BM);
           tma_load_2d(smem_u32(sB + stage * b_bytes), &tmG, fb, (kb * p.nsplit + sp) * RT_BK, h * p.E);
-          if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
         }
+        __syncwarp();
+        if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      const uint32_t idesc = idesc_bf16(RT_BM, p.Npad);
-      for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+    // MMA issuer: the whole warp loops and waits, lane 0 issues
+    int stage = 0;
+    uint32_t phase = 0, acc_phase = 0;
+    const uint32_t idesc = idesc_bf16(RT_BM, p.Npad);
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+      tc_fence_after();
+      for (int k = 0; k < nk; ++k) {
+        if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
         tc_fence_after();
-        for (int k = 0; k < nk; ++k) {
-          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
-          tc_fence_after();
+        if (lane == 0) {
           const uint32_t a_s = smem_u32(sA + stage * a_bytes);
           const uint32_t b_s = smem_u32(sB + stage * b_bytes);
 #pragma unroll
@@ -145,11 +148,13 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
             mma_bf16(tmem_base, sdesc_kmajor_sw128(a_s + j * 32), sdesc_kmajor_sw128(b_s + j * 32), idesc,
                      (k | j) != 0 ? 1u : 0u);
           tc_commit(smem_u32(&empty_bar[stage]));
-          if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
         }
-        tc_commit(smem_u32(tfull_bar));
-        acc_phase ^= 1;
+        __syncwarp();
+        if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
       }
+      if (lane == 0) tc_commit(smem_u32(tfull_bar));
+      __syncwarp();
+      acc_phase ^= 1;
     }
   } else {
     const int q = warp & 3;
