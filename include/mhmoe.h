@@ -161,7 +161,48 @@ MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_strid
                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
                     void* const* stage_events, void* stream);
 
+/* The FFN above on rows that are already NVFP4 (per-row scales): xq [T, dh/2], xsf
+ * [T, dh/16] row-major scales, xg [T]; gather_ids index these T rows (H = 1).  Used by
+ * the expert-parallel receiver, whose rows arrive quantised.  y: [T, dh] bf16 rows with
+ * pitch y_stride (combined through tok_rows / tok_offsets / k_fixed as above). */
+MHMOE_API int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float* xg, int T, int dh, int de,
+                                        int n_experts, int64_t R, const int32_t* gather_ids,
+                                        const float* probs_sorted, const int64_t* expert_offsets,
+                                        const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale,
+                                        const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                                        const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed,
+                                        void* workspace, void* y, int64_t y_stride, int* dev_status,
+                                        uint64_t timeout_ns, void* stream);
+
 /* ───────────────────────── building blocks (tests, EP) ───────────────────────── */
+
+/* Per-token NVFP4 of x [S, H, dh] (bf16): row t = s*H + h of xq [T, dh/2], xsf [T, dh/16]
+ * (row-major scales), xg [T] = amax(row)/2688.  dh % 256 == 0. */
+MHMOE_API int mhmoe_quant_tokens(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh,
+                                 uint8_t* xq, uint8_t* xsf, float* xg, void* stream);
+
+/* Deterministic combine: y[s,h,:] = bf16(sum, in ascending row id, of P[map(r), :] over
+ * the rows r of key h*S + s), rows from tok_rows/tok_offsets (or k_fixed rows per key);
+ * map = pad_of_row when given, else identity.  Replaces the scatter of the reference
+ * FFN (triton/mh_moe_fwd.py:213-221, :229-255) and, in expert parallelism, the head
+ * un-dispatch (magi2_preview.py:3303-3327). */
+MHMOE_API int mhmoe_combine(const void* P, int64_t P_rows, const int32_t* pad_of_row, int dh, int S, int H,
+                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R, void* y,
+                            int64_t y_stride_s, int64_t y_stride_h, void* stream);
+
+/* Expert-parallel dispatch packing.  Replaces the send side of ep_dispatch
+ * (magi2_preview.py:3277-3299) for token -> expert sharding: sorted row r (grouped by
+ * destination because each rank owns a contiguous expert range of E_loc experts) gets
+ * the NVFP4 row of its token (xq/xsf/xg, T = S*H rows) and a 16-byte meta record
+ * {g, local expert id (int bits), prob, 0}. */
+MHMOE_API int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E,
+                            int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                            const int64_t* expert_offsets, uint8_t* send_xq, uint8_t* send_xsf, void* send_meta,
+                            int* dev_status, void* stream);
+
+/* Receiver side: meta records -> g [R], local expert id int64 [R], prob [R]. */
+MHMOE_API int mhmoe_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
+                              int* dev_status, void* stream);
 
 /* Per-row NVFP4 quantisation of bf16 rows x[r, 0:K] (row pitch in elements):
  * data [M, K/2], sf atoms, gscale [M] = amax(row)/2688.  K % 64 == 0. */

@@ -226,6 +226,86 @@ int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S
   return rc;
 }
 
+int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float* xg, int T, int dh, int de,
+                              int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                              const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                              const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
+                              const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed,
+                              void* workspace, void* y, int64_t y_stride, int* dev_status, uint64_t timeout_ns,
+                              void* stream) {
+  MHMOE_REQUIRE(xq && xsf && xg && y && expert_offsets && gu_data && gu_sf && gu_gscale && dn_data && dn_sf &&
+                dn_gscale);
+  MHMOE_REQUIRE(T >= 0 && n_experts > 0 && R >= 0 && dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
+  MHMOE_REQUIRE(aligned16(xq) && aligned16(xsf) && aligned16(y) && y_stride % 8 == 0);
+  MHMOE_REQUIRE(tok_rows || !tok_offsets);
+  MHMOE_REQUIRE(!tok_rows || tok_offsets || k_fixed > 0);
+  MHMOE_CHECK_ARCH();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) return MHMOE_OK;
+  if (R == 0) {
+    const cudaError_t e = cudaMemset2DAsync(y, sizeof(__nv_bfloat16) * y_stride, 0, sizeof(__nv_bfloat16) * dh, T, st);
+    return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ffn_nvfp4_quantized (zero fill)");
+  }
+  MHMOE_REQUIRE(workspace && gather_ids && probs_sorted);
+  cudaError_t ce = cudaSuccess;
+  const int rc = ffn_nvfp4(nullptr, 0, 0, T, 1, dh, de, n_experts, R, gather_ids, probs_sorted, expert_offsets,
+                           gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, tok_rows, tok_offsets, k_fixed,
+                           workspace, static_cast<__nv_bfloat16*>(y), y_stride, dh, dev_status, timeout_ns, nullptr,
+                           st, &ce, xq, xsf, xg);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4_quantized");
+  if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
+  return rc;
+}
+
+int mhmoe_quant_tokens(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, uint8_t* xq,
+                       uint8_t* xsf, float* xg, void* stream) {
+  MHMOE_REQUIRE(x && xq && xsf && xg && S >= 0 && H > 0 && dh > 0 && dh % 256 == 0);
+  MHMOE_REQUIRE(aligned16(x) && x_stride_s % 8 == 0 && x_stride_h % 8 == 0 && aligned16(xq) && aligned16(xsf));
+  MHMOE_CHECK_ARCH();
+  if (S == 0) return MHMOE_OK;
+  const cudaError_t e = launch_quant_tokens(static_cast<const __nv_bfloat16*>(x), x_stride_s, x_stride_h, S, H, dh,
+                                            xq, xsf, xg, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "quant_tokens");
+}
+
+int mhmoe_combine(const void* P, int64_t P_rows, const int32_t* pad_of_row, int dh, int S, int H,
+                  const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R, void* y,
+                  int64_t y_stride_s, int64_t y_stride_h, void* stream) {
+  MHMOE_REQUIRE(y && S >= 0 && H > 0 && dh > 0 && dh % 8 == 0 && R >= 0);
+  MHMOE_REQUIRE(tok_rows && (tok_offsets || k_fixed > 0));
+  MHMOE_REQUIRE(aligned16(y) && y_stride_s % 8 == 0 && y_stride_h % 8 == 0 && (R == 0 || (P && aligned16(P))));
+  MHMOE_CHECK_ARCH();
+  if (S == 0) return MHMOE_OK;
+  const cudaError_t e = launch_combine(static_cast<const __nv_bfloat16*>(P), pad_of_row, dh, S, H, tok_rows,
+                                       tok_offsets, k_fixed, R, P_rows, static_cast<__nv_bfloat16*>(y), y_stride_s,
+                                       y_stride_h, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "combine");
+}
+
+int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E, int E_loc,
+                  int64_t R, const int32_t* gather_ids, const float* probs_sorted, const int64_t* expert_offsets,
+                  uint8_t* send_xq, uint8_t* send_xsf, void* send_meta, int* dev_status, void* stream) {
+  MHMOE_REQUIRE(xq && xsf && xg && gather_ids && probs_sorted && expert_offsets && send_xq && send_xsf && send_meta);
+  MHMOE_REQUIRE(T >= 0 && dh % 256 == 0 && H > 0 && E > 0 && E_loc > 0 && (H * E) % E_loc == 0 && R >= 0);
+  MHMOE_REQUIRE(aligned16(xq) && aligned16(xsf) && aligned16(send_xq) && aligned16(send_xsf) && aligned16(send_meta));
+  MHMOE_CHECK_ARCH();
+  if (R == 0) return MHMOE_OK;
+  const cudaError_t e = launch_ep_pack(xq, xsf, xg, T, dh, H, E, E_loc, R, gather_ids, probs_sorted, expert_offsets,
+                                       H * E, send_xq, send_xsf, send_meta, dev_status,
+                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_pack");
+}
+
+int mhmoe_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
+                    int* dev_status, void* stream) {
+  MHMOE_REQUIRE(meta && g && local_expert && prob && R >= 0 && E_loc > 0);
+  MHMOE_CHECK_ARCH();
+  if (R == 0) return MHMOE_OK;
+  const cudaError_t e =
+      launch_ep_unpack(meta, R, E_loc, g, local_expert, prob, dev_status, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_unpack");
+}
+
 int mhmoe_quantize_rows_nvfp4(const void* x, int64_t row_pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
                               float* gscale, void* stream) {
   MHMOE_REQUIRE(x && data && sf && gscale);

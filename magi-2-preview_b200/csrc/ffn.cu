@@ -85,6 +85,9 @@ struct FfnWorkspace {
   uint8_t* xq;           // [T, dh/2]  per-token quantised x (T = S*H rows, row = s*H + h)
   uint8_t* xsf;          // [T, dh/16] row-major scales
   float* xg;             // [T]
+  uint8_t* a_data;       // [rows_pad, dh/2] grouped A operand of the gate/up GEMM
+  uint8_t* a_sf;         // SF atoms of a_data
+  float* a_gscale;       // [rows_pad]
   uint8_t* h_data;       // [rows_pad, de/2] quantised SwiGLU hidden
   uint8_t* h_sf;         // SF atoms of the hidden
   __nv_bfloat16* P;      // [rows_pad, dh] bf16(y_acc * prob) per padded row
@@ -114,6 +117,9 @@ static FfnWorkspace carve(uint8_t* base, int64_t R, int64_t T, int dh, int de, i
   w.xq = take((size_t)T * dh / 2);
   w.xsf = take((size_t)T * dh / 16);
   w.xg = reinterpret_cast<float*>(take(sizeof(float) * T));
+  w.a_data = take((size_t)rows * dh / 2);
+  w.a_sf = take((size_t)rows * dh / 16);
+  w.a_gscale = reinterpret_cast<float*>(take(sizeof(float) * rows));
   w.h_data = take((size_t)rows * de / 2);
   w.h_sf = take((size_t)rows * de / 16);
   w.P = reinterpret_cast<__nv_bfloat16*>(take(sizeof(__nv_bfloat16) * (size_t)rows * dh));
@@ -133,9 +139,14 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
-              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr) {
+              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
+              const uint8_t* xq_in, const uint8_t* xsf_in, const float* xg_in) {
   const int64_t T = (int64_t)S * H;
   FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
+  const bool prequant = xq_in != nullptr;
+  const uint8_t* xq = prequant ? xq_in : w.xq;
+  const uint8_t* xsf = prequant ? xsf_in : w.xsf;
+  const float* xg = prequant ? xg_in : w.xg;
   const int64_t max_mt = mtiles_upper_bound(R, HE);
   const int64_t rows = max_mt * 128;
   cudaError_t e;
@@ -155,10 +166,12 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
                                status, st));
   MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
-  MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
+  if (!prequant) MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
+  MHMOE_TRY(launch_group_rows(xq, xsf, xg, T, dh, H, HE / H, gather_ids, w.cu_tiles, HE, max_mt, w.tile_expert,
+                              w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale, status, st));
 
   CUtensorMap ta1, tb1, ta2, tb2, tc2;
-  if (encode_tmap_2d_u8(&ta1, w.xq, dh / 2, (uint64_t)T, 128, 1) != cudaSuccess ||
+  if (encode_tmap_2d_u8(&ta1, w.a_data, dh / 2, rows, 128, 128) != cudaSuccess ||
       encode_tmap_2d_u8(&tb1, gu_data, dh / 2, (uint64_t)HE * 2 * de, 128, 256) != cudaSuccess ||
       encode_tmap_2d_u8(&ta2, w.h_data, de / 2, rows, 128, 128) != cudaSuccess ||
       encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess ||
@@ -168,6 +181,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
 
   mark(1);
   FfnGemmParams p1{};
+  p1.sfa = w.a_sf;
   p1.sfb = gu_sf;
   p1.n_mtiles_dev = w.cu_tiles + HE;
   p1.n_mtiles_host = (int)max_mt;
@@ -176,12 +190,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p1.tile_rows = w.tile_rows;
   p1.K = dh;
   p1.N = 2 * de;
-  p1.gather_ids = gather_ids;
-  p1.xsf = w.xsf;
-  p1.xg = w.xg;
-  p1.H = H;
-  p1.E_per_head = HE / H;
-  p1.T = (int)T;
+  p1.row_gscale = w.a_gscale;
   p1.gs_gate = gu_gscale;
   p1.gs_up = gu_gscale + HE;
   p1.h_data = w.h_data;

@@ -7,13 +7,10 @@
 //   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
 //
 // Warp roles (320 threads):
-//   warp 0      producer into a shared-memory stage ring (one stage = 256 K-elements):
-//               B tile (256 x 256 FP4 = 32 KB, TMA, 128-B swizzle) and its UE4M3 scale
-//               atoms (4 KB, untiled bulk copies);
-//               A tile (128 x 256 FP4 = 16 KB): for EPI_SWIGLU gathered straight from the
-//               per-token quantised x with TMA tile::gather4 (each lane fetches its 4 rows)
-//               while the lanes place the rows' scale bytes into the atom layout; for the
-//               other epilogues a tiled TMA load of an already grouped operand.
+//   warp 0      TMA producer into a 4-stage (EPI_DOWN: 3-stage) shared-memory ring, one
+//               stage = 256 K-elements: A tile (128 x 256 FP4 = 16 KB) and B tile
+//               (256 x 256 FP4 = 32 KB), 128-B swizzle, plus their UE4M3 scale atoms
+//               (2 KB + 4 KB, untiled bulk copies).  The whole warp waits; lane 0 issues.
 //   warp 1      TMEM owner + MMA issuer: per stage copies the scale atoms into TMEM
 //               (tcgen05.cp 32x128b.warpx4) and issues 4 x tcgen05.mma
 //               kind::mxf4nvf4 block16 (M128 N256 K64).
@@ -49,7 +46,6 @@ constexpr int GEMM_SFA_BYTES = GEMM_BM * GEMM_BK / 16;       // 2048
 constexpr int GEMM_SFB_BYTES = GEMM_BN * GEMM_BK / 16;       // 4096
 constexpr int GEMM_STAGE_TX = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFA_BYTES + GEMM_SFB_BYTES;
 constexpr int GEMM_STAGE_BYTES = GEMM_STAGE_TX;
-constexpr int GEMM_STAGE_TMA = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFB_BYTES;   // gather mode: SFA by threads
 constexpr int GEMM_STG_BYTES = 8 * 32 * 128;                 // EPI_DOWN: 4 KB store staging per epilogue warp
 constexpr int GEMM_TMEM_COLS = 512;
 constexpr int GEMM_SF_COL0 = 256;
@@ -73,13 +69,8 @@ struct FfnGemmParams {
   const int* tile_rows;      // [m-tile] -> valid rows in the tile
   int K;                     // reduction length in elements
   int N;                     // B rows per expert
-  // EPI_SWIGLU (A gathered from the per-token quantised x)
-  const int32_t* gather_ids; // [R] token of each sorted row
-  const uint8_t* xsf;        // [T, K/16] row-major UE4M3 scales of the quantised tokens
-  const float* xg;           // [T] second-level scale of each quantised token row
-  int H;                     // heads: token row = gather_id * H + head
-  int E_per_head;
-  int T;                     // quantised token rows (S * H)
+  // EPI_SWIGLU
+  const float* row_gscale;   // [128 * n_mtiles] second-level scale of each A row
   const float* gs_gate;      // [n_experts]
   const float* gs_up;        // [n_experts]
   uint8_t* h_data;           // [128 * n_mtiles, N/4]  (hidden has N/2 columns, 2 per byte)
@@ -100,8 +91,7 @@ __device__ __forceinline__ float swiglu7(float g, float u) {
   return g * sig * (u + 1.0f);
 }
 
-// tmA: EPI_SWIGLU -> quantised tokens [T, K/2] with a 128 x 1 box (gather4);
-//      otherwise  -> grouped A operand [128 * n_mtiles, K/2], box 128 x 128.
+// tmA: grouped A operand [128 * n_mtiles, K/2], box 128 x 128.
 // tmB: B operand [n_experts * N, K/2], box 128 x 256.
 // tmC: EPI_DOWN -> P [128 * n_mtiles, N] bf16, box 64 x 32 (store); unused otherwise.
 template <int EPI>
@@ -109,7 +99,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const FfnGemmParams p) {
   constexpr int STAGES = gemm_stages(EPI);
-  constexpr bool GATHER = EPI == EPI_SWIGLU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -130,7 +119,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full_bar[s]), GATHER ? 33 : 1);
+      mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     mbar_init(smem_u32(tfull_bar), 1);
@@ -157,90 +146,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
 
   if (warp == 0) {
-    // ───────── producer (whole warp; lane 0 issues the TMA / bulk copies) ─────────
+    // ───────── producer (whole warp waits; lane 0 issues the TMA / bulk copies) ─────────
     int stage = 0;
     uint32_t phase = 0;
     const size_t k_atoms = (size_t)(p.K / 64);
     const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
-    // gather mode: quantised token rows of this lane's tile rows 4*lane + j, for the current
-    // tile and (prefetched one tile ahead) the next one
-    int trow[4] = {0, 0, 0, 0}, trow_next[4] = {0, 0, 0, 0};
-    auto tile_token_rows = [&](int t, int* out) {
-      const int mt = t / n_ntiles;
-      const int e = p.tile_expert[mt];
-      const int nrows = p.tile_rows[mt], row0 = p.tile_row0[mt];
-      const int h = e / p.E_per_head;
-      int fallback = p.gather_ids[row0] * p.H + h;            // padding rows re-read a real row
-      if (fallback < 0 || fallback >= p.T) fallback = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int m = 4 * lane + j;
-        int r = fallback;
-        if (m < nrows) {
-          const int s = p.gather_ids[row0 + m];
-          r = s * p.H + h;
-          if (s < 0 || r >= p.T) {            // out-of-range token id: never dereference it
-            record_error(p.status, MHMOE_ERR_ARGS);
-            r = fallback;
-          }
-        }
-        out[j] = r;
-      }
-    };
-    if constexpr (GATHER) {
-      if (blockIdx.x < total) tile_token_rows(blockIdx.x, trow);
-    }
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
       const int e = p.tile_expert[mt];
       const int brow = e * p.N + nt * GEMM_BN;
-      if constexpr (GATHER) {
-        if (t + (int)gridDim.x < total) tile_token_rows(t + gridDim.x, trow_next);
-      }
       for (int kb = 0; kb < n_kblk; ++kb) {
-        int ok = 1;
-        if (lane == 0) ok = mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) goto done;
-        const uint32_t fb = smem_u32(&full_bar[stage]);
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
         if (lane == 0) {
-          mbar_arrive_expect_tx(fb, GATHER ? GEMM_STAGE_TMA : GEMM_STAGE_TX);
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, GEMM_STAGE_TX);
+          tma_load_2d(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
           tma_load_2d(smem_u32(sB + stage * GEMM_B_BYTES), &tmB, fb, kb * (GEMM_BK / 2), brow);
+          const uint8_t* sfa_src = p.sfa + ((size_t)mt * k_atoms + (size_t)kb * 4) * 512;
+          bulk_load(smem_u32(sSFA + stage * GEMM_SFA_BYTES), sfa_src, GEMM_SFA_BYTES, fb);
 #pragma unroll
           for (int nb = 0; nb < 2; ++nb) {
             const uint8_t* sfb_src =
                 p.sfb + (size_t)e * sfb_expert_bytes + ((size_t)(nt * 2 + nb) * k_atoms + (size_t)kb * 4) * 512;
             bulk_load(smem_u32(sSFB + stage * GEMM_SFB_BYTES + nb * 2048), sfb_src, 2048, fb);
           }
-          if constexpr (!GATHER) {
-            tma_load_2d(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
-            const uint8_t* sfa_src = p.sfa + ((size_t)mt * k_atoms + (size_t)kb * 4) * 512;
-            bulk_load(smem_u32(sSFA + stage * GEMM_SFA_BYTES), sfa_src, GEMM_SFA_BYTES, fb);
-          }
-        }
-        if constexpr (GATHER) {
-          __syncwarp();
-          tma_gather4(smem_u32(sA + stage * GEMM_A_BYTES + lane * 512), &tmA, fb, kb * (GEMM_BK / 2), trow[0],
-                      trow[1], trow[2], trow[3]);
-          // this stage's 16 scale bytes of each of the lane's rows -> 4 atoms x 4 bytes,
-          // copied asynchronously; the lane's noinc arrive fires once they have landed
-          const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int m = 4 * lane + j;
-            const uint8_t* src = p.xsf + (size_t)trow[j] * (size_t)(p.K / 16) + kb * 16;
-            const uint32_t off = (uint32_t)((m & 31) * 16 + (m >> 5) * 4);
-#pragma unroll
-            for (int a = 0; a < 4; ++a) cp_async_4(sfa_s + a * 512 + off, src + 4 * a);
-          }
-          cp_async_arrive_noinc(fb);
         }
         __syncwarp();
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
-      }
-      if constexpr (GATHER) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) trow[j] = trow_next[j];
       }
     }
   } else if (warp == 1) {
@@ -255,7 +187,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
         tc_fence_after();
         if (lane == 0) {
-          if constexpr (GATHER) fence_proxy_async_shared();   // scale bytes arrived through cp.async
           const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
           const uint32_t tsfb = tsfa + 16;
           const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
@@ -307,12 +238,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int e = p.tile_expert[mt];
       const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
       if constexpr (EPI == EPI_SWIGLU) {
-        float gr = 1.0f;
-        if (m < p.tile_rows[mt]) {
-          const int s = p.gather_ids[p.tile_row0[mt] + m];
-          const int tr = s * p.H + e / p.E_per_head;
-          if (s >= 0 && tr < p.T) gr = p.xg[tr];
-        }
+        const float gr = p.row_gscale[prow];
         const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
         const float s_up = __fmul_rn(gr, p.gs_up[e]);
         const int hid_cols = p.N / 2;

@@ -26,10 +26,10 @@ cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, con
                               void* ws, int32_t* tok_offsets, int32_t* tok_rows, int* status, cudaStream_t st);
 
 // quant.cu
-cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int dh, int E_per_head,
-                                const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
-                                const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
-                                uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
+cudaError_t launch_group_rows(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H,
+                              int E_per_head, const int32_t* gather_ids, const int* cu_tiles, int HE,
+                              int64_t max_mtiles, const int* tile_expert, const int* tile_row0, const int* tile_rows,
+                              uint8_t* a_data, uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
 cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
                                 uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st);
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
@@ -62,7 +62,16 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
-              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr);
+              uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
+              const uint8_t* xq_in = nullptr, const uint8_t* xsf_in = nullptr, const float* xg_in = nullptr);
+
+// ep.cu
+cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E,
+                           int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                           const int64_t* expert_offsets, int HE, uint8_t* send_xq, uint8_t* send_xsf,
+                           void* send_meta, int* status, cudaStream_t st);
+cudaError_t launch_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
+                             int* status, cudaStream_t st);
 int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
                    const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out, int* status,
                    uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);

@@ -117,17 +117,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// TMA gather of four rows (box one row high, 128 B wide): rows r0..r3 at column c0 land
-// as four consecutive 128-B rows at dst (the 128-B swizzle follows the smem address).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0, int32_t r0,
-                                            int32_t r1, int32_t r2, int32_t r3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes "
-      "[%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"(tmap), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-      : "memory");
-}
-
 // 2-D tiled TMA store shared -> global, tracked by the issuing thread's bulk group.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t c0, int32_t c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
@@ -141,16 +130,6 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 }
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// 4-byte asynchronous copy global -> shared (tracked by cp.async groups / mbarrier).
-__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-}
-// Arrive on `bar` once this thread's prior cp.async copies have landed; the arrival counts
-// toward the barrier's expected count (.noinc).
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
 
 // Untiled bulk copy global -> shared; both addresses 16-B aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

@@ -61,33 +61,43 @@ __device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, 
   }
 }
 
-// One warp per padded row of the expert-grouped row space; padding rows are zeroed.
-__global__ void quant_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int dh,
-                                    int E_per_head, const int32_t* __restrict__ gather_ids,
-                                    const int* __restrict__ cu_tiles, int HE, const int* __restrict__ tile_expert,
-                                    const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
-                                    uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf,
-                                    float* __restrict__ a_gscale, int* __restrict__ status) {
+// Grouped A operand of the gate/up GEMM: one warp per padded row of the expert-grouped
+// row space copies its token's NVFP4 row (per-token quantised x: data, row-major scales,
+// row scale) into place, scales into the SF-atom layout.  Padding rows are zeroed.
+__global__ void group_rows_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf,
+                                  const float* __restrict__ xg, int64_t T, int dh, int H, int E_per_head,
+                                  const int32_t* __restrict__ gather_ids, const int* __restrict__ cu_tiles, int HE,
+                                  const int* __restrict__ tile_expert, const int* __restrict__ tile_row0,
+                                  const int* __restrict__ tile_rows, uint8_t* __restrict__ a_data,
+                                  uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
+                                  int* __restrict__ status) {
   const int lane = threadIdx.x & 31;
   const int64_t prow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int mt = (int)(prow >> 7);
   if (mt >= cu_tiles[HE]) return;
   const int m = (int)(prow & 127);
-  const __nv_bfloat16* src = nullptr;
+  int64_t t = -1;
   if (m < tile_rows[mt]) {
-    const int e = tile_expert[mt];
     const int s = gather_ids[tile_row0[mt] + m];
-    if (s >= 0 && s < S) {
-      src = x + (int64_t)s * sx_s + (int64_t)(e / E_per_head) * sx_h;
-    } else if (lane == 0) {
-      record_error(status, MHMOE_ERR_ARGS);
+    t = (int64_t)s * H + tile_expert[mt] / E_per_head;
+    if (s < 0 || t >= T) {
+      if (lane == 0) record_error(status, MHMOE_ERR_ARGS);
+      t = -1;
     }
   }
-  warp_quant_row(src, dh, (uint64_t)prow, a_data, a_sf, a_gscale, lane);
+  uint4* dst = reinterpret_cast<uint4*>(a_data + prow * (dh / 2));
+  const uint4* src = t >= 0 ? reinterpret_cast<const uint4*>(xq + t * (dh / 2)) : nullptr;
+  for (int i = lane; i < dh / 32; i += 32) dst[i] = src ? src[i] : make_uint4(0, 0, 0, 0);
+  const uint32_t* ssrc = t >= 0 ? reinterpret_cast<const uint32_t*>(xsf + t * (dh / 16)) : nullptr;
+  for (int w = lane; w < dh / 64; w += 32) {
+    const uint32_t v = ssrc ? ssrc[w] : 0u;
+    *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)(4 * w), (uint32_t)dh)) = v;
+  }
+  if (lane == 0) a_gscale[prow] = t >= 0 ? xg[t] : 1.0f;
 }
 
-// Per-token quantisation for the gathered gate/up GEMM: row t = s * H + h of x
-// [S, H, dh]; scales row-major [T, dh/16] so a stage's 16 bytes of a row are contiguous.
+// Per-token quantisation: row t = s * H + h of x [S, H, dh]; scales row-major [T, dh/16].
+// Each token is quantised once, however many experts it is routed to.
 __global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
                                     int dh, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf,
                                     float* __restrict__ xg) {
@@ -167,14 +177,14 @@ __global__ void pack_tile_kernel(const __nv_bfloat16* __restrict__ w, int Kdim, 
 
 // ───────────────────────────── launchers ─────────────────────────────
 
-cudaError_t launch_quant_gather(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int dh, int E_per_head,
-                                const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
-                                const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
-                                uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
+cudaError_t launch_group_rows(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H,
+                              int E_per_head, const int32_t* gather_ids, const int* cu_tiles, int HE,
+                              int64_t max_mtiles, const int* tile_expert, const int* tile_row0, const int* tile_rows,
+                              uint8_t* a_data, uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
   const int64_t rows = max_mtiles * 128;
-  quant_gather_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(x, sx_s, sx_h, S, dh, E_per_head, gather_ids, cu_tiles,
-                                                            HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
-                                                            a_gscale, status);
+  group_rows_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(xq, xsf, xg, T, dh, H, E_per_head, gather_ids, cu_tiles,
+                                                          HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
+                                                          a_gscale, status);
   return cudaGetLastError();
 }
 

@@ -162,3 +162,47 @@ def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def nvfp4_expert_rows_ref(codes, sf, g, expert, prob, gu_pack: dict, down_pack: dict) -> np.ndarray:
+    """Per-row NVFP4 expert FFN on already-quantised rows (the expert-parallel receiver's
+    work): codes [R, dh] E2M1 codes, sf [R, dh/16] E4M3 bytes, g [R] row scales, expert
+    [R] index into the packs, prob [R].  Returns bf16-valued fp32 rows [R, dh] =
+    bf16(down(swiglu7(gate/up)) * prob) — the rows ``mh_moe_fwd_nvfp4_ref`` combines."""
+    codes = np.asarray(codes, np.uint8)
+    R, dh = codes.shape
+    de = gu_pack["de"]
+    out = np.zeros((R, dh), np.float32)
+    x_deq = nv.dequantize(codes, sf)
+    is_up = ((np.arange(2 * de) // 16) % 2).astype(bool)
+    gu_codes = nv.unpack_codes(gu_pack["data"])
+    dn_codes = nv.unpack_codes(down_pack["data"])
+    expert = np.asarray(expert, np.int64)
+    for e in np.unique(expert):
+        rows = np.nonzero(expert == e)[0]
+        b = nv.dequantize(gu_codes[e], nv.atoms_to_sf(gu_pack["sf_atoms"][e], 2 * de, dh)).astype(np.float64)
+        acc = (x_deq[rows].astype(np.float64) @ b.T).astype(np.float32)
+        s_gate = (np.asarray(g, np.float32)[rows] * gu_pack["gscale_gate"][e]).astype(np.float32)
+        s_up = (np.asarray(g, np.float32)[rows] * gu_pack["gscale_up"][e]).astype(np.float32)
+        scale = np.where(is_up[None, :], s_up[:, None], s_gate[:, None]).astype(np.float32)
+        v = (acc * scale).astype(np.float32).reshape(-1, de // 16, 2, 16)
+        hid = swiglu7(v[:, :, 0, :], v[:, :, 1, :]).reshape(-1, de)
+        hc, hsf = nv.quantize_blocks(hid, nv.HIDDEN_GLOBAL)
+        ha = nv.dequantize(hc, hsf).astype(np.float64)
+        wd = nv.dequantize(dn_codes[e], nv.atoms_to_sf(down_pack["sf_atoms"][e], dh, de)).astype(np.float64)
+        acc2 = (ha @ wd.T).astype(np.float32)
+        s_dn = np.float32(nv.HIDDEN_GLOBAL * down_pack["gscale"][e])
+        out[rows] = nv.bf16_round(((acc2 * s_dn).astype(np.float32) *
+                                   np.asarray(prob, np.float32)[rows, None]).astype(np.float32))
+    return out
+
+
+def slice_packs(gu_pack: dict, down_pack: dict, lo: int, hi: int) -> tuple[dict, dict]:
+    """Expert slice [lo, hi) of packed weights (an EP rank's shard)."""
+    gu = dict(gu_pack)
+    dn = dict(down_pack)
+    for k in ("data", "sf_atoms", "gscale_gate", "gscale_up"):
+        gu[k] = gu_pack[k][lo:hi]
+    for k in ("data", "sf_atoms", "gscale"):
+        dn[k] = down_pack[k][lo:hi]
+    return gu, dn
