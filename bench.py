@@ -11,9 +11,10 @@ weight ~ N(0,0.02) bf16-valued fp32, expert weights ~ N(0,0.02) cast to bf16, th
 packed to NVFP4 at load).  Inputs are larger than L2 (0.68 GB of NVFP4 weights and
 0.1 GB of x are streamed every step), so no explicit flush is needed.
 
-Rank 0 prints one JSON line.  Under torchrun (N>1) every rank runs an independent
-replica of the config-1 layer on its own tokens (weak scaling); the expert-parallel
-layer is exercised by the multi-GPU tests.
+Rank 0 prints one JSON line.  Under torchrun (N>1) the job is BASELINE config 3: the
+expert-parallel layer with E=128 experts sharded contiguously over the N GPUs (128/N
+each), 8192 tokens per GPU (weak scaling), NVFP4 token rows dispatched to their experts
+and results returned over NCCL all-to-all (flash_mh_moe/ep.py).
 
 `--impl reference` times the reference's CPU path for the same layer (router fp32
 einsum, route.py top-k and global sort, and the bf16 FFN of mh_moe_fwd.py restated in
@@ -39,8 +40,13 @@ for p in (str(ROOT), str(PKG)):
         sys.path.insert(0, p)
 
 CFG1 = dict(name="config1", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=1, score_func="softmax")
+CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, score_func="softmax")
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
-KERNELS_PER_STEP = 10   # fused router, sort x4, tile tables, quant, gate/up GEMM, down GEMM, combine
+# libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, token quantise,
+# row grouping, gate/up GEMM, down GEMM, combine.  EP adds pack, unpack, the receiver's sort x4
+# and the source-side combine.
+KERNELS_PER_STEP = 12
+KERNELS_PER_STEP_EP = 19
 CPU_SAMPLE_TOKENS = 512
 
 
@@ -120,14 +126,28 @@ def dist_setup():
     return world, rank, local
 
 
-def make_layer(cfg, device, rank):
+def make_layer(cfg, device, rank, ep_group=None):
     import torch
     from flash_mh_moe.moe import CoreMultiHeadMoE, CoreMultiHeadMoEConfig, init_moe_params_
     mc = CoreMultiHeadMoEConfig(hidden_size=cfg["d"], num_heads=cfg["H"], num_experts=cfg["E"], top_k=cfg["K"],
                                 expert_intermediate_size=cfg["de"], num_layers=1, params_dtype=torch.bfloat16,
                                 score_func=cfg["score_func"], route_norm=True, route_scale=1.0)
-    m = CoreMultiHeadMoE(mc).to(device)
-    init_moe_params_(m, seed=cfg["seed"], device=device)
+    if ep_group is None:
+        m = CoreMultiHeadMoE(mc).to(device)
+        init_moe_params_(m, seed=cfg["seed"], device=device)
+    else:
+        # every rank draws the same full weight set, keeps its contiguous expert slice
+        full = CoreMultiHeadMoE(mc).to(device)
+        init_moe_params_(full, seed=cfg["seed"], device=device)
+        m = CoreMultiHeadMoE(mc, ep_group=ep_group).to(device)
+        lo, hi = m.expert_lo, m.expert_lo + m.local_flatten_num_experts
+        with torch.no_grad():
+            m.gate.copy_(full.gate)
+            m.W_gate.copy_(full.W_gate[lo:hi])
+            m.W_up.copy_(full.W_up[lo:hi])
+            m.W_down.copy_(full.W_down[lo:hi])
+        del full
+        torch.cuda.empty_cache()
     g = torch.Generator().manual_seed(cfg["seed"] * 1000 + rank)
     x_host = torch.randn(cfg["S"], cfg["d"], generator=g).to(torch.bfloat16)
     return m, x_host
@@ -146,13 +166,26 @@ def step_explicit(m, x, ev):
     return ffn_nvfp4(x_heads, gids, ps, offs, gu, dn, tok_rows=inv, k_fixed=m.topk, stage_events=ev[2:7])
 
 
+def step_ep(m, x, ev):
+    """The expert-parallel module forward spelled out, with events between the stages."""
+    from flash_mh_moe.ep import ep_moe_layer
+    x_heads = x.view(-1, m.num_heads, m.d_head)
+    ev[0].record()
+    probs, idx = m._route(x_heads)
+    ev[1].record()
+    gu, dn = m.packed_weights()
+    y = ep_moe_layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7])
+    ev[7].record()
+    return y
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
     from flash_mh_moe import _lib
-    cfg = CFG1
+    cfg = CFG1 if world == 1 else CFG3
     dev = torch.device("cuda", local if world > 1 else 0)
-    m, x_host = make_layer(cfg, dev, rank)
+    m, x_host = make_layer(cfg, dev, rank, ep_group=dist.group.WORLD if world > 1 else None)
     x = x_host.to(dev)
     m.packed_weights()
     if args.release_master:
@@ -160,9 +193,10 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
     torch.cuda.synchronize()
 
-    nev = 7
+    nev = 7 if world == 1 else 8
+    step = step_explicit if world == 1 else step_ep
     for _ in range(args.warmup):
-        step_explicit(m, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
+        step(m, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
     torch.cuda.synchronize()
     _lib.check_device_status(dev)
     if world > 1:
@@ -176,7 +210,7 @@ def run_ours(args, world, rank, local):
             dist.barrier()
         t0.record()
         for k in range(args.steps):
-            step_explicit(m, x, evs[k])
+            step(m, x, evs[k])
         t1.record()
         torch.cuda.synchronize()
     if world > 1:
@@ -192,8 +226,13 @@ def run_ours(args, world, rank, local):
     def avg(i, j):
         return sum(e[i].elapsed_time(e[j]) for e in evs) / len(evs)
 
-    stages = {"route_ms": avg(0, 1), "sort_ms": avg(1, 2), "quant_tables_ms": avg(2, 3),
-              "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "combine_ms": avg(5, 6)}
+    if world == 1:
+        stages = {"route_ms": avg(0, 1), "sort_ms": avg(1, 2), "quant_tables_ms": avg(2, 3),
+                  "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "combine_ms": avg(5, 6)}
+    else:
+        stages = {"route_ms": avg(0, 1), "dispatch_ms": avg(1, 2), "quant_tables_ms": avg(2, 3),
+                  "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "local_combine_ms": avg(5, 6),
+                  "return_combine_ms": avg(6, 7)}
 
     # end-to-end through the public module API, host buffers, copies inside the timed region
     e2e_ms = float("nan")
@@ -231,7 +270,12 @@ def _e2e(args, m, x_host, dev, world):
 def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
     S, d, de, K = cfg["S"], cfg["d"], cfg["de"], cfg["K"]
     R = S * K * cfg["H"]
-    flop_gate_up = 2.0 * R * (d // cfg["H"]) * (2 * de)
+    if world > 1:
+        from flash_mh_moe.ep import LAST_STATS
+        R_gemm = LAST_STATS.get("rows_received", R)     # rows this rank's expert GEMMs processed
+    else:
+        R_gemm = R
+    flop_gate_up = 2.0 * R_gemm * (d // cfg["H"]) * (2 * de)
     flop_total = 6.0 * R * (d // cfg["H"]) * de
     peaks = load_peaks()
     fp4_peak = 4.0 * peaks["bf16_tflops_sustained"]
@@ -247,9 +291,12 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
         "data": "synthetic (seeded, config-1 distributions)",
-        "config": {"workload": "config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024",
-                   "tokens_per_gpu": S, "global_batch": world * S, "parallelism":
-                       f"{world} independent replicas" if world > 1 else "1 GPU",
+        "config": {"workload": ("config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024"
+                                if world == 1 else
+                                f"config3: {S} tokens/GPU, d=3072 (H=1), E=128 sharded {cfg['E'] // world}/GPU, "
+                                "top-8 softmax, SwiGLU7 de=1024"),
+                   "tokens_per_gpu": S, "global_batch": world * S,
+                   "parallelism": f"ep{world} (token->expert all-to-all, NCCL)" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (0.68 GB NVFP4 weights + 0.1 GB x per step)"},
         "tokens_per_s_per_gpu": round(value / world, 1),
         "layer_tflops": round(layer_tflops, 1),
@@ -265,7 +312,7 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "e2e": None if e2e_ms != e2e_ms else {"value": round(world * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": S * d * 2, "d2h_bytes_per_step": S * d * 2,
                 "ms_per_step": round(e2e_ms, 4), "api": "CoreMultiHeadMoE.forward (custom op magi2_b200::mh_moe)"},
-        "gpu_launches": KERNELS_PER_STEP * args.steps,   # kernels of libmhmoe inside the device-timed region
+        "gpu_launches": (KERNELS_PER_STEP if world == 1 else KERNELS_PER_STEP_EP) * args.steps,   # kernels of libmhmoe inside the device-timed region
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline and not args.release_master:

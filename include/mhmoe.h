@@ -164,7 +164,8 @@ MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_strid
 /* The FFN above on rows that are already NVFP4 (per-row scales): xq [T, dh/2], xsf
  * [T, dh/16] row-major scales, xg [T]; gather_ids index these T rows (H = 1).  Used by
  * the expert-parallel receiver, whose rows arrive quantised.  y: [T, dh] bf16 rows with
- * pitch y_stride (combined through tok_rows / tok_offsets / k_fixed as above). */
+ * pitch y_stride (combined through tok_rows / tok_offsets / k_fixed as above).
+ * stage_events: as for mhmoe_ffn_nvfp4 (optional). */
 MHMOE_API int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float* xg, int T, int dh, int de,
                                         int n_experts, int64_t R, const int32_t* gather_ids,
                                         const float* probs_sorted, const int64_t* expert_offsets,
@@ -172,7 +173,7 @@ MHMOE_API int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, c
                                         const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
                                         const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed,
                                         void* workspace, void* y, int64_t y_stride, int* dev_status,
-                                        uint64_t timeout_ns, void* stream);
+                                        uint64_t timeout_ns, void* const* stage_events, void* stream);
 
 /* ───────────────────────── building blocks (tests, EP) ───────────────────────── */
 

@@ -232,7 +232,7 @@ int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float
                               const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
                               const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed,
                               void* workspace, void* y, int64_t y_stride, int* dev_status, uint64_t timeout_ns,
-                              void* stream) {
+                              void* const* stage_events, void* stream) {
   MHMOE_REQUIRE(xq && xsf && xg && y && expert_offsets && gu_data && gu_sf && gu_gscale && dn_data && dn_sf &&
                 dn_gscale);
   MHMOE_REQUIRE(T >= 0 && n_experts > 0 && R >= 0 && dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
@@ -250,8 +250,8 @@ int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float
   cudaError_t ce = cudaSuccess;
   const int rc = ffn_nvfp4(nullptr, 0, 0, T, 1, dh, de, n_experts, R, gather_ids, probs_sorted, expert_offsets,
                            gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, tok_rows, tok_offsets, k_fixed,
-                           workspace, static_cast<__nv_bfloat16*>(y), y_stride, dh, dev_status, timeout_ns, nullptr,
-                           st, &ce, xq, xsf, xg);
+                           workspace, static_cast<__nv_bfloat16*>(y), y_stride, dh, dev_status, timeout_ns,
+                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce, xq, xsf, xg);
   if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4_quantized");
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
   return rc;

@@ -24,7 +24,8 @@ namespace mhmoe {
 
 constexpr int RT_BM = 128;
 constexpr int RT_BK = 64;                // bf16 elements per stage row (128 B)
-constexpr int RT_STAGES = 4;
+constexpr int RT_MAX_STAGES = 4;
+constexpr int RT_SCRATCH_BYTES = 2 * 32 * 128 * 4;
 constexpr int RT_THREADS = 192;
 constexpr int RT_MAXK = 16;
 
@@ -33,7 +34,7 @@ struct RouterParams {
   float* probs;            // [H, S, K]
   int64_t* idx;            // [H, S, K]
   float* logits;           // [H, S, E] or null
-  int S, H, dh, E, Npad, K, nsplit, score_func, route_norm;
+  int S, H, dh, E, Npad, K, nsplit, score_func, route_norm, stages;
   float norm_eps, route_scale;
   int* status;
   uint64_t timeout_ns;
@@ -72,19 +73,21 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
   const int a_bytes = RT_BM * RT_BK * 2;
   const int b_bytes = p.Npad * RT_BK * 2;
   uint8_t* sA = smem;
-  uint8_t* sB = sA + RT_STAGES * a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + RT_STAGES * b_bytes);
+  const int STAGES = p.stages;
+  uint8_t* sB = sA + STAGES * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * b_bytes);
   uint64_t* full_bar = bars;
-  uint64_t* empty_bar = bars + RT_STAGES;
-  uint64_t* tfull_bar = bars + 2 * RT_STAGES;
+  uint64_t* empty_bar = bars + RT_MAX_STAGES;
+  uint64_t* tfull_bar = bars + 2 * RT_MAX_STAGES;
   uint64_t* tempty_bar = tfull_bar + 1;
   uint64_t* drain_bar = tfull_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  float* scratch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // 2 x [32][128] fp32
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tcols = p.Npad <= 32 ? 32 : p.Npad <= 64 ? 64 : p.Npad <= 128 ? 128 : 256;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < RT_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
@@ -126,7 +129,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           tma_load_2d(smem_u32(sB + stage * b_bytes), &tmG, fb, (kb * p.nsplit + sp) * RT_BK, h * p.E);
         }
         __syncwarp();
-        if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
   } else if (warp == 1) {
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           tc_commit(smem_u32(&empty_bar[stage]));
         }
         __syncwarp();
-        if (++stage == RT_STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       if (lane == 0) tc_commit(smem_u32(tfull_bar));
       __syncwarp();
@@ -204,18 +207,32 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         ts[j] = 0.f;
         ti[j] = 0;
       }
+      // pass 3: scores of a 32-column chunk go to this thread's column of the shared
+      // scratch (unrolled, cheap), then only candidates above the running k-th value are
+      // inserted, through one non-unrolled loop (keeps the code small).
+      float* sv = scratch + (threadIdx.x - 64);          // [32][128] selection values
+      float* ss = sv + 32 * 128;                          // [32][128] unbiased scores
       for (int c = 0; c < nchunk; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
+        uint32_t cand = 0;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int e = c * 32 + i;
+          float v = -INFINITY, sc = 0.f;
           if (e < p.E) {
             const float l = __uint_as_float(r[i]);
-            const float sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
-            const float v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
-            topk_insert(v, e, sc, tv, ti, ts, p.K, thr);
+            sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
+            v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
           }
+          sv[i * 128] = v;
+          ss[i * 128] = sc;
+          cand |= (v > thr ? 1u : 0u) << i;
+        }
+        while (cand) {
+          const int i = __ffs(cand) - 1;
+          cand &= cand - 1;
+          topk_insert(sv[i * 128], c * 32 + i, ss[i * 128], tv, ti, ts, p.K, thr);
         }
       }
       tc_fence_before();
@@ -320,12 +337,14 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   p.norm_eps = norm_eps;
   p.route_scale = route_scale;
   p.status = status;
-  const int smem = RT_STAGES * (RT_BM * RT_BK * 2 + Npad * RT_BK * 2) + 256 + 1024;
+  const int stage_bytes = RT_BM * RT_BK * 2 + Npad * RT_BK * 2;
+  const int fixed = 256 + RT_SCRATCH_BYTES + 1024;
+  p.stages = std::min(RT_MAX_STAGES, (227 * 1024 - fixed) / stage_bytes);
+  const int smem = p.stages * stage_bytes + fixed;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                RT_STAGES * (RT_BM * RT_BK * 2 + 256 * RT_BK * 2) + 256 + 1024);
+    attr = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (attr != cudaSuccess) {
     *cerr = attr;

@@ -40,7 +40,7 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_ffn_nvfp4": (i32, [vp, i64, i64, i32, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                               vp, vp, i32, vp, vp, i64, i64, vp, u64, vp, vp]),
     "mhmoe_ffn_nvfp4_quantized": (i32, [vp, vp, vp, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                                        vp, vp, i32, vp, vp, i64, vp, u64, vp]),
+                                        vp, vp, i32, vp, vp, i64, vp, u64, vp, vp]),
     "mhmoe_quant_tokens": (i32, [vp, i64, i64, i32, i32, i32, vp, vp, vp, vp]),
     "mhmoe_combine": (i32, [vp, i64, vp, i32, i32, i32, vp, vp, i32, i64, vp, i64, i64, vp]),
     "mhmoe_ep_pack": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp]),

@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .fwd import _events
 
 
 # ───────────────────────── reference-compatible head sharding ─────────────────────────
@@ -107,7 +108,8 @@ class CudaBackend:
         from .route import flash_mh_moe_global_sort_with_inverse
         return flash_mh_moe_global_sort_with_inverse(probs, idx, num_experts)
 
-    def ffn_rows(self, xq, xsf, xg, gather_ids, probs_sorted, expert_offsets, row_of_flat, gu, dn):
+    def ffn_rows(self, xq, xsf, xg, gather_ids, probs_sorted, expert_offsets, row_of_flat, gu, dn,
+                 stage_events=None):
         """One bf16 output row per quantised input row (prob applied), in input-row order."""
         T = xq.shape[0]
         dh = xq.shape[1] * 2
@@ -123,7 +125,7 @@ class CudaBackend:
             probs_sorted.data_ptr(), expert_offsets.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(),
             gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(), dn.gscale.data_ptr(), row_of_flat.data_ptr(),
             None, 1, ws.data_ptr(), y.data_ptr(), y.stride(0), _lib.device_status(dev).data_ptr(), 0,
-            _lib.stream_ptr(dev)), "ffn_nvfp4_quantized")
+            _events(stage_events), _lib.stream_ptr(dev)), "ffn_nvfp4_quantized")
         return y
 
     def combine(self, rows, S, H, row_of_flat, K):
@@ -134,6 +136,9 @@ class CudaBackend:
                                              H, row_of_flat.data_ptr(), None, K, rows.shape[0], y.data_ptr(),
                                              y.stride(0), y.stride(1), _lib.stream_ptr(dev)), "combine")
         return y
+
+
+LAST_STATS: dict = {}   # rows sent / received by the last ep_moe_layer call on this process
 
 
 def _a2a_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group) -> torch.Tensor:
@@ -156,7 +161,7 @@ def ep_exchange_counts(expert_offsets: torch.Tensor, ep: int, E_loc: int, group)
 
 
 def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn, group,
-                 backend=None) -> torch.Tensor:
+                 backend=None, stage_events=None) -> torch.Tensor:
     """Token -> expert EP forward of the routed FFN for this rank's tokens.
 
     x_heads [S, H, dh]; probs/idx [H, S, K] from this rank's router (global per-head
@@ -184,16 +189,22 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
     rmeta = _a2a_rows(meta, send_counts, recv_counts, group)
     # 4. local experts on the received rows (one output row per received row)
     Rr = rxq.shape[0]
+    LAST_STATS.update(rows_sent=int(sum(send_counts)), rows_received=int(Rr),
+                      bytes_sent=int(sum(send_counts)) * (sxq.shape[1] + sxsf.shape[1] + 16))
     rg, rexp, rprob = be.unpack(rmeta, E_loc)
     lg, lps, loffs, linv = be.sort(rprob.view(1, Rr, 1), rexp.view(1, Rr, 1), E_loc)
-    out_rows = be.ffn_rows(rxq, rxsf, rg, lg, lps, loffs, linv, gu, dn)
+    if stage_events is not None:
+        out_rows = be.ffn_rows(rxq, rxsf, rg, lg, lps, loffs, linv, gu, dn, stage_events=stage_events)
+    else:
+        out_rows = be.ffn_rows(rxq, rxsf, rg, lg, lps, loffs, linv, gu, dn)
     # 5. rows back to their sources; combine in ascending global-expert order
     back = _a2a_rows(out_rows, recv_counts, send_counts, group)
     return be.combine(back, S, H, inv, K)
 
 
-def ep_moe_forward(module, x_heads: torch.Tensor) -> torch.Tensor:
+def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None) -> torch.Tensor:
     """``CoreMultiHeadMoE`` forward with ``ep_size > 1`` (route locally, EP FFN)."""
     probs, idx = module._route(x_heads)
     gu, dn = module.packed_weights()
-    return ep_moe_layer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group)
+    return ep_moe_layer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
+                        stage_events=stage_events)
