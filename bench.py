@@ -40,7 +40,9 @@ for p in (str(ROOT), str(PKG)):
         sys.path.insert(0, p)
 
 CFG1 = dict(name="config1", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=1, score_func="softmax")
+CFG2 = dict(name="config2", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=2, score_func="softmax", zipf=True)
 CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, score_func="softmax")
+CFG4 = dict(name="config4", S=256, d=3072, H=1, E=128, K=8, de=1024, seed=4, score_func="softmax", layers=4)
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
 # libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, token quantise,
 # row grouping, gate/up GEMM, down GEMM, combine.  EP adds pack, unpack, the receiver's sort x4
@@ -156,10 +158,15 @@ def make_layer(cfg, device, rank, ep_group=None):
 def step_explicit(m, x, ev):
     """The module forward spelled out, with events between the stages (same kernels)."""
     from flash_mh_moe.fwd import ffn_nvfp4
-    from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse
+    from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse, route_fused
     x_heads = x.view(-1, m.num_heads, m.d_head)
     ev[0].record()
-    probs, idx = m._route(x_heads)
+    if getattr(m, "_logit_bias", None) is not None:
+        planes, nsplit = m.router_planes()
+        probs, idx = route_fused(x_heads, planes, nsplit, m.num_experts, m.topk, m.config.score_func,
+                                 logit_bias=m._logit_bias)
+    else:
+        probs, idx = m._route(x_heads)
     ev[1].record()
     gids, ps, offs, inv = flash_mh_moe_global_sort_with_inverse(probs, idx, m.num_experts)
     gu, dn = m.packed_weights()
@@ -183,9 +190,17 @@ def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
     from flash_mh_moe import _lib
-    cfg = CFG1 if world == 1 else CFG3
+    cfg = {1: CFG1, 2: CFG2, 4: CFG4}[args.config] if world == 1 else CFG3
+    if args.tokens:
+        cfg = dict(cfg, S=args.tokens)
     dev = torch.device("cuda", local if world > 1 else 0)
+    if cfg.get("layers", 1) > 1:
+        return run_stack(args, cfg, dev)
     m, x_host = make_layer(cfg, dev, rank, ep_group=dist.group.WORLD if world > 1 else None)
+    if cfg.get("zipf"):
+        # config 2: per-expert logit bias b_e = 2 * ln((e+1)^-1.2) -> a few crowded, many empty experts
+        e = torch.arange(cfg["E"], dtype=torch.float32, device=dev)
+        m._logit_bias = (2.0 * torch.log((e + 1.0) ** -1.2)).repeat(cfg["H"])
     x = x_host.to(dev)
     m.packed_weights()
     if args.release_master:
@@ -291,7 +306,8 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
         "data": "synthetic (seeded, config-1 distributions)",
-        "config": {"workload": ("config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024"
+        "config": {"workload": (f"{cfg['name']}: S={S} tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024"
+                                + (", Zipf logit bias 2*ln((e+1)^-1.2)" if cfg.get("zipf") else "")
                                 if world == 1 else
                                 f"config3: {S} tokens/GPU, d=3072 (H=1), E=128 sharded {cfg['E'] // world}/GPU, "
                                 "top-8 softmax, SwiGLU7 de=1024"),
@@ -315,9 +331,58 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "gpu_launches": (KERNELS_PER_STEP if world == 1 else KERNELS_PER_STEP_EP) * args.steps,   # kernels of libmhmoe inside the device-timed region
         "clocks": clk.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline and not args.release_master:
+    if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == 1:
         out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
     return out
+
+
+def run_stack(args, cfg, dev):
+    """Config 4: 4 MoE layers stacked with a bf16 residual add, 256 tokens — dominated by
+    streaming each layer's NVFP4 weights from HBM (reported as GB/s)."""
+    import torch
+    from flash_mh_moe import _lib
+    layers = []
+    for i in range(cfg["layers"]):
+        m, x_host = make_layer(dict(cfg, seed=cfg["seed"] * 10 + i), dev, 0)
+        m.release_master_weights()
+        layers.append(m)
+    torch.cuda.empty_cache()
+    x0 = x_host.to(dev)
+
+    def fwd(x):
+        for m in layers:
+            x = x + m(x)
+        return x
+    for _ in range(args.warmup):
+        fwd(x0)
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        t0.record()
+        for _ in range(args.steps):
+            fwd(x0)
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    gu, dn = layers[0].packed_weights()
+    wbytes = sum(t.numel() * t.element_size() for t in (gu.data, gu.sf, gu.gscale, dn.data, dn.sf, dn.gscale))
+    act = cfg["S"] * cfg["d"] * 2 * 2
+    total_bytes = cfg["layers"] * (wbytes + act)
+    peaks = load_peaks()
+    gbs = total_bytes / (ms * 1e-3) / 1e9
+    return {"metric": METRIC, "value": round(cfg["S"] / (ms * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
+            "data": "synthetic (seeded, config-4 distributions)",
+            "config": {"workload": f"config4: {cfg['S']} tokens, {cfg['layers']} stacked MoE layers + bf16 residual, "
+                                   "d=3072, E=128, top-8, de=1024", "tokens_per_gpu": cfg["S"]},
+            "roofline": {"kernel": "whole 4-layer stack (weight streaming)", "bound": "hbm",
+                         "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
+                         "algorithmic_bytes_per_step": total_bytes,
+                         "peak_note": f"{peaks['source']} HBM copy bandwidth; vs 8000 GB/s nominal: {gbs / 8000:.3f}"},
+            "gpu_launches": KERNELS_PER_STEP * cfg["layers"] * args.steps, "clocks": clk.summary()}
 
 
 # ───────────────────────────── CPU reference path (oracle port) ─────────────────────────────
@@ -404,14 +469,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--config", type=int, choices=[1, 2, 4], default=1,
+                    help="BASELINE config at N=1 (1: headline; 2: Zipf-skewed routing; 4: 4-layer small batch)")
     ap.add_argument("--release-master", action="store_true",
                     help="free the bf16 expert weights after NVFP4 packing (profiler captures)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default: config 1's 16384; smaller only for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.tokens:
-        CFG1["S"] = args.tokens
     world, rank, local = dist_setup()
     try:
         out = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)

@@ -78,11 +78,13 @@ MHMOE_API int mhmoe_router_prepare(const float* gate, int n_experts, int dh, int
  * for selection, top-k (sorted desc, ties to the lower id), L1 normalisation and
  * route_scale (route.py:28-148 without virtual groups).  x bf16 [S, H, dh] with heads
  * contiguous (x_stride_h == dh).  E <= 256, K <= 16, dh % 64 == 0.
- * logits (optional) receives fp32 [H, S, E]. */
+ * logit_bias (optional, fp32 [H*E]) is added to the logits before scoring (a gate bias
+ * term; the reference has none, pass NULL).  logits (optional) receives the fp32 [H, S, E]
+ * logits the scores were computed from. */
 MHMOE_API int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const void* planes, int nsplit,
-                          int S, int H, int dh, int E, int K, int score_func, const float* expert_bias,
-                          int route_norm, float norm_eps, float route_scale, float* probs, int64_t* idx,
-                          float* logits, int* dev_status, void* stream);
+                          int S, int H, int dh, int E, int K, int score_func, const float* logit_bias,
+                          const float* expert_bias, int route_norm, float norm_eps, float route_scale, float* probs,
+                          int64_t* idx, float* logits, int* dev_status, void* stream);
 
 /* Top-k gating from logits.  Replaces compute_topk_probs_and_indices
  * (inference/flash_mh_moe/route.py:157-199 -> :28-148).

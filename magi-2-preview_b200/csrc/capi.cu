@@ -106,8 +106,9 @@ int mhmoe_router_prepare(const float* gate, int n_experts, int dh, int nsplit, v
 }
 
 int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const void* planes, int nsplit, int S, int H,
-                int dh, int E, int K, int score_func, const float* expert_bias, int route_norm, float norm_eps,
-                float route_scale, float* probs, int64_t* idx, float* logits, int* dev_status, void* stream) {
+                int dh, int E, int K, int score_func, const float* logit_bias, const float* expert_bias, int route_norm,
+                float norm_eps, float route_scale, float* probs, int64_t* idx, float* logits, int* dev_status,
+                void* stream) {
   MHMOE_REQUIRE(x && planes && probs && idx);
   MHMOE_REQUIRE(S >= 0 && H > 0 && dh > 0 && dh % 64 == 0 && E > 0 && E <= 256 && K > 0 && K <= 16 && K <= E);
   MHMOE_REQUIRE(nsplit >= 1 && nsplit <= 3 && (score_func == 0 || score_func == 1));
@@ -117,8 +118,8 @@ int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const voi
   if (S == 0) return MHMOE_OK;
   cudaError_t ce = cudaSuccess;
   const int rc = router_tc(static_cast<const __nv_bfloat16*>(x), x_stride_s, static_cast<const __nv_bfloat16*>(planes),
-                           nsplit, S, H, dh, E, K, score_func, expert_bias, route_norm, norm_eps, route_scale, probs,
-                           idx, logits, dev_status, static_cast<cudaStream_t>(stream), &ce);
+                           nsplit, S, H, dh, E, K, score_func, logit_bias, expert_bias, route_norm, norm_eps,
+                           route_scale, probs, idx, logits, dev_status, static_cast<cudaStream_t>(stream), &ce);
   if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "route");
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed (route)";
   return rc;

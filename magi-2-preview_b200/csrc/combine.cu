@@ -63,13 +63,22 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
     for (int j = 0; j < cnt; ++j) nvalid += srt[warp][j] != 0x7fffffff;
     for (int c = lane; c < nvec; c += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j = 0; j < nvalid; ++j) {
-        const uint4 u = *reinterpret_cast<const uint4*>(P + (int64_t)srt[warp][j] * dh + c * 8);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int j0 = 0; j0 < nvalid; j0 += 8) {
+        // issue up to 8 independent row loads before accumulating (in ascending row order)
+        uint4 u[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
-          acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u));
+        for (int jj = 0; jj < 8; ++jj)
+          if (j0 + jj < nvalid) u[jj] = *reinterpret_cast<const uint4*>(P + (int64_t)srt[warp][j0 + jj] * dh + c * 8);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          if (j0 + jj < nvalid) {
+            const uint32_t w[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
+              acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xFFFF0000u));
+            }
+          }
         }
       }
       uint32_t o[4];

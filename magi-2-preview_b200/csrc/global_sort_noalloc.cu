@@ -32,8 +32,10 @@ namespace {
 
 constexpr int64_t NOALLOC_MAX_ROWS = 262144;
 constexpr int64_t NOALLOC_MAX_EXPERTS = 1024;
-// global_sort_ws_bytes() at the limits: chunks of 1024 rows -> 256 chunk histograms.
-constexpr int64_t NOALLOC_CHUNKS = NOALLOC_MAX_ROWS / 1024;
+// This entry point sorts in chunks of >= 1024 rows, so at the limits the scratch holds
+// 256 chunk histograms (global_sort_ws_bytes(..., NOALLOC_MIN_CHUNK)).
+constexpr int NOALLOC_MIN_CHUNK = 1024;
+constexpr int64_t NOALLOC_CHUNKS = NOALLOC_MAX_ROWS / NOALLOC_MIN_CHUNK;
 constexpr int64_t NOALLOC_MTILES = NOALLOC_MAX_ROWS / 128 + NOALLOC_MAX_EXPERTS;
 constexpr size_t NOALLOC_SCRATCH_BYTES =
     ((size_t)(NOALLOC_CHUNKS + 2) * NOALLOC_MAX_EXPERTS + 1 + 3 * (size_t)NOALLOC_MTILES) * sizeof(int) + 256;
@@ -75,7 +77,7 @@ extern "C" MHMOE_API int mhmoe_global_sort_noalloc(const float* topk_probs, cons
   const int64_t R = (int64_t)H * S * K;
   const int64_t HE = (int64_t)H * E;
   if (R > NOALLOC_MAX_ROWS || HE > NOALLOC_MAX_EXPERTS ||
-      global_sort_ws_bytes(H, S, K, E) > NOALLOC_SCRATCH_BYTES) {
+      global_sort_ws_bytes(H, S, K, E, NOALLOC_MIN_CHUNK) > NOALLOC_SCRATCH_BYTES) {
     set_last_error("mhmoe_global_sort_noalloc: " + std::to_string(R) + " routed rows / " + std::to_string(HE) +
                    " experts exceed the built-in scratch limits (" + std::to_string(NOALLOC_MAX_ROWS) +
                    " rows, " + std::to_string(NOALLOC_MAX_EXPERTS) + " experts); use mhmoe_global_sort");
@@ -96,7 +98,7 @@ extern "C" MHMOE_API int mhmoe_global_sort_noalloc(const float* topk_probs, cons
   cudaError_t e = scratch_address(&ws);
   if (e == cudaSuccess)
     e = launch_global_sort(topk_probs, topk_idx, H, S, K, E, ws, gather_ids, probs_sorted, expert_offsets,
-                           row_of_flat, dev_status, st);
+                           row_of_flat, dev_status, st, NOALLOC_MIN_CHUNK);
   if (e != cudaSuccess) {
     set_last_error(std::string("mhmoe_global_sort_noalloc: ") + cudaGetErrorString(e));
     return MHMOE_ERR_LAUNCH;

@@ -13,11 +13,13 @@ namespace mhmoe {
 inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts) { return (R + 127) / 128 + n_experts; }
 
 // permute.cu
-int sort_chunk_size(int64_t R);
-size_t global_sort_ws_bytes(int H, int S, int K, int E);
+// Sort chunks hold at least min_chunk flat entries (256 by default; larger chunks shrink the
+// histogram scratch).
+int sort_chunk_size(int64_t R, int min_chunk = 256);
+size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk = 256);
 cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, int S, int K, int E, void* ws,
                                int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
-                               int32_t* row_of_flat, int* status, cudaStream_t st);
+                               int32_t* row_of_flat, int* status, cudaStream_t st, int min_chunk = 256);
 cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
                                int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st);
 size_t token_rows_ws_bytes(int64_t T);
@@ -85,8 +87,8 @@ cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataTy
 cudaError_t launch_split_gate(const float* gate, int64_t HE, int dh, int nsplit, __nv_bfloat16* out, int* flags,
                               cudaStream_t st);
 int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_planes, int nsplit, int S, int H,
-              int dh, int E, int K, int score_func, const float* bias, int route_norm, float norm_eps,
-              float route_scale, float* probs, int64_t* idx, float* logits, int* status, cudaStream_t st,
-              cudaError_t* cerr);
+              int dh, int E, int K, int score_func, const float* logit_bias, const float* bias, int route_norm,
+              float norm_eps, float route_scale, float* probs, int64_t* idx, float* logits, int* status,
+              cudaStream_t st, cudaError_t* cerr);
 
 }  // namespace mhmoe

@@ -36,17 +36,26 @@ __global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int
   for (int g = threadIdx.x; g < HE; g += blockDim.x) row[g] = sh[g];
 }
 
+// One warp per key: exclusive prefix over the chunk histograms, 32 chunks per step.
 __global__ void sort_colscan_kernel(int* __restrict__ hist, int nchunks, int HE, int* __restrict__ total) {
-  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (g >= HE) return;
   int run = 0;
-  for (int c = 0; c < nchunks; ++c) {
-    int* p = hist + (size_t)c * HE + g;
-    const int v = *p;
-    *p = run;
-    run += v;
+  for (int c0 = 0; c0 < nchunks; c0 += 32) {
+    const int c = c0 + lane;
+    int* ptr = hist + (size_t)c * HE + g;
+    const int v = c < nchunks ? *ptr : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (c < nchunks) *ptr = run + incl - v;
+    run += __shfl_sync(0xffffffffu, incl, 31);
   }
-  total[g] = run;
+  if (lane == 0) total[g] = run;
 }
 
 // Single CTA: expert_offsets / tile tables from per-expert counts (counts != nullptr)
@@ -260,18 +269,20 @@ __global__ void tok_fill_kernel(const int32_t* __restrict__ gather_ids, const in
 
 // ───────────────────────────── host launchers ─────────────────────────────
 
-int sort_chunk_size(int64_t R) {
-  int64_t c = (R + 1023) / 1024;
+// Chunk of flat entries per histogram row: 256 entries (8 warp steps in the scatter) up to
+// 2048 chunks, larger chunks beyond that so the histogram stays <= 2048 x H*E ints.
+int sort_chunk_size(int64_t R, int min_chunk) {
+  int64_t c = (R + 2047) / 2048;
   c = (c + 31) / 32 * 32;
-  return (int)std::max<int64_t>(1024, c);
+  return (int)std::max<int64_t>(min_chunk, c);
 }
 
 cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, int S, int K, int E, void* ws,
                                int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
-                               int32_t* row_of_flat, int* status, cudaStream_t st) {
+                               int32_t* row_of_flat, int* status, cudaStream_t st, int min_chunk) {
   const int64_t R = (int64_t)H * S * K;
   const int HE = H * E;
-  const int chunk = sort_chunk_size(R);
+  const int chunk = sort_chunk_size(R, min_chunk);
   const int nchunks = (int)((R + chunk - 1) / chunk);
   const int64_t mt = mtiles_upper_bound(R, HE);
   int* hist = static_cast<int*>(ws);
@@ -282,7 +293,7 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   int* tile_rows = tile_row0 + mt;
   const size_t shb = (size_t)HE * sizeof(int);
   sort_hist_kernel<<<nchunks, 256, shb, st>>>(idx, R, S * K, E, HE, chunk, hist, status);
-  sort_colscan_kernel<<<(HE + 255) / 256, 256, 0, st>>>(hist, nchunks, HE, total);
+  sort_colscan_kernel<<<(HE + 7) / 8, 256, 0, st>>>(hist, nchunks, HE, total);
   tile_tables_kernel<<<1, 1024, 0, st>>>(total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
                                          tile_rows, mtiles_upper_bound(R, HE), status);
   sort_scatter_kernel<<<nchunks, 32, shb, st>>>(idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
@@ -290,9 +301,9 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   return cudaGetLastError();
 }
 
-size_t global_sort_ws_bytes(int H, int S, int K, int E) {
+size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk) {
   const int64_t R = (int64_t)H * S * K;
-  const int chunk = sort_chunk_size(R);
+  const int chunk = sort_chunk_size(R, min_chunk);
   const int64_t nchunks = (R + chunk - 1) / chunk;
   const int64_t mt = mtiles_upper_bound(R, (int64_t)H * E);
   return ((size_t)(nchunks + 2) * (size_t)(H * E) + 1 + 3 * (size_t)mt) * sizeof(int) + 256;

@@ -30,6 +30,7 @@ constexpr int RT_THREADS = 192;
 constexpr int RT_MAXK = 16;
 
 struct RouterParams {
+  const float* logit_bias; // [H*E] or null: added to the logits before scoring
   const float* bias;       // [H*E] or null
   float* probs;            // [H, S, K]
   int64_t* idx;            // [H, S, K]
@@ -183,7 +184,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         for (int i = 0; i < 32; ++i) {
           const int e = c * 32 + i;
           if (e < p.E) {
-            const float l = __uint_as_float(r[i]);
+            const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
+                                         : __uint_as_float(r[i]);
             mx = fmaxf(mx, l);
             if (valid && p.logits) p.logits[row * p.E + e] = l;
           }
@@ -195,8 +197,14 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < p.E) sum += expf(__uint_as_float(r[i]) - mx);
+          for (int i = 0; i < 32; ++i) {
+            const int e = c * 32 + i;
+            if (e < p.E) {
+              const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
+                                           : __uint_as_float(r[i]);
+              sum += expf(l - mx);
+            }
+          }
         }
       }
       float tv[RT_MAXK], ts[RT_MAXK], thr = -INFINITY;
@@ -221,7 +229,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           const int e = c * 32 + i;
           float v = -INFINITY, sc = 0.f;
           if (e < p.E) {
-            const float l = __uint_as_float(r[i]);
+            const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
+                                         : __uint_as_float(r[i]);
             sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
             v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
           }
@@ -311,9 +320,9 @@ cudaError_t launch_split_gate(const float* gate, int64_t HE, int dh, int nsplit,
 }
 
 int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_planes, int nsplit, int S, int H,
-              int dh, int E, int K, int score_func, const float* bias, int route_norm, float norm_eps,
-              float route_scale, float* probs, int64_t* idx, float* logits, int* status, cudaStream_t st,
-              cudaError_t* cerr) {
+              int dh, int E, int K, int score_func, const float* logit_bias, const float* bias, int route_norm,
+              float norm_eps, float route_scale, float* probs, int64_t* idx, float* logits, int* status,
+              cudaStream_t st, cudaError_t* cerr) {
   const int Npad = std::max(16, (E + 15) / 16 * 16);
   CUtensorMap tx, tg;
   if (encode_bf16_2d(&tx, x, (uint64_t)H * dh, (uint64_t)S, (uint64_t)sx_s * 2, RT_BK, RT_BM) != cudaSuccess ||
@@ -321,6 +330,7 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
                      (uint32_t)Npad) != cudaSuccess)
     return MHMOE_ERR_DRIVER;
   RouterParams p{};
+  p.logit_bias = logit_bias;
   p.bias = bias;
   p.probs = probs;
   p.idx = idx;

@@ -28,8 +28,8 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_last_error": (C.c_char_p, []),
     "mhmoe_router_logits": (i32, [vp, i64, i64, vp, i32, i32, i32, i32, vp, vp]),
     "mhmoe_router_prepare": (i32, [vp, i32, i32, i32, vp, vp, vp]),
-    "mhmoe_route": (i32, [vp, i64, i64, vp, i32, i32, i32, i32, i32, i32, i32, vp, i32, f32, f32, vp, vp, vp, vp,
-                          vp]),
+    "mhmoe_route": (i32, [vp, i64, i64, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, i32, f32, f32, vp, vp, vp,
+                          vp, vp]),
     "mhmoe_topk": (i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, i32, f32, f32, vp, vp, vp]),
     "mhmoe_global_sort_workspace_bytes": (sz, [i32, i32, i32, i32]),
     "mhmoe_global_sort": (i32, [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp]),

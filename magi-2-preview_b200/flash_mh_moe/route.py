@@ -155,11 +155,13 @@ def fused_router_supported(E: int, K: int, dh: int) -> bool:
 
 def route_fused(x_heads: torch.Tensor, planes: torch.Tensor, nsplit: int, num_experts: int, top_k: int,
                 score_func: str = "softmax", expert_bias: torch.Tensor | None = None, route_norm: bool = True,
-                norm_eps: float = 1e-12, route_scale: float = 1.0, return_logits: bool = False):
+                norm_eps: float = 1e-12, route_scale: float = 1.0, return_logits: bool = False,
+                logit_bias: torch.Tensor | None = None):
     """Router logits + top-k in one tcgen05 kernel (``CoreMultiHeadMoE._route``).
 
     x_heads [S, H, dh] bf16 (heads contiguous).  Returns (probs fp32 [H,S,K], idx int64
     [H,S,K]) and, with ``return_logits``, the fp32 logits [H,S,E] as a third item.
+    ``logit_bias`` [H*E] (optional) is added to the logits before scoring.
     """
     if score_func not in score_func_name2id_map:
         raise ValueError(f"Unknown score_func: {score_func}")
@@ -174,10 +176,12 @@ def route_fused(x_heads: torch.Tensor, planes: torch.Tensor, nsplit: int, num_ex
     idx = torch.empty(H, S, K, dtype=torch.int64, device=dev)
     logits = torch.empty(H, S, E, dtype=torch.float32, device=dev) if return_logits else None
     bias = None if expert_bias is None else expert_bias.reshape(-1).float().contiguous()
+    lbias = None if logit_bias is None else logit_bias.reshape(-1).float().contiguous()
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().mhmoe_route(
             x.data_ptr(), x.stride(0), x.stride(1), planes.data_ptr(), int(nsplit), S, H, dh, E, K,
-            score_func_name2id_map[score_func], _lib.ptr(bias), int(bool(route_norm)), float(norm_eps),
+            score_func_name2id_map[score_func], _lib.ptr(lbias), _lib.ptr(bias), int(bool(route_norm)),
+            float(norm_eps),
             float(route_scale), probs.data_ptr(), idx.data_ptr(), _lib.ptr(logits),
             _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)), "route")
     return (probs, idx, logits) if return_logits else (probs, idx)
