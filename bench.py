@@ -287,7 +287,7 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
     R = S * K * cfg["H"]
     if world > 1:
         from flash_mh_moe.ep import LAST_STATS
-        R_gemm = LAST_STATS.get("rows_received", R)     # rows this rank's expert GEMMs processed
+        R_gemm = int(LAST_STATS["rows_received"].item()) if "rows_received" in LAST_STATS else R  # expert-GEMM rows
     else:
         R_gemm = R
     flop_gate_up = 2.0 * R_gemm * (d // cfg["H"]) * (2 * de)

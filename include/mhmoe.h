@@ -107,9 +107,10 @@ MHMOE_API size_t mhmoe_global_sort_workspace_bytes(int H, int S, int K, int E);
  * Replaces flash_mh_moe_global_sort (inference/flash_mh_moe/route.py:209-253):
  * gather_ids int32 [R], probs_sorted fp32 [R], expert_offsets int64 [H*E+1],
  * bit-identical to argsort(stable=True).  row_of_flat int32 [R] (optional):
- * the sorted position of flat entry f.  H*E <= 12288.  An expert id outside
- * [0, E) is never used as an index: the entry is dropped and MHMOE_ERR_ARGS is
- * recorded in dev_status. */
+ * the sorted position of flat entry f (-1 for dropped entries).  H*E <= 12288.
+ * A negative expert id marks an empty slot and is skipped (the reference never emits
+ * one; expert-parallel packing uses them); an id >= E is never used as an index: the
+ * entry is dropped and MHMOE_ERR_ARGS is recorded in dev_status. */
 MHMOE_API int mhmoe_global_sort(const float* topk_probs, const int64_t* topk_idx, int H, int S, int K, int E,
                       void* workspace, int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
                       int32_t* row_of_flat, int* dev_status, void* stream);
@@ -163,12 +164,15 @@ MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_strid
                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
                     void* const* stage_events, void* stream);
 
-/* The FFN above on rows that are already NVFP4 (per-row scales): xq [T, dh/2], xsf
- * [T, dh/16] row-major scales, xg [T]; gather_ids index these T rows (H = 1).  Used by
- * the expert-parallel receiver, whose rows arrive quantised.  y: [T, dh] bf16 rows with
- * pitch y_stride (combined through tok_rows / tok_offsets / k_fixed as above).
- * stage_events: as for mhmoe_ffn_nvfp4 (optional). */
-MHMOE_API int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float* xg, int T, int dh, int de,
+/* The FFN above on rows that are already NVFP4 (per-row scales): row t has its dh/2
+ * data bytes at xq + t*xq_pitch, its dh/16 row-major scale bytes at xsf + t*xsf_pitch
+ * and its fp32 row scale at xg + t*xg_pitch (byte pitches, 16-B aligned data/scales);
+ * gather_ids index these T rows (H = 1).  Used by the expert-parallel receiver, which
+ * reads the received records in place.  y: [T, dh] bf16 rows with pitch y_stride
+ * (combined through tok_rows / tok_offsets / k_fixed as above).  stage_events: as for
+ * mhmoe_ffn_nvfp4 (optional). */
+MHMOE_API int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, int64_t xq_pitch, const uint8_t* xsf, int64_t xsf_pitch,
+                                        const uint8_t* xg, int64_t xg_pitch, int T, int dh, int de,
                                         int n_experts, int64_t R, const int32_t* gather_ids,
                                         const float* probs_sorted, const int64_t* expert_offsets,
                                         const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale,
@@ -193,19 +197,27 @@ MHMOE_API int mhmoe_combine(const void* P, int64_t P_rows, const int32_t* pad_of
                             const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R, void* y,
                             int64_t y_stride_s, int64_t y_stride_h, void* stream);
 
-/* Expert-parallel dispatch packing.  Replaces the send side of ep_dispatch
- * (magi2_preview.py:3277-3299) for token -> expert sharding: sorted row r (grouped by
- * destination because each rank owns a contiguous expert range of E_loc experts) gets
- * the NVFP4 row of its token (xq/xsf/xg, T = S*H rows) and a 16-byte meta record
- * {g, local expert id (int bits), prob, 0}. */
-MHMOE_API int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E,
-                            int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
-                            const int64_t* expert_offsets, uint8_t* send_xq, uint8_t* send_xsf, void* send_meta,
+/* Expert-parallel dispatch (token -> expert sharding over n_ranks contiguous ranges of
+ * E_loc flattened experts).  Replaces the head-sharded ep_dispatch / ep_undispatch of
+ * the reference (magi2_preview.py:3277-3327).  A token row travels once to each rank
+ * owning any of its K experts, as one record of mhmoe_ep_row_bytes(dh, K) bytes:
+ * [dh/2 NVFP4 data][dh/16 scales][16 B {g, count, 0, 0}][K x {local expert, prob}].
+ *   mhmoe_ep_dest: dest [H*S, n_ranks] int64 (key h*S + s): d if the row goes to rank
+ *     d, else -1 (sorting it with mhmoe_global_sort, H = 1, K = n_ranks, E = n_ranks,
+ *     gives the send order, per-rank counts and the (key, rank) -> send row map).
+ *   mhmoe_ep_pack: send row j (key send_key[j], destination from send_offsets) ->
+ *     its record, from the per-token quantised x (mhmoe_quant_tokens) and the routing.
+ *   mhmoe_ep_unpack: received records -> local expert ids int64 [R, K] (-1 past the
+ *     count) and probs [R, K]. */
+MHMOE_API int64_t mhmoe_ep_row_bytes(int dh, int K);
+MHMOE_API int mhmoe_ep_dest(const int64_t* topk_idx, int H, int S, int K, int E, int n_ranks, int64_t* dest,
                             int* dev_status, void* stream);
-
-/* Receiver side: meta records -> g [R], local expert id int64 [R], prob [R]. */
-MHMOE_API int mhmoe_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
-                              int* dev_status, void* stream);
+MHMOE_API int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                            const int64_t* topk_idx, const float* topk_probs, int K, int E, int n_ranks,
+                            const int32_t* send_key, const int64_t* send_offsets, int64_t R_send, uint8_t* send,
+                            void* stream);
+MHMOE_API int mhmoe_ep_unpack(const uint8_t* recv, int64_t R, int dh, int K, int E_loc, int64_t* local_expert,
+                              float* probs, int* dev_status, void* stream);
 
 /* Per-row NVFP4 quantisation of bf16 rows x[r, 0:K] (row pitch in elements):
  * data [M, K/2], sf atoms, gscale [M] = amax(row)/2688.  K % 64 == 0. */

@@ -227,7 +227,8 @@ int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S
   return rc;
 }
 
-int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float* xg, int T, int dh, int de,
+int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, int64_t xq_pitch, const uint8_t* xsf, int64_t xsf_pitch,
+                              const uint8_t* xg, int64_t xg_pitch, int T, int dh, int de,
                               int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
                               const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
                               const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
@@ -238,6 +239,8 @@ int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float
                 dn_gscale);
   MHMOE_REQUIRE(T >= 0 && n_experts > 0 && R >= 0 && dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
   MHMOE_REQUIRE(aligned16(xq) && aligned16(xsf) && aligned16(y) && y_stride % 8 == 0);
+  MHMOE_REQUIRE(xq_pitch >= dh / 2 && xq_pitch % 16 == 0 && xsf_pitch >= dh / 16 && xsf_pitch % 16 == 0);
+  MHMOE_REQUIRE(xg_pitch >= 4 && xg_pitch % 4 == 0 && (reinterpret_cast<uintptr_t>(xg) & 3) == 0);
   MHMOE_REQUIRE(tok_rows || !tok_offsets);
   MHMOE_REQUIRE(!tok_rows || tok_offsets || k_fixed > 0);
   MHMOE_CHECK_ARCH();
@@ -252,7 +255,8 @@ int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, const uint8_t* xsf, const float
   const int rc = ffn_nvfp4(nullptr, 0, 0, T, 1, dh, de, n_experts, R, gather_ids, probs_sorted, expert_offsets,
                            gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, tok_rows, tok_offsets, k_fixed,
                            workspace, static_cast<__nv_bfloat16*>(y), y_stride, dh, dev_status, timeout_ns,
-                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce, xq, xsf, xg);
+                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce, xq, xsf, xg, xq_pitch,
+                           xsf_pitch, xg_pitch);
   if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4_quantized");
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
   return rc;
@@ -283,27 +287,40 @@ int mhmoe_combine(const void* P, int64_t P_rows, const int32_t* pad_of_row, int 
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "combine");
 }
 
-int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E, int E_loc,
-                  int64_t R, const int32_t* gather_ids, const float* probs_sorted, const int64_t* expert_offsets,
-                  uint8_t* send_xq, uint8_t* send_xsf, void* send_meta, int* dev_status, void* stream) {
-  MHMOE_REQUIRE(xq && xsf && xg && gather_ids && probs_sorted && expert_offsets && send_xq && send_xsf && send_meta);
-  MHMOE_REQUIRE(T >= 0 && dh % 256 == 0 && H > 0 && E > 0 && E_loc > 0 && (H * E) % E_loc == 0 && R >= 0);
-  MHMOE_REQUIRE(aligned16(xq) && aligned16(xsf) && aligned16(send_xq) && aligned16(send_xsf) && aligned16(send_meta));
+int64_t mhmoe_ep_row_bytes(int dh, int K) { return ep_row_bytes(dh, K); }
+
+int mhmoe_ep_dest(const int64_t* topk_idx, int H, int S, int K, int E, int n_ranks, int64_t* dest, int* dev_status,
+                  void* stream) {
+  MHMOE_REQUIRE(topk_idx && dest && H > 0 && S >= 0 && K > 0 && E > 0 && n_ranks > 0 && n_ranks <= 32);
+  MHMOE_REQUIRE(((int64_t)H * E) % n_ranks == 0);
   MHMOE_CHECK_ARCH();
-  if (R == 0) return MHMOE_OK;
-  const cudaError_t e = launch_ep_pack(xq, xsf, xg, T, dh, H, E, E_loc, R, gather_ids, probs_sorted, expert_offsets,
-                                       H * E, send_xq, send_xsf, send_meta, dev_status,
+  if (S == 0) return MHMOE_OK;
+  const cudaError_t e = launch_ep_dest(topk_idx, H, S, K, E, n_ranks, H * E / n_ranks, dest, dev_status,
                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_dest");
+}
+
+int mhmoe_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                  const int64_t* topk_idx, const float* topk_probs, int K, int E, int n_ranks, const int32_t* send_key,
+                  const int64_t* send_offsets, int64_t R_send, uint8_t* send, void* stream) {
+  MHMOE_REQUIRE(xq && xsf && xg && topk_idx && topk_probs && send_key && send_offsets && send);
+  MHMOE_REQUIRE(H > 0 && S >= 0 && dh > 0 && dh % 256 == 0 && K > 0 && E > 0 && n_ranks > 0 && n_ranks <= 32);
+  MHMOE_REQUIRE(((int64_t)H * E) % n_ranks == 0 && R_send >= 0);
+  MHMOE_REQUIRE(aligned16(xq) && aligned16(xsf) && aligned16(send));
+  MHMOE_CHECK_ARCH();
+  if (R_send == 0) return MHMOE_OK;
+  const cudaError_t e = launch_ep_pack(xq, xsf, xg, H, S, dh, topk_idx, topk_probs, K, E, H * E / n_ranks, send_key,
+                                       send_offsets, n_ranks, R_send, send, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_pack");
 }
 
-int mhmoe_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
+int mhmoe_ep_unpack(const uint8_t* recv, int64_t R, int dh, int K, int E_loc, int64_t* local_expert, float* probs,
                     int* dev_status, void* stream) {
-  MHMOE_REQUIRE(meta && g && local_expert && prob && R >= 0 && E_loc > 0);
+  MHMOE_REQUIRE(recv && local_expert && probs && R >= 0 && dh > 0 && dh % 256 == 0 && K > 0 && E_loc > 0);
   MHMOE_CHECK_ARCH();
   if (R == 0) return MHMOE_OK;
-  const cudaError_t e =
-      launch_ep_unpack(meta, R, E_loc, g, local_expert, prob, dev_status, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = launch_ep_unpack(recv, R, dh, K, E_loc, local_expert, probs, dev_status,
+                                         static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_unpack");
 }
 

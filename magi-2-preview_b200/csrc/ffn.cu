@@ -140,13 +140,19 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
-              const uint8_t* xq_in, const uint8_t* xsf_in, const float* xg_in) {
+              const uint8_t* xq_in, const uint8_t* xsf_in, const uint8_t* xg_in, int64_t xq_pitch, int64_t xsf_pitch,
+              int64_t xg_pitch) {
   const int64_t T = (int64_t)S * H;
   FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
   const bool prequant = xq_in != nullptr;
   const uint8_t* xq = prequant ? xq_in : w.xq;
   const uint8_t* xsf = prequant ? xsf_in : w.xsf;
-  const float* xg = prequant ? xg_in : w.xg;
+  const uint8_t* xg = prequant ? xg_in : reinterpret_cast<const uint8_t*>(w.xg);
+  if (!prequant) {
+    xq_pitch = dh / 2;
+    xsf_pitch = dh / 16;
+    xg_pitch = sizeof(float);
+  }
   const int64_t max_mt = mtiles_upper_bound(R, HE);
   const int64_t rows = max_mt * 128;
   cudaError_t e;
@@ -167,8 +173,9 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
                                status, st));
   MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
   if (!prequant) MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
-  MHMOE_TRY(launch_group_rows(xq, xsf, xg, T, dh, H, HE / H, gather_ids, w.cu_tiles, HE, max_mt, w.tile_expert,
-                              w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale, status, st));
+  MHMOE_TRY(launch_group_rows(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H, HE / H, gather_ids, w.cu_tiles,
+                              HE, max_mt, w.tile_expert, w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale,
+                              status, st));
 
   CUtensorMap ta1, tb1, ta2, tb2, tc2;
   if (encode_tmap_2d_u8(&ta1, w.a_data, dh / 2, rows, 128, 128) != cudaSuccess ||

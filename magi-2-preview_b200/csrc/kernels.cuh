@@ -28,10 +28,11 @@ cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, con
                               void* ws, int32_t* tok_offsets, int32_t* tok_rows, int* status, cudaStream_t st);
 
 // quant.cu
-cudaError_t launch_group_rows(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H,
-                              int E_per_head, const int32_t* gather_ids, const int* cu_tiles, int HE,
-                              int64_t max_mtiles, const int* tile_expert, const int* tile_row0, const int* tile_rows,
-                              uint8_t* a_data, uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
+cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t* xsf, int64_t xsf_pitch,
+                              const uint8_t* xg, int64_t xg_pitch, int64_t T, int dh, int H, int E_per_head,
+                              const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
+                              const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
+                              uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
 cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
                                 uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st);
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
@@ -65,15 +66,20 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               const uint8_t* dn_sf, const float* dn_gscale, const int32_t* tok_rows, const int32_t* tok_offsets,
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
-              const uint8_t* xq_in = nullptr, const uint8_t* xsf_in = nullptr, const float* xg_in = nullptr);
+              const uint8_t* xq_in = nullptr, const uint8_t* xsf_in = nullptr, const uint8_t* xg_in = nullptr,
+              int64_t xq_pitch = 0, int64_t xsf_pitch = 0, int64_t xg_pitch = 0);
 
 // ep.cu
-cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H, int E,
-                           int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
-                           const int64_t* expert_offsets, int HE, uint8_t* send_xq, uint8_t* send_xsf,
-                           void* send_meta, int* status, cudaStream_t st);
-cudaError_t launch_ep_unpack(const void* meta, int64_t R, int E_loc, float* g, int64_t* local_expert, float* prob,
+int64_t ep_row_bytes(int dh, int K);
+cudaError_t launch_ep_dest(const int64_t* idx, int H, int S, int K, int E, int n_ranks, int E_loc, int64_t* dest,
+                           int* status, cudaStream_t st);
+cudaError_t launch_ep_pack(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                           const int64_t* idx, const float* probs, int K, int E, int E_loc, const int32_t* send_key,
+                           const int64_t* send_offsets, int n_ranks, int64_t R_send, uint8_t* send, cudaStream_t st);
+cudaError_t launch_ep_unpack(const uint8_t* recv, int64_t R, int dh, int K, int E_loc, int64_t* idx, float* probs,
                              int* status, cudaStream_t st);
+
+// ffn.cu (continued)
 int gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtiles, const int32_t* tile_expert,
                    const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out, int* status,
                    uint64_t timeout_ns, cudaStream_t st, cudaError_t* cerr);

@@ -24,7 +24,8 @@ __global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int
   const int64_t f1 = min(f0 + chunk, R);
   for (int64_t f = f0 + threadIdx.x; f < f1; f += blockDim.x) {
     const int64_t e = idx[f];
-    if (e < 0 || e >= E) {            // out-of-range expert id: record, never index with it
+    if (e < 0) continue;              // negative id: "no expert" slot, skipped
+    if (e >= E) {                     // out-of-range expert id: record, never index with it
       record_error(status, MHMOE_ERR_ARGS);
       continue;
     }
@@ -132,8 +133,8 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
                                     int S, int K, int E, int HE, int chunk, const int* __restrict__ hist,
                                     const int64_t* __restrict__ offsets, int32_t* __restrict__ gather_ids,
                                     float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat) {
-  // Entries with an out-of-range expert id were rejected (and recorded) by
-  // sort_hist_kernel; they get no slot here either.
+  // Entries with a negative ("no expert") or out-of-range id get no slot; their
+  // row_of_flat entry is -1.
   extern __shared__ int cursor[];
   const int lane = threadIdx.x;
   const int* row = hist + (size_t)blockIdx.x * HE;
@@ -164,6 +165,8 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
       gather_ids[pos] = (int32_t)((f / K) % S);
       probs_sorted[pos] = probs[f];
       if (row_of_flat) row_of_flat[f] = pos;
+    } else if (f < f1 && row_of_flat) {
+      row_of_flat[f] = -1;
     }
   }
 }

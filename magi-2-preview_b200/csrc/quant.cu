@@ -64,8 +64,9 @@ __device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, 
 // Grouped A operand of the gate/up GEMM: one warp per padded row of the expert-grouped
 // row space copies its token's NVFP4 row (per-token quantised x: data, row-major scales,
 // row scale) into place, scales into the SF-atom layout.  Padding rows are zeroed.
-__global__ void group_rows_kernel(const uint8_t* __restrict__ xq, const uint8_t* __restrict__ xsf,
-                                  const float* __restrict__ xg, int64_t T, int dh, int H, int E_per_head,
+__global__ void group_rows_kernel(const uint8_t* __restrict__ xq, int64_t xq_pitch, const uint8_t* __restrict__ xsf,
+                                  int64_t xsf_pitch, const uint8_t* __restrict__ xg, int64_t xg_pitch, int64_t T,
+                                  int dh, int H, int E_per_head,
                                   const int32_t* __restrict__ gather_ids, const int* __restrict__ cu_tiles, int HE,
                                   const int* __restrict__ tile_expert, const int* __restrict__ tile_row0,
                                   const int* __restrict__ tile_rows, uint8_t* __restrict__ a_data,
@@ -86,14 +87,14 @@ __global__ void group_rows_kernel(const uint8_t* __restrict__ xq, const uint8_t*
     }
   }
   uint4* dst = reinterpret_cast<uint4*>(a_data + prow * (dh / 2));
-  const uint4* src = t >= 0 ? reinterpret_cast<const uint4*>(xq + t * (dh / 2)) : nullptr;
+  const uint4* src = t >= 0 ? reinterpret_cast<const uint4*>(xq + t * xq_pitch) : nullptr;
   for (int i = lane; i < dh / 32; i += 32) dst[i] = src ? src[i] : make_uint4(0, 0, 0, 0);
-  const uint32_t* ssrc = t >= 0 ? reinterpret_cast<const uint32_t*>(xsf + t * (dh / 16)) : nullptr;
+  const uint32_t* ssrc = t >= 0 ? reinterpret_cast<const uint32_t*>(xsf + t * xsf_pitch) : nullptr;
   for (int w = lane; w < dh / 64; w += 32) {
     const uint32_t v = ssrc ? ssrc[w] : 0u;
     *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)(4 * w), (uint32_t)dh)) = v;
   }
-  if (lane == 0) a_gscale[prow] = t >= 0 ? xg[t] : 1.0f;
+  if (lane == 0) a_gscale[prow] = t >= 0 ? *reinterpret_cast<const float*>(xg + t * xg_pitch) : 1.0f;
 }
 
 // Per-token quantisation: row t = s * H + h of x [S, H, dh]; scales row-major [T, dh/16].
@@ -177,12 +178,14 @@ __global__ void pack_tile_kernel(const __nv_bfloat16* __restrict__ w, int Kdim, 
 
 // ───────────────────────────── launchers ─────────────────────────────
 
-cudaError_t launch_group_rows(const uint8_t* xq, const uint8_t* xsf, const float* xg, int64_t T, int dh, int H,
-                              int E_per_head, const int32_t* gather_ids, const int* cu_tiles, int HE,
-                              int64_t max_mtiles, const int* tile_expert, const int* tile_row0, const int* tile_rows,
-                              uint8_t* a_data, uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
+cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t* xsf, int64_t xsf_pitch,
+                              const uint8_t* xg, int64_t xg_pitch, int64_t T, int dh, int H, int E_per_head,
+                              const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
+                              const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
+                              uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
   const int64_t rows = max_mtiles * 128;
-  group_rows_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(xq, xsf, xg, T, dh, H, E_per_head, gather_ids, cu_tiles,
+  group_rows_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H,
+                                                          E_per_head, gather_ids, cu_tiles,
                                                           HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
                                                           a_gscale, status);
   return cudaGetLastError();

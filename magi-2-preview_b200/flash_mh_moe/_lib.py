@@ -39,12 +39,14 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_pack_weights_nvfp4": (i32, [i32, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp]),
     "mhmoe_ffn_nvfp4": (i32, [vp, i64, i64, i32, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                               vp, vp, i32, vp, vp, i64, i64, vp, u64, vp, vp]),
-    "mhmoe_ffn_nvfp4_quantized": (i32, [vp, vp, vp, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                                        vp, vp, i32, vp, vp, i64, vp, u64, vp, vp]),
+    "mhmoe_ffn_nvfp4_quantized": (i32, [vp, i64, vp, i64, vp, i64, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp,
+                                        vp, vp, vp, vp, vp, i32, vp, vp, i64, vp, u64, vp, vp]),
     "mhmoe_quant_tokens": (i32, [vp, i64, i64, i32, i32, i32, vp, vp, vp, vp]),
     "mhmoe_combine": (i32, [vp, i64, vp, i32, i32, i32, vp, vp, i32, i64, vp, i64, i64, vp]),
-    "mhmoe_ep_pack": (i32, [vp, vp, vp, i64, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp]),
-    "mhmoe_ep_unpack": (i32, [vp, i64, i32, vp, vp, vp, vp, vp]),
+    "mhmoe_ep_row_bytes": (i64, [i32, i32]),
+    "mhmoe_ep_dest": (i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp]),
+    "mhmoe_ep_pack": (i32, [vp, vp, vp, i32, i32, i32, vp, vp, i32, i32, i32, vp, vp, i64, vp, vp]),
+    "mhmoe_ep_unpack": (i32, [vp, i64, i32, i32, i32, vp, vp, vp, vp]),
     "mhmoe_quantize_rows_nvfp4": (i32, [vp, i64, i64, i32, vp, vp, vp, vp]),
     "mhmoe_gemm_nvfp4_raw": (i32, [vp, vp, i32, vp, vp, vp, i32, i32, i32, vp, vp, u64, vp]),
 }

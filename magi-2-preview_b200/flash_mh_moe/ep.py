@@ -5,18 +5,23 @@ group and swaps the whole activation with one ``all_to_all_single`` each way; wi
 heads padded to 16 on 8 ranks, two ranks hold only zero "dummy" heads
 (``magi2_preview.py:2514-2537``).  Here the flattened experts ``[0, H*E)`` are split into
 ``ep`` contiguous ranges (the same dim-0 row slices the reference's EP checkpoint loader
-reads when ``H % ep == 0``) and only routed rows move, in NVFP4:
+reads when ``H % ep == 0``) and only routed token rows move, in NVFP4, once per
+destination rank:
 
-  1. route + stable sort the rank's own tokens (rows come out grouped by destination rank,
-     because expert ranges are contiguous);
-  2. quantise each token once, pack one NVFP4 row (+ 16-byte meta: row scale, local expert,
-     prob) per sorted row;
-  3. exchange counts (``all_to_all_single`` of n ints, read on the host), then the rows;
-  4. receiver: sort received rows by local expert, run the NVFP4 FFN on them, keep one
-     bf16 output row per received row (prob already applied);
-  5. send the output rows back; the source combines each (token, head)'s K rows in
-     ascending global-expert order — the same order as the single-GPU layer, so the EP
-     output equals the single-device output bit for bit.
+  1. quantise each (head, token) row once; mark the ranks owning any of its K experts and
+     sort those (row, rank) pairs by rank (stable) -> send order and per-rank counts;
+  2. pack one record per (row, rank): NVFP4 data + scales + {row scale, count, the
+     rank's (local expert, prob) pairs};
+  3. exchange counts (``all_to_all_single`` of n ints, read on the host), then records;
+  4. receiver: expand records into (row, local expert) entries, sort them by expert, run
+     the NVFP4 FFN reading the received records in place, and sum each record's experts
+     in ascending expert order (fp32, rounded once to bf16) -> one row per record;
+  5. send those rows back; the source sums each (head, token)'s per-rank rows in
+     ascending rank order — i.e. ascending global expert ranges — and rounds to bf16.
+
+Per token, ~min(n, K) records cross the links each way instead of K rows.  The sum is
+grouped by rank, so the result matches the single-GPU layer to bf16 rounding of the
+per-rank partial sums (not bit for bit); it is deterministic.
 
 Device steps go through a backend object (``CudaBackend``: libmhmoe kernels) so the host
 logic (splits, orders, collectives) is testable on CPU ranks with ``gloo`` by substituting
@@ -79,53 +84,65 @@ class CudaBackend:
                    "quant_tokens")
         return xq, xsf, xg
 
-    def pack(self, xq, xsf, xg, H, E, E_loc, gather_ids, probs_sorted, expert_offsets):
-        R = gather_ids.numel()
+    def dest(self, idx, num_experts, n_ranks):
+        H, S, K = idx.shape
+        dev = idx.device
+        d = torch.empty(H * S, n_ranks, dtype=torch.int64, device=dev)
+        _lib.check(_lib.lib().mhmoe_ep_dest(idx.data_ptr(), H, S, K, num_experts, n_ranks, d.data_ptr(),
+                                             _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)), "ep_dest")
+        return d
+
+    def row_bytes(self, dh, K):
+        return int(_lib.lib().mhmoe_ep_row_bytes(dh, K))
+
+    def pack(self, xq, xsf, xg, H, S, idx, probs, num_experts, n_ranks, send_key, send_offsets, R_send):
         dev = xq.device
         dh = xq.shape[1] * 2
-        sxq = torch.empty(R, dh // 2, dtype=torch.uint8, device=dev)
-        sxsf = torch.empty(R, dh // 16, dtype=torch.uint8, device=dev)
-        meta = torch.empty(R, 4, dtype=torch.float32, device=dev)
-        _lib.check(_lib.lib().mhmoe_ep_pack(xq.data_ptr(), xsf.data_ptr(), xg.data_ptr(), xq.shape[0], dh, H, E,
-                                             E_loc, R, gather_ids.data_ptr(), probs_sorted.data_ptr(),
-                                             expert_offsets.data_ptr(), sxq.data_ptr(), sxsf.data_ptr(),
-                                             meta.data_ptr(), _lib.device_status(dev).data_ptr(),
-                                             _lib.stream_ptr(dev)), "ep_pack")
-        return sxq, sxsf, meta
+        K = idx.shape[-1]
+        send = torch.empty(R_send, self.row_bytes(dh, K), dtype=torch.uint8, device=dev)
+        _lib.check(_lib.lib().mhmoe_ep_pack(xq.data_ptr(), xsf.data_ptr(), xg.data_ptr(), H, S, dh, idx.data_ptr(),
+                                             probs.data_ptr(), K, num_experts, n_ranks, send_key.data_ptr(),
+                                             send_offsets.data_ptr(), R_send, send.data_ptr(), _lib.stream_ptr(dev)),
+                   "ep_pack")
+        return send
 
-    def unpack(self, meta, E_loc):
-        R = meta.shape[0]
-        dev = meta.device
-        g = torch.empty(R, dtype=torch.float32, device=dev)
-        le = torch.empty(R, dtype=torch.int64, device=dev)
-        pr = torch.empty(R, dtype=torch.float32, device=dev)
-        _lib.check(_lib.lib().mhmoe_ep_unpack(meta.data_ptr(), R, E_loc, g.data_ptr(), le.data_ptr(), pr.data_ptr(),
-                                               _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)),
-                   "ep_unpack")
-        return g, le, pr
+    def unpack(self, recv, dh, K, E_loc):
+        R = recv.shape[0]
+        dev = recv.device
+        le = torch.empty(R, K, dtype=torch.int64, device=dev)
+        pr = torch.empty(R, K, dtype=torch.float32, device=dev)
+        if R:
+            _lib.check(_lib.lib().mhmoe_ep_unpack(recv.data_ptr(), R, dh, K, E_loc, le.data_ptr(), pr.data_ptr(),
+                                                   _lib.device_status(dev).data_ptr(), _lib.stream_ptr(dev)),
+                       "ep_unpack")
+        return le, pr
 
     def sort(self, probs, idx, num_experts):
         from .route import flash_mh_moe_global_sort_with_inverse
         return flash_mh_moe_global_sort_with_inverse(probs, idx, num_experts)
 
-    def ffn_rows(self, xq, xsf, xg, gather_ids, probs_sorted, expert_offsets, row_of_flat, gu, dn,
-                 stage_events=None):
-        """One bf16 output row per quantised input row (prob applied), in input-row order."""
-        T = xq.shape[0]
-        dh = xq.shape[1] * 2
-        dev = xq.device
+    def ffn_records(self, recv, dh, K, gather_ids, probs_sorted, expert_offsets, row_of_flat, gu, dn,
+                    stage_events=None):
+        """Per received record: bf16 sum (ascending expert) of its experts' prob-weighted outputs."""
+        T = recv.shape[0]
+        dev = recv.device
         y = torch.empty(T, dh, dtype=torch.bfloat16, device=dev)
+        if T == 0:
+            return y
         n = expert_offsets.numel() - 1
         R = gather_ids.numel()
+        rb = recv.shape[1]
         L = _lib.lib()
         ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, T, 1, dh, gu.d_expert, n)), dtype=torch.uint8,
                          device=dev)
+        base = recv.data_ptr()
         _lib.check(L.mhmoe_ffn_nvfp4_quantized(
-            xq.data_ptr(), xsf.data_ptr(), xg.data_ptr(), T, dh, gu.d_expert, n, R, gather_ids.data_ptr(),
-            probs_sorted.data_ptr(), expert_offsets.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(),
-            gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(), dn.gscale.data_ptr(), row_of_flat.data_ptr(),
-            None, 1, ws.data_ptr(), y.data_ptr(), y.stride(0), _lib.device_status(dev).data_ptr(), 0,
-            _events(stage_events), _lib.stream_ptr(dev)), "ffn_nvfp4_quantized")
+            base, rb, base + dh // 2, rb, base + dh // 2 + dh // 16, rb, T, dh, gu.d_expert, n, R,
+            gather_ids.data_ptr(), probs_sorted.data_ptr(), expert_offsets.data_ptr(), gu.data.data_ptr(),
+            gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(), dn.gscale.data_ptr(),
+            row_of_flat.data_ptr(), None, K, ws.data_ptr(), y.data_ptr(), y.stride(0),
+            _lib.device_status(dev).data_ptr(), 0, _events(stage_events), _lib.stream_ptr(dev)),
+            "ffn_nvfp4_quantized")
         return y
 
     def combine(self, rows, S, H, row_of_flat, K):
@@ -138,7 +155,7 @@ class CudaBackend:
         return y
 
 
-LAST_STATS: dict = {}   # rows sent / received by the last ep_moe_layer call on this process
+LAST_STATS: dict = {}   # records / rows moved by the last ep_moe_layer call on this process
 
 
 def _a2a_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group) -> torch.Tensor:
@@ -147,13 +164,12 @@ def _a2a_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], g
     return out
 
 
-def ep_exchange_counts(expert_offsets: torch.Tensor, ep: int, E_loc: int, group) -> tuple[list[int], list[int]]:
-    """Per-destination row counts of this rank's sorted rows, and what every peer sends us.
+def ep_exchange_counts(send_offsets: torch.Tensor, group) -> tuple[list[int], list[int]]:
+    """Per-destination record counts of this rank and what every peer sends us.
 
-    The only host synchronisation of the EP layer: the split sizes of the row
+    The only host synchronisation of the EP layer: the split sizes of the record
     all-to-alls must be known on the host."""
-    bounds = expert_offsets[torch.arange(0, ep + 1, device=expert_offsets.device) * E_loc]
-    send = (bounds[1:] - bounds[:-1]).to(torch.int64)
+    send = (send_offsets[1:] - send_offsets[:-1]).to(torch.int64)
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)
     both = torch.stack([send, recv]).cpu()
@@ -164,8 +180,8 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
                  backend=None, stage_events=None) -> torch.Tensor:
     """Token -> expert EP forward of the routed FFN for this rank's tokens.
 
-    x_heads [S, H, dh]; probs/idx [H, S, K] from this rank's router (global per-head
-    expert ids); gu/dn: this rank's NVFP4 expert slice (flattened experts
+    x_heads [S, H, dh]; probs/idx [H, S, K] from this rank's router (per-head expert
+    ids); gu/dn: this rank's NVFP4 expert slice (flattened experts
     [rank*E_loc, (rank+1)*E_loc)).  Returns y [S, H, dh] bf16.
     """
     be = backend or CudaBackend()
@@ -177,29 +193,27 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
     if HE % ep:
         raise ValueError(f"H*E ({HE}) must be divisible by ep_size ({ep})")
     E_loc = HE // ep
-    # 1. stable sort of the local routed rows by global expert (grouped by destination rank)
-    gids, ps, offs, inv = be.sort(probs, idx, E)
-    # 2. NVFP4 rows + meta, in sorted order
+    T = H * S
+    # 1. one record per ((head, token), destination rank), grouped by destination
     xq, xsf, xg = be.quant_tokens(x_heads)
-    sxq, sxsf, meta = be.pack(xq, xsf, xg, H, E, E_loc, gids, ps, offs)
-    # 3. counts, then rows
-    send_counts, recv_counts = ep_exchange_counts(offs, ep, E_loc, group)
-    rxq = _a2a_rows(sxq, send_counts, recv_counts, group)
-    rxsf = _a2a_rows(sxsf, send_counts, recv_counts, group)
-    rmeta = _a2a_rows(meta, send_counts, recv_counts, group)
-    # 4. local experts on the received rows (one output row per received row)
-    Rr = rxq.shape[0]
-    LAST_STATS.update(rows_sent=int(sum(send_counts)), rows_received=int(Rr),
-                      bytes_sent=int(sum(send_counts)) * (sxq.shape[1] + sxsf.shape[1] + 16))
-    rg, rexp, rprob = be.unpack(rmeta, E_loc)
-    lg, lps, loffs, linv = be.sort(rprob.view(1, Rr, 1), rexp.view(1, Rr, 1), E_loc)
-    if stage_events is not None:
-        out_rows = be.ffn_rows(rxq, rxsf, rg, lg, lps, loffs, linv, gu, dn, stage_events=stage_events)
-    else:
-        out_rows = be.ffn_rows(rxq, rxsf, rg, lg, lps, loffs, linv, gu, dn)
-    # 5. rows back to their sources; combine in ascending global-expert order
-    back = _a2a_rows(out_rows, recv_counts, send_counts, group)
-    return be.combine(back, S, H, inv, K)
+    dest = be.dest(idx, E, ep)                                           # [T, ep], key h*S + s
+    zeros = torch.zeros(1, T, ep, dtype=torch.float32, device=dest.device)
+    send_key, _, send_offs, send_slot = be.sort(zeros, dest.view(1, T, ep), ep)
+    # 2./3. counts, then records
+    send_counts, recv_counts = ep_exchange_counts(send_offs, group)
+    R_send = int(sum(send_counts))
+    send = be.pack(xq, xsf, xg, H, S, idx, probs, E, ep, send_key, send_offs, R_send)
+    recv = _a2a_rows(send, send_counts, recv_counts, group)
+    R_recv = recv.shape[0]
+    LAST_STATS.update(records_sent=R_send, records_received=R_recv, bytes_sent=R_send * send.shape[1])
+    # 4. local experts on the received records
+    lidx, lprobs = be.unpack(recv, dh, K, E_loc)
+    lg, lps, loffs, linv = be.sort(lprobs.view(1, R_recv, K), lidx.view(1, R_recv, K), E_loc)
+    LAST_STATS.update(rows_received=loffs[-1])     # device scalar: read it after the step, not here
+    out = be.ffn_records(recv, dh, K, lg, lps, loffs, linv, gu, dn, stage_events=stage_events)
+    # 5. per-record partial sums back to their sources; combine in ascending rank order
+    back = _a2a_rows(out, recv_counts, send_counts, group)
+    return be.combine(back, S, H, send_slot, ep)
 
 
 def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None) -> torch.Tensor:

@@ -1,7 +1,8 @@
 """GPU, 2 ranks (needs >= 2 GPUs; skipped otherwise): the expert-parallel MoE module over
-NCCL against the single-GPU module on each rank's own tokens.  Because every routed row's
-output depends only on that row and the combine order is the global expert order in both,
-the outputs must be identical."""
+NCCL against the single-GPU module on each rank's own tokens.  The EP layer sums each
+token's experts per rank (bf16 partial sums) before the source adds the ranks, so the
+outputs agree to that rounding: rel L2 <= 1e-2 (typically ~1e-3); EP runs are
+run-to-run identical."""
 import os
 import socket
 
@@ -52,8 +53,8 @@ def _worker(rank, world, port, q):
         y_1 = full(x)
         torch.cuda.synchronize()
         _lib.check_device_status(dev)
-        q.put((rank, bool(torch.equal(y_ep, y_1)), bool(torch.equal(y_ep, y_ep2)),
-               float((y_ep.float() - y_1.float()).abs().max())))
+        err = float((y_ep.float() - y_1.float()).norm() / y_1.float().norm())
+        q.put((rank, err < 1e-2, bool(torch.equal(y_ep, y_ep2)), err))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -75,4 +76,4 @@ def test_ep_module_matches_single_gpu():
         assert p.exitcode == 0
     for rank, same, repeat, err in res:
         assert repeat, f"rank {rank}: EP output not deterministic"
-        assert same, f"rank {rank}: EP output differs from the single-GPU module (max abs {err})"
+        assert same, f"rank {rank}: EP output differs from the single-GPU module (rel L2 {err})"
