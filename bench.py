@@ -45,10 +45,11 @@ CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, sc
 CFG4 = dict(name="config4", S=256, d=3072, H=1, E=128, K=8, de=1024, seed=4, score_func="softmax", layers=4)
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
 # libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, token quantise,
-# row grouping, gate/up GEMM, down GEMM, combine.  EP adds pack, unpack, the receiver's sort x4
-# and the source-side combine.
+# row grouping, gate/up GEMM, down GEMM, combine.  EP (records arrive quantised): router,
+# token quantise, destination mask, send sort x4, pack, unpack, receiver sort x4, tile tables,
+# pad map, row grouping, gate/up GEMM, down GEMM, per-record combine, source-side combine.
 KERNELS_PER_STEP = 12
-KERNELS_PER_STEP_EP = 19
+KERNELS_PER_STEP_EP = 20
 CPU_SAMPLE_TOKENS = 512
 
 
@@ -253,7 +254,31 @@ def run_ours(args, world, rank, local):
     e2e_ms = float("nan")
     if not args.no_e2e:
         e2e_ms = _e2e(args, m, x_host, dev, world)
-    return _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host)
+    out = _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host)
+    if world == 1 and args.config == 1 and not args.tokens:
+        out["weak_scaling_base"] = _one_gpu_config3(args, m, x)
+    return out
+
+
+def _one_gpu_config3(args, m, x):
+    """Config 3's per-GPU shape (8192 tokens, all 128 experts local) on this one GPU: the
+    N=1 point of the expert-parallel weak-scaling series (N>1 runs config 3)."""
+    import torch
+    S3 = CFG3["S"]
+    xs = x[:S3].contiguous()
+    for _ in range(args.warmup):
+        step_explicit(m, xs, [torch.cuda.Event(enable_timing=True) for _ in range(7)])
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for k in range(args.steps):
+        step_explicit(m, xs, evs[k])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    return {"workload": f"config3 per-GPU shape on 1 GPU: {S3} tokens, E=128 local", "value": round(S3 / (ms * 1e-3), 1),
+            "unit": "tokens/s", "ms_per_step": round(ms, 4)}
 
 
 def _e2e(args, m, x_host, dev, world):

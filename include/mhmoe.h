@@ -231,6 +231,20 @@ MHMOE_API int mhmoe_gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, i
                          const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out,
                          int* dev_status, uint64_t timeout_ns, void* stream);
 
+/* ───────────────────────── failure detection ───────────────────────── */
+
+/* Self test of the bounded device waits (no counterpart in the reference).  Every
+ * kernel here waits only with a time limit: on expiry it records MHMOE_ERR_TIMEOUT in
+ * dev_status, finishes its copies in flight, frees its tensor memory and returns, so
+ * the CUDA context stays usable.  This entry runs those waits against conditions that
+ * never complete: mode bit 0 waits on a shared-memory barrier nothing arrives on, bit 1
+ * waits for the int at `flag` to reach `expected` (flag may be NULL when bit 1 is
+ * clear).  Each wait gives up after timeout_ns (must be 1 us .. 10 s).  elapsed_ns
+ * (device, may be NULL) receives the total time waited.  Asynchronous: read dev_status
+ * after synchronising the stream. */
+MHMOE_API int mhmoe_wait_selftest(const int* flag, int expected, int mode, uint64_t timeout_ns, int* dev_status,
+                                  int64_t* elapsed_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -349,4 +349,14 @@ int mhmoe_gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, int n_mtile
   return rc;
 }
 
+int mhmoe_wait_selftest(const int* flag, int expected, int mode, uint64_t timeout_ns, int* dev_status,
+                        int64_t* elapsed_ns, void* stream) {
+  MHMOE_REQUIRE(dev_status && mode >= 0 && mode <= 3 && (!(mode & 2) || flag));
+  MHMOE_REQUIRE(timeout_ns >= 1000ull && timeout_ns <= 10000000000ull);
+  MHMOE_CHECK_ARCH();
+  const cudaError_t e = launch_wait_selftest(flag, expected, mode, timeout_ns, dev_status, elapsed_ns,
+                                             static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "wait_selftest");
+}
+
 }  // extern "C"

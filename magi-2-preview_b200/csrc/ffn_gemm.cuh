@@ -149,14 +149,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ───────── producer (whole warp waits; lane 0 issues the TMA / bulk copies) ─────────
     int stage = 0;
     uint32_t phase = 0;
+    int64_t issued = 0;
+    bool ok = true;
     const size_t k_atoms = (size_t)(p.K / 64);
     const size_t sfb_expert_bytes = (size_t)p.N * (size_t)(p.K / 16);
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
       const int e = p.tile_expert[mt];
       const int brow = e * p.N + nt * GEMM_BN;
       for (int kb = 0; kb < n_kblk; ++kb) {
-        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) {
+          ok = false;
+          break;
+        }
         if (lane == 0) {
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, GEMM_STAGE_TX);
@@ -172,9 +177,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
         __syncwarp();
+        ++issued;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
+    // Every copy this CTA issued lands before it can exit.  Loads older than the last
+    // STAGES were consumed already; on the normal path the last ones were too, so these
+    // waits return at once — they matter when a consumer gave up on an error.
+    for (int64_t i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
+      mbar_wait(smem_u32(&full_bar[i % STAGES]), (uint32_t)((i / STAGES) & 1), nullptr, 0, MHMOE_DRAIN_NS);
   } else if (warp == 1) {
     // ───────── MMA issuer (whole warp waits; lane 0 issues) ─────────
     int stage = 0;
@@ -314,7 +325,7 @@ done:
     // Retire every tcgen05 op this thread issued before TMEM is released
     // (matters only on an error path; on the normal path they are done already).
     tc_commit(smem_u32(drain_bar));
-    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, timeout);
+    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
   tc_fence_before();
   __syncthreads();

@@ -89,6 +89,10 @@ cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataTy
                            uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
                            uint32_t box_rows);
 
+// wait_selftest.cu
+cudaError_t launch_wait_selftest(const int* flag, int expected, int mode, uint64_t timeout_ns, int* status,
+                                 int64_t* elapsed_ns, cudaStream_t st);
+
 // router_tc.cu
 cudaError_t launch_split_gate(const float* gate, int64_t HE, int dh, int nsplit, __nv_bfloat16* out, int* flags,
                               cudaStream_t st);

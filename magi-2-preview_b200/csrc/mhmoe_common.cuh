@@ -97,6 +97,30 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Limit for the waits of an exit path (copies in flight, issued tcgen05 ops): these always
+// complete, so the limit only bounds a hardware stall; it is independent of the caller's
+// (possibly tiny) timeout.
+constexpr uint64_t MHMOE_DRAIN_NS = 2000000000ull;
+
+// Bounded wait for a global flag written by another agent (kernel, peer, host) to reach
+// `expected` or more.  Same contract as mbar_wait.
+__device__ __forceinline__ bool flag_wait_geq(const int* flag, int expected, int* err, int code,
+                                              uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= expected) return true;
+    if ((i & 63u) == 63u) {
+      if (err && ld_volatile_i32(err) != 0) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        record_error(err, code);
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -15,7 +15,8 @@
 // K' = nsplit * dh, iterated as (dh block of 64, plane) so each x tile is re-read from L2
 // right after its first load.  Warp 0: TMA producer (x tile 128x64 bf16, gate tile
 // Nx64 bf16, 128-B swizzle, 4 stages); warp 1: TMEM owner + MMA issuer
-// (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-5: epilogue, one token row per thread.
+// (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-5: epilogue, one token row per thread,
+// top-k kept in registers by branch-free insertion (8 entries for K <= 8, else 16).
 #include <mutex>
 
 #include "kernels.cuh"
@@ -27,7 +28,6 @@ constexpr int RT_BK = 64;                // bf16 elements per stage row (128 B)
 constexpr int RT_MAX_STAGES = 4;
 constexpr int RT_SCRATCH_BYTES = 2 * 32 * 128 * 4;
 constexpr int RT_THREADS = 192;
-constexpr int RT_MAXK = 16;
 
 struct RouterParams {
   const float* logit_bias; // [H*E] or null: added to the logits before scoring
@@ -41,31 +41,28 @@ struct RouterParams {
   uint64_t timeout_ns;
 };
 
-// Insert (v, e, sc) into the descending list tv[0..K) (ties keep the earlier, lower
-// index first).  All indices are compile-time after unrolling, so the lists stay in
-// registers; `thr` caches tv[K-1] so most candidates are rejected by one compare.
-__device__ __forceinline__ void topk_insert(float v, int e, float sc, float* tv, int* ti, float* ts, int K,
-                                            float& thr) {
-  if (!(v > thr)) return;
+// Insert (v, e, sc) into the descending list tv[0..KM) without branches: every entry
+// takes its new value by selects, so lanes never diverge.  v enters above an entry only
+// when strictly larger, and values arrive in ascending expert order, so equal values keep
+// the lower expert first.  NaN and -inf never enter.
+template <int KM>
+__device__ __forceinline__ void topk_insert(float v, int e, float sc, float (&tv)[KM], int (&ti)[KM],
+                                            float (&ts)[KM]) {
 #pragma unroll
-  for (int j = RT_MAXK - 1; j >= 0; --j) {
-    if (j < K) {
-      if (j > 0 && v > tv[j > 0 ? j - 1 : 0]) {
-        tv[j] = tv[j > 0 ? j - 1 : 0];
-        ti[j] = ti[j > 0 ? j - 1 : 0];
-        ts[j] = ts[j > 0 ? j - 1 : 0];
-      } else if (v > tv[j]) {
-        tv[j] = v;
-        ti[j] = e;
-        ts[j] = sc;
-      }
-    }
+  for (int j = KM - 1; j >= 1; --j) {
+    const bool above_prev = v > tv[j - 1];
+    const bool above_cur = v > tv[j];
+    tv[j] = above_prev ? tv[j - 1] : (above_cur ? v : tv[j]);
+    ti[j] = above_prev ? ti[j - 1] : (above_cur ? e : ti[j]);
+    ts[j] = above_prev ? ts[j - 1] : (above_cur ? sc : ts[j]);
   }
-#pragma unroll
-  for (int j = 0; j < RT_MAXK; ++j)
-    if (j == K - 1) thr = tv[j];
+  const bool top = v > tv[0];
+  tv[0] = top ? v : tv[0];
+  ti[0] = top ? e : ti[0];
+  ts[0] = top ? sc : ts[0];
 }
 
+template <int KM>
 __global__ void __launch_bounds__(RT_THREADS, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
                      const RouterParams p) {
@@ -118,11 +115,16 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
     // producer: the whole warp loops and waits, lane 0 issues
     int stage = 0;
     uint32_t phase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+    int64_t issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
       const int h = t / mtiles, mt = t % mtiles;
       for (int k = 0; k < nk; ++k) {
         const int kb = k / p.nsplit, sp = k % p.nsplit;
-        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) {
+          ok = false;
+          break;
+        }
         if (lane == 0) {
           const uint32_t fb = smem_u32(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, (uint32_t)(a_bytes + b_bytes));
@@ -130,9 +132,13 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           tma_load_2d(smem_u32(sB + stage * b_bytes), &tmG, fb, (kb * p.nsplit + sp) * RT_BK, h * p.E);
         }
         __syncwarp();
+        ++issued;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
+    // every load issued lands before the CTA exits (returns at once on the normal path)
+    for (int64_t i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
+      mbar_wait(smem_u32(&full_bar[i % STAGES]), (uint32_t)((i / STAGES) & 1), nullptr, 0, MHMOE_DRAIN_NS);
   } else if (warp == 1) {
     // MMA issuer: the whole warp loops and waits, lane 0 issues
     int stage = 0;
@@ -161,19 +167,23 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       acc_phase ^= 1;
     }
   } else {
+    // epilogue: one token row per thread (TMEM lane = row)
     const int q = warp & 3;
     const int m = q * 32 + lane;
+    const int nchunk = p.Npad / 32 + (p.Npad % 32 ? 1 : 0);
+    float* sv = scratch + (threadIdx.x - 64);          // [32][128] selection values of this thread
+    float* ss = sv + 32 * 128;                          // [32][128] unbiased scores
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int h = t / mtiles, mt = t % mtiles;
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
       const int s = mt * RT_BM + m;
       const bool valid = s < p.S;
       const int64_t row = (int64_t)h * p.S + s;
-      const int nchunk = p.Npad / 32 + (p.Npad % 32 ? 1 : 0);
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+      const float* lb = p.logit_bias ? p.logit_bias + (int64_t)h * p.E : nullptr;
       uint32_t r[32];
       // pass 1: max (softmax) and optional logits output
       float mx = -INFINITY;
@@ -184,13 +194,13 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         for (int i = 0; i < 32; ++i) {
           const int e = c * 32 + i;
           if (e < p.E) {
-            const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
-                                         : __uint_as_float(r[i]);
+            const float l = lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i]);
             mx = fmaxf(mx, l);
             if (valid && p.logits) p.logits[row * p.E + e] = l;
           }
         }
       }
+      // pass 2: softmax denominator (ascending expert order)
       float sum = 0.f;
       if (p.score_func == 0) {
         for (int c = 0; c < nchunk; ++c) {
@@ -199,50 +209,37 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int e = c * 32 + i;
-            if (e < p.E) {
-              const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
-                                           : __uint_as_float(r[i]);
-              sum += expf(l - mx);
-            }
+            if (e < p.E) sum += expf((lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i])) - mx);
           }
         }
       }
-      float tv[RT_MAXK], ts[RT_MAXK], thr = -INFINITY;
-      int ti[RT_MAXK];
+      // pass 3: scores of a 32-column chunk go to this thread's column of the shared
+      // scratch, then a compact loop inserts them into the top-KM list (branch-free).
+      float tv[KM], ts[KM];
+      int ti[KM];
 #pragma unroll
-      for (int j = 0; j < RT_MAXK; ++j) {
+      for (int j = 0; j < KM; ++j) {
         tv[j] = -INFINITY;
         ts[j] = 0.f;
         ti[j] = 0;
       }
-      // pass 3: scores of a 32-column chunk go to this thread's column of the shared
-      // scratch (unrolled, cheap), then only candidates above the running k-th value are
-      // inserted, through one non-unrolled loop (keeps the code small).
-      float* sv = scratch + (threadIdx.x - 64);          // [32][128] selection values
-      float* ss = sv + 32 * 128;                          // [32][128] unbiased scores
       for (int c = 0; c < nchunk; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
-        uint32_t cand = 0;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int e = c * 32 + i;
           float v = -INFINITY, sc = 0.f;
           if (e < p.E) {
-            const float l = p.logit_bias ? __fadd_rn(__uint_as_float(r[i]), p.logit_bias[(int64_t)h * p.E + e])
-                                         : __uint_as_float(r[i]);
+            const float l = lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i]);
             sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
             v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
           }
           sv[i * 128] = v;
           ss[i * 128] = sc;
-          cand |= (v > thr ? 1u : 0u) << i;
         }
-        while (cand) {
-          const int i = __ffs(cand) - 1;
-          cand &= cand - 1;
-          topk_insert(sv[i * 128], c * 32 + i, ss[i * 128], tv, ti, ts, p.K, thr);
-        }
+#pragma unroll 2
+        for (int i = 0; i < 32; ++i) topk_insert<KM>(sv[i * 128], c * 32 + i, ss[i * 128], tv, ti, ts);
       }
       tc_fence_before();
       __syncwarp();
@@ -252,12 +249,12 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         if (p.route_norm) {
           float a = 0.f;
 #pragma unroll
-          for (int j = 0; j < RT_MAXK; ++j)
+          for (int j = 0; j < KM; ++j)
             if (j < p.K) a += fabsf(ts[j]);
           nrm = fmaxf(a, p.norm_eps);
         }
 #pragma unroll
-        for (int j = 0; j < RT_MAXK; ++j) {
+        for (int j = 0; j < KM; ++j) {
           if (j < p.K) {
             const float pr = p.route_norm ? __fdiv_rn(ts[j], nrm) : ts[j];
             p.probs[row * p.K + j] = __fmul_rn(pr, p.route_scale);
@@ -270,7 +267,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
 done:
   if (warp == 1 && lane == 0) {
     tc_commit(smem_u32(drain_bar));
-    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, timeout);
+    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
   tc_fence_before();
   __syncthreads();
@@ -351,10 +348,14 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   const int fixed = 256 + RT_SCRATCH_BYTES + 1024;
   p.stages = std::min(RT_MAX_STAGES, (227 * 1024 - fixed) / stage_bytes);
   const int smem = p.stages * stage_bytes + fixed;
+  // top-K lists of 8 entries cover K <= 8; 16 entries otherwise (K <= 16)
+  auto kernel = K <= 8 ? router_tc_kernel<8> : router_tc_kernel<16>;
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = cudaFuncSetAttribute(router_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (attr == cudaSuccess)
+      attr = cudaFuncSetAttribute(router_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   });
   if (attr != cudaSuccess) {
     *cerr = attr;
@@ -362,7 +363,7 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   }
   const int tiles = ((S + RT_BM - 1) / RT_BM) * H;
   const int grid = std::max(1, std::min(tiles, num_sms()));
-  router_tc_kernel<<<grid, RT_THREADS, smem, st>>>(tx, tg, p);
+  kernel<<<grid, RT_THREADS, smem, st>>>(tx, tg, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     *cerr = e;

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_ep_unpack": (i32, [vp, i64, i32, i32, i32, vp, vp, vp, vp]),
     "mhmoe_quantize_rows_nvfp4": (i32, [vp, i64, i64, i32, vp, vp, vp, vp]),
     "mhmoe_gemm_nvfp4_raw": (i32, [vp, vp, i32, vp, vp, vp, i32, i32, i32, vp, vp, u64, vp]),
+    "mhmoe_wait_selftest": (i32, [vp, i32, i32, u64, vp, vp, vp]),
 }
 
 _lib = None
