@@ -182,7 +182,8 @@ def step_ep(m, x, ev):
     probs, idx = m._route(x_heads)
     ev[1].record()
     gu, dn = m.packed_weights()
-    y = ep_moe_layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7])
+    y = ep_moe_layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7],
+                     comm_events=ev[8:12])
     ev[7].record()
     return y
 
@@ -209,7 +210,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.empty_cache()
     torch.cuda.synchronize()
 
-    nev = 7 if world == 1 else 8
+    nev = 7 if world == 1 else 12
     step = step_explicit if world == 1 else step_ep
     for _ in range(args.warmup):
         step(m, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
@@ -248,7 +249,7 @@ def run_ours(args, world, rank, local):
     else:
         stages = {"route_ms": avg(0, 1), "dispatch_ms": avg(1, 2), "quant_tables_ms": avg(2, 3),
                   "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "local_combine_ms": avg(5, 6),
-                  "return_combine_ms": avg(6, 7)}
+                  "return_combine_ms": avg(6, 7), "a2a_records_ms": avg(8, 9), "a2a_return_ms": avg(10, 11)}
 
     # end-to-end through the public module API, host buffers, copies inside the timed region
     e2e_ms = float("nan")
@@ -356,6 +357,16 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "gpu_launches": (KERNELS_PER_STEP if world == 1 else KERNELS_PER_STEP_EP) * args.steps,   # kernels of libmhmoe inside the device-timed region
         "clocks": clk.summary(),
     }
+    if world > 1:
+        from flash_mh_moe.ep import LAST_STATS
+        bd, br = LAST_STATS.get("dispatch_remote_bytes", 0), LAST_STATS.get("return_remote_bytes", 0)
+        td, tr = stages["a2a_records_ms"], stages["a2a_return_ms"]
+        out["nvlink"] = {"records_remote_bytes": bd, "return_remote_bytes": br,
+                         "records_GBps": round(bd / (td * 1e-3) / 1e9, 1) if td > 0 else None,
+                         "return_GBps": round(br / (tr * 1e-3) / 1e9, 1) if tr > 0 else None,
+                         "peak": 770.0, "unit": "GB/s per direction per GPU",
+                         "note": "rank 0: bytes it sends to other ranks / device time of that all-to-all "
+                                 "(NCCL; includes waiting for the slowest peer); peak = measured peer copy"}
     if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == 1:
         out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
     return out

@@ -177,12 +177,14 @@ def ep_exchange_counts(send_offsets: torch.Tensor, group) -> tuple[list[int], li
 
 
 def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn, group,
-                 backend=None, stage_events=None) -> torch.Tensor:
+                 backend=None, stage_events=None, comm_events=None) -> torch.Tensor:
     """Token -> expert EP forward of the routed FFN for this rank's tokens.
 
     x_heads [S, H, dh]; probs/idx [H, S, K] from this rank's router (per-head expert
     ids); gu/dn: this rank's NVFP4 expert slice (flattened experts
     [rank*E_loc, (rank+1)*E_loc)).  Returns y [S, H, dh] bf16.
+    comm_events: optional 4 CUDA events recorded before/after the record all-to-all and
+    before/after the return all-to-all (for link-bandwidth measurement).
     """
     be = backend or CudaBackend()
     ep = dist.get_world_size(group)
@@ -203,16 +205,29 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
     send_counts, recv_counts = ep_exchange_counts(send_offs, group)
     R_send = int(sum(send_counts))
     send = be.pack(xq, xsf, xg, H, S, idx, probs, E, ep, send_key, send_offs, R_send)
+    if comm_events:
+        comm_events[0].record()
     recv = _a2a_rows(send, send_counts, recv_counts, group)
+    if comm_events:
+        comm_events[1].record()
     R_recv = recv.shape[0]
-    LAST_STATS.update(records_sent=R_send, records_received=R_recv, bytes_sent=R_send * send.shape[1])
+    me = dist.get_rank(group)
+    remote_out = R_send - send_counts[me]
+    remote_in = R_recv - recv_counts[me]
+    LAST_STATS.update(records_sent=R_send, records_received=R_recv, bytes_sent=R_send * send.shape[1],
+                      dispatch_remote_bytes=remote_out * send.shape[1],
+                      return_remote_bytes=remote_in * dh * 2)
     # 4. local experts on the received records
     lidx, lprobs = be.unpack(recv, dh, K, E_loc)
     lg, lps, loffs, linv = be.sort(lprobs.view(1, R_recv, K), lidx.view(1, R_recv, K), E_loc)
     LAST_STATS.update(rows_received=loffs[-1])     # device scalar: read it after the step, not here
     out = be.ffn_records(recv, dh, K, lg, lps, loffs, linv, gu, dn, stage_events=stage_events)
     # 5. per-record partial sums back to their sources; combine in ascending rank order
+    if comm_events:
+        comm_events[2].record()
     back = _a2a_rows(out, recv_counts, send_counts, group)
+    if comm_events:
+        comm_events[3].record()
     return be.combine(back, S, H, send_slot, ep)
 
 
