@@ -176,14 +176,14 @@ def step_explicit(m, x, ev):
 
 def step_ep(m, x, ev):
     """The expert-parallel module forward spelled out, with events between the stages."""
-    from flash_mh_moe.ep import ep_moe_layer
+    from flash_mh_moe.ep import ep_moe_layer, ep_moe_layer_peer, ep_transport
     x_heads = x.view(-1, m.num_heads, m.d_head)
     ev[0].record()
     probs, idx = m._route(x_heads)
     ev[1].record()
     gu, dn = m.packed_weights()
-    y = ep_moe_layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7],
-                     comm_events=ev[8:12])
+    layer = ep_moe_layer_peer if ep_transport(m) == "peer" else ep_moe_layer
+    y = layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7], comm_events=ev[8:12])
     ev[7].record()
     return y
 
@@ -359,14 +359,22 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
     }
     if world > 1:
         from flash_mh_moe.ep import LAST_STATS
-        bd, br = LAST_STATS.get("dispatch_remote_bytes", 0), LAST_STATS.get("return_remote_bytes", 0)
-        td, tr = stages["a2a_records_ms"], stages["a2a_return_ms"]
-        out["nvlink"] = {"records_remote_bytes": bd, "return_remote_bytes": br,
-                         "records_GBps": round(bd / (td * 1e-3) / 1e9, 1) if td > 0 else None,
-                         "return_GBps": round(br / (tr * 1e-3) / 1e9, 1) if tr > 0 else None,
-                         "peak": 770.0, "unit": "GB/s per direction per GPU",
-                         "note": "rank 0: bytes it sends to other ranks / device time of that all-to-all "
-                                 "(NCCL; includes waiting for the slowest peer); peak = measured peer copy"}
+        out["config"]["parallelism"] = (f"ep{world} (token->expert records, "
+                                        + ("fused NVLink peer stores)" if LAST_STATS.get("transport") == "peer"
+                                           else "NCCL all-to-all)"))
+        if LAST_STATS.get("transport") == "nccl":
+            bd, br = LAST_STATS.get("dispatch_remote_bytes", 0), LAST_STATS.get("return_remote_bytes", 0)
+            td, tr = stages["a2a_records_ms"], stages["a2a_return_ms"]
+            out["nvlink"] = {"records_remote_bytes": bd, "return_remote_bytes": br,
+                             "records_GBps": round(bd / (td * 1e-3) / 1e9, 1) if td > 0 else None,
+                             "return_GBps": round(br / (tr * 1e-3) / 1e9, 1) if tr > 0 else None,
+                             "peak": 770.0, "unit": "GB/s per direction per GPU",
+                             "note": "rank 0: bytes it sends to other ranks / device time of that all-to-all "
+                                     "(NCCL; includes waiting for the slowest peer); peak = measured peer copy"}
+        else:
+            out["nvlink"] = {"note": "records are stored to peers by the send kernel and sums by the receiver's "
+                                     "combine (fused); a2a_records_ms = send kernel + wait for every source, "
+                                     "a2a_return_ms = wait for the returns after this rank's own combine"}
     if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == 1:
         out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
     return out

@@ -231,6 +231,64 @@ MHMOE_API int mhmoe_gemm_nvfp4_raw(const uint8_t* a_data, const uint8_t* a_sf, i
                          const uint8_t* b_data, const uint8_t* b_sf, int n_experts, int N, int K, float* out,
                          int* dev_status, uint64_t timeout_ns, void* stream);
 
+/* ─────────────── expert-parallel exchange over peer memory ───────────────
+ * Replaces the two all_to_all_single calls of ep_dispatch / ep_undispatch
+ * (inference/model/magi2_preview.py:3277-3327) for ranks on the GPUs of one node: the
+ * record and return kernels store straight into the destination rank's buffer (mapped
+ * with CUDA IPC; plain NVLink stores, no multicast) and raise per-source arrival
+ * counters there; no host synchronisation.  One buffer per rank, same layout on all:
+ * flags, meta, rx records [n][cap][mhmoe_ep_row_bytes] and a return area
+ * [n*cap][dh] bf16.  cap >= H*S (rows per rank).  Every call of one layer step passes
+ * the same epoch, 1 for the first step and +1 per step, identically on all ranks. */
+
+/* Bytes of the per-rank buffer (0 on bad arguments). */
+MHMOE_API size_t mhmoe_ep_sym_bytes(int n_ranks, int64_t cap, int dh, int K);
+
+/* Byte offsets of the buffer's parts: out[5] = {flags, meta, rx, back, total}. */
+MHMOE_API int mhmoe_ep_sym_offsets(int n_ranks, int64_t cap, int dh, int K, int64_t* out);
+
+/* Allocate and zero a buffer on the current device and export it: ipc_handle receives
+ * the 64-byte CUDA IPC handle the other ranks open. */
+MHMOE_API int mhmoe_ep_sym_alloc(size_t bytes, void** ptr, void* ipc_handle);
+
+/* Map another rank's buffer from its 64-byte handle (peer access enabled lazily). */
+MHMOE_API int mhmoe_ep_sym_open(const void* ipc_handle, void** peer_ptr);
+MHMOE_API int mhmoe_ep_sym_close(void* peer_ptr);
+MHMOE_API int mhmoe_ep_sym_free(void* ptr);
+
+/* Source side: one record per send row (send_key / send_offsets from mhmoe_global_sort
+ * of mhmoe_ep_dest's mask, grouped by destination) stored into destination d's rx at
+ * slot rank*cap + (row - send_offsets[d]); then {count, send_offsets[d]} into d's meta
+ * and d's records flag for this rank raised.  peer_bases: host array of n_ranks buffer
+ * pointers as mapped on this device (this rank's own at [rank]). */
+MHMOE_API int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                                    const int64_t* topk_idx, const float* topk_probs, int K, int E,
+                                    const int32_t* send_key, const int64_t* send_offsets, int n_ranks, int rank,
+                                    int64_t cap, void* const* peer_bases, int* dev_status, void* stream);
+
+/* Wait on the device until every source's flag of `kind` (0 records, 1 returns) in this
+ * rank's buffer reaches `epoch`; gives up after timeout_ns with MHMOE_ERR_PEER in
+ * dev_status.  Later work on the stream runs after it. */
+MHMOE_API int mhmoe_ep_wait(const void* local_base, int kind, int n_ranks, int epoch, uint64_t timeout_ns,
+                            int* dev_status, void* stream);
+
+/* Receiver: rx slot i -> local expert ids int64 [n_ranks*cap, K] and probs, -1 / 0 for
+ * unused pairs and for slots past the source's count. */
+MHMOE_API int mhmoe_ep_unpack_slots(const void* local_base, int n_ranks, int64_t cap, int dh, int K, int E_loc,
+                                    int64_t* local_expert, float* probs, int* dev_status, void* stream);
+
+/* Receiver: the expert FFN over the rx records in place (as mhmoe_ffn_nvfp4_quantized,
+ * R = n_ranks*cap*K entries from the sort of mhmoe_ep_unpack_slots' output), whose
+ * combine stores each record's bf16 expert sum into the source rank's return area at
+ * row (source's send position) and raises the source's return flag for this rank. */
+MHMOE_API int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K,
+                                  int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                                  const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                                  const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
+                                  const float* dn_gscale, const int32_t* row_of_flat, void* workspace,
+                                  void* const* peer_bases, int* dev_status, uint64_t timeout_ns,
+                                  void* const* stage_events, void* stream);
+
 /* ───────────────────────── failure detection ───────────────────────── */
 
 /* Self test of the bounded device waits (no counterpart in the reference).  Every

@@ -359,4 +359,144 @@ int mhmoe_wait_selftest(const int* flag, int expected, int mode, uint64_t timeou
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "wait_selftest");
 }
 
+/* ───────── expert-parallel exchange over peer memory ───────── */
+
+size_t mhmoe_ep_sym_bytes(int n_ranks, int64_t cap, int dh, int K) {
+  if (n_ranks <= 0 || n_ranks > EP_MAX_RANKS || cap < 0 || dh <= 0 || K <= 0) return 0;
+  return (size_t)ep_layout(n_ranks, cap, dh, ep_row_bytes(dh, K)).bytes;
+}
+
+int mhmoe_ep_sym_offsets(int n_ranks, int64_t cap, int dh, int K, int64_t* out) {
+  MHMOE_REQUIRE(out && n_ranks > 0 && n_ranks <= EP_MAX_RANKS && cap >= 0 && dh > 0 && K > 0);
+  const EpLayout L = ep_layout(n_ranks, cap, dh, ep_row_bytes(dh, K));
+  out[0] = L.off_flags;
+  out[1] = L.off_meta;
+  out[2] = L.off_rx;
+  out[3] = L.off_back;
+  out[4] = L.bytes;
+  return MHMOE_OK;
+}
+
+int mhmoe_ep_sym_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  MHMOE_REQUIRE(ptr && ipc_handle && bytes > 0);
+  MHMOE_CHECK_ARCH();
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail_cuda(e, "ep_sym_alloc (cudaMalloc)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail_cuda(e, "ep_sym_alloc (ipc handle)");
+  }
+  *ptr = p;
+  return MHMOE_OK;
+}
+
+int mhmoe_ep_sym_open(const void* ipc_handle, void** peer_ptr) {
+  MHMOE_REQUIRE(ipc_handle && peer_ptr);
+  MHMOE_CHECK_ARCH();
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_sym_open (cudaIpcOpenMemHandle)");
+}
+
+int mhmoe_ep_sym_close(void* peer_ptr) {
+  MHMOE_REQUIRE(peer_ptr);
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_sym_close");
+}
+
+int mhmoe_ep_sym_free(void* ptr) {
+  MHMOE_REQUIRE(ptr);
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_sym_free");
+}
+
+static bool fill_peers(void* const* peer_bases, int n, EpPeers* peers) {
+  for (int d = 0; d < EP_MAX_RANKS; ++d) peers->base[d] = nullptr;
+  for (int d = 0; d < n; ++d) {
+    if (!peer_bases[d] || !aligned16(peer_bases[d])) return false;
+    peers->base[d] = static_cast<uint8_t*>(peer_bases[d]);
+  }
+  return true;
+}
+
+int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                          const int64_t* idx, const float* probs, int K, int E, const int32_t* send_key,
+                          const int64_t* send_offsets, int n_ranks, int rank, int64_t cap, void* const* peer_bases,
+                          int* dev_status, void* stream) {
+  MHMOE_REQUIRE(xq && xsf && xg && idx && probs && send_key && send_offsets && peer_bases && dev_status);
+  MHMOE_REQUIRE(H > 0 && S >= 0 && dh > 0 && dh % 256 == 0 && K > 0 && K <= 16 && E > 0);
+  MHMOE_REQUIRE(n_ranks > 0 && n_ranks <= EP_MAX_RANKS && rank >= 0 && rank < n_ranks && (H * E) % n_ranks == 0);
+  MHMOE_REQUIRE(cap >= (int64_t)H * S);
+  MHMOE_CHECK_ARCH();
+  EpPeers peers;
+  MHMOE_REQUIRE(fill_peers(peer_bases, n_ranks, &peers));
+  const cudaError_t e = launch_ep_send_records(xq, xsf, xg, H, S, dh, idx, probs, K, E, H * E / n_ranks, send_key,
+                                               send_offsets, n_ranks, rank, cap, peers, peers.base[rank], dev_status,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_send_records");
+}
+
+int mhmoe_ep_wait(const void* local_base, int kind, int n_ranks, int epoch, uint64_t timeout_ns, int* dev_status,
+                  void* stream) {
+  MHMOE_REQUIRE(local_base && dev_status && (kind == 0 || kind == 1) && n_ranks > 0 && n_ranks <= EP_MAX_RANKS);
+  MHMOE_REQUIRE(epoch > 0 && timeout_ns >= 1000ull && timeout_ns <= 600000000000ull);
+  MHMOE_CHECK_ARCH();
+  const cudaError_t e = launch_ep_wait(static_cast<const uint8_t*>(local_base), kind, n_ranks, epoch, timeout_ns,
+                                       dev_status, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_wait");
+}
+
+int mhmoe_ep_unpack_slots(const void* local_base, int n_ranks, int64_t cap, int dh, int K, int E_loc,
+                          int64_t* local_expert, float* probs, int* dev_status, void* stream) {
+  MHMOE_REQUIRE(local_base && local_expert && probs && dev_status && n_ranks > 0 && n_ranks <= EP_MAX_RANKS);
+  MHMOE_REQUIRE(cap >= 0 && dh > 0 && dh % 256 == 0 && K > 0 && K <= 16 && E_loc > 0);
+  MHMOE_CHECK_ARCH();
+  if ((int64_t)n_ranks * cap == 0) return MHMOE_OK;
+  const cudaError_t e = launch_ep_unpack_slots(static_cast<const uint8_t*>(local_base), n_ranks, cap, dh, K, E_loc,
+                                               local_expert, probs, dev_status, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_unpack_slots");
+}
+
+int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K, int E_loc,
+                        int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                        const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                        const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                        const int32_t* row_of_flat, void* workspace, void* const* peer_bases, int* dev_status,
+                        uint64_t timeout_ns, void* const* stage_events, void* stream) {
+  MHMOE_REQUIRE(local_base && gather_ids && probs_sorted && expert_offsets && gu_data && gu_sf && gu_gscale &&
+                dn_data && dn_sf && dn_gscale && row_of_flat && workspace && peer_bases && dev_status);
+  MHMOE_REQUIRE(n_ranks > 0 && n_ranks <= EP_MAX_RANKS && rank >= 0 && rank < n_ranks && cap > 0);
+  MHMOE_REQUIRE(dh > 0 && dh % 256 == 0 && de > 0 && de % 256 == 0 && K > 0 && K <= 16 && E_loc > 0);
+  MHMOE_REQUIRE(R == (int64_t)n_ranks * cap * K);
+  MHMOE_CHECK_ARCH();
+  EpPeers peers;
+  MHMOE_REQUIRE(fill_peers(peer_bases, n_ranks, &peers));
+  MHMOE_REQUIRE(peers.base[rank] == local_base);
+  const int64_t rb = ep_row_bytes(dh, K);
+  EpReturn ret;
+  ret.peers = peers;
+  ret.local = static_cast<uint8_t*>(const_cast<void*>(local_base));
+  ret.layout = ep_layout(n_ranks, cap, dh, rb);
+  ret.cap = cap;
+  ret.n = n_ranks;
+  ret.me = rank;
+  ret.status = dev_status;
+  const uint8_t* rx = ret.local + ret.layout.off_rx;
+  const int64_t T = (int64_t)n_ranks * cap;
+  MHMOE_REQUIRE(T <= 0x7fffffff);
+  cudaError_t ce = cudaSuccess;
+  const int rc = ffn_nvfp4(nullptr, 0, 0, (int)T, 1, dh, de, E_loc, R, gather_ids, probs_sorted, expert_offsets,
+                           gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, row_of_flat, nullptr, K, workspace,
+                           nullptr, dh, dh, dev_status, timeout_ns,
+                           reinterpret_cast<cudaEvent_t const*>(stage_events), static_cast<cudaStream_t>(stream), &ce,
+                           rx, rx + dh / 2, rx + dh / 2 + dh / 16, rb, rb, rb, &ret);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ep_ffn_return");
+  if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
+  return rc;
+}
+
 }  // extern "C"

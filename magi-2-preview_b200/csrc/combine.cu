@@ -21,28 +21,13 @@ __global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const 
   if (m < tile_rows[mt]) pad_of_row[tile_row0[mt] + m] = mt * 128 + m;
 }
 
-__global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row, int dh,
-                               int S, int H,
-                               const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
-                               int k_fixed, int64_t R, int64_t P_rows, __nv_bfloat16* __restrict__ y, int64_t sy_s,
-                               int64_t sy_h) {
-  __shared__ int srt[COMBINE_WARPS][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
-  if (key >= (int64_t)H * S) return;
-  const int h = (int)(key / S), s = (int)(key % S);
-  int64_t begin;
-  int cnt;
-  if (tok_offsets) {
-    begin = tok_offsets[key];
-    cnt = tok_offsets[key + 1] - (int)begin;
-  } else {
-    begin = key * k_fixed;
-    cnt = k_fixed;
-  }
-  __nv_bfloat16* yrow = y + (int64_t)s * sy_s + (int64_t)h * sy_h;
+// Sum of one key's rows (cnt ids at tok_rows[begin..]) into yrow, one warp.
+// srt: this warp's 32-entry shared scratch.
+__device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
+                                            int dh, const int32_t* __restrict__ tok_rows, int64_t begin, int cnt,
+                                            int64_t R, int64_t P_rows, __nv_bfloat16* yrow, int* srt) {
+  const int lane = threadIdx.x & 31;
   const int nvec = dh / 8;
-
   if (cnt <= 32) {
     // rank sort of <= 32 row ids (ascending; ids are distinct)
     int r = lane < cnt ? tok_rows[begin + lane] : 0x7fffffff;
@@ -57,10 +42,10 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
       const int o = __shfl_sync(0xffffffffu, r, j);
       rank += (o < r) || (o == r && j < lane);
     }
-    srt[warp][rank] = prow;   // ascending sorted row <=> ascending padded row
+    srt[rank] = prow;   // ascending sorted row <=> ascending padded row
     __syncwarp();
     int nvalid = 0;
-    for (int j = 0; j < cnt; ++j) nvalid += srt[warp][j] != 0x7fffffff;
+    for (int j = 0; j < cnt; ++j) nvalid += srt[j] != 0x7fffffff;
     for (int c = lane; c < nvec; c += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int j0 = 0; j0 < nvalid; j0 += 8) {
@@ -68,7 +53,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
         uint4 u[8];
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj)
-          if (j0 + jj < nvalid) u[jj] = *reinterpret_cast<const uint4*>(P + (int64_t)srt[warp][j0 + jj] * dh + c * 8);
+          if (j0 + jj < nvalid) u[jj] = *reinterpret_cast<const uint4*>(P + (int64_t)srt[j0 + jj] * dh + c * 8);
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
           if (j0 + jj < nvalid) {
@@ -89,6 +74,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
       }
       *reinterpret_cast<uint4*>(yrow + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
+    __syncwarp();
   } else {
     // rare long lists: ascending selection, one row at a time
     for (int c = lane; c < nvec; c += 32) {
@@ -123,6 +109,57 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
   }
 }
 
+__global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row, int dh,
+                               int S, int H,
+                               const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
+                               int k_fixed, int64_t R, int64_t P_rows, __nv_bfloat16* __restrict__ y, int64_t sy_s,
+                               int64_t sy_h) {
+  __shared__ int srt[COMBINE_WARPS][32];
+  const int warp = threadIdx.x >> 5;
+  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
+  if (key >= (int64_t)H * S) return;
+  const int h = (int)(key / S), s = (int)(key % S);
+  int64_t begin;
+  int cnt;
+  if (tok_offsets) {
+    begin = tok_offsets[key];
+    cnt = tok_offsets[key + 1] - (int)begin;
+  } else {
+    begin = key * k_fixed;
+    cnt = k_fixed;
+  }
+  combine_key(P, pad_of_row, dh, tok_rows, begin, cnt, R, P_rows, y + (int64_t)s * sy_s + (int64_t)h * sy_h,
+              srt[warp]);
+}
+
+// Expert-parallel receiver: key = received record slot (source src = key / cap, slot
+// key % cap).  The record's sum goes straight into the source rank's return area, row
+// (source's send position of the record) = meta offset + slot, over NVLink; slots past
+// the source's count are skipped.  The last CTA to finish raises the return flag of
+// this rank in every peer (system-scope release after every CTA's stores).
+__global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
+                                      int dh, const int32_t* __restrict__ tok_rows, int k_fixed, int64_t R,
+                                      int64_t P_rows, const EpReturn r) {
+  __shared__ int srt[COMBINE_WARPS][32];
+  const int warp = threadIdx.x >> 5;
+  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;
+  const int64_t slots = (int64_t)r.n * r.cap;
+  if (key < slots && ld_volatile_i32(r.status) == 0) {
+    const int src = (int)(key / r.cap);
+    const int64_t slot = key % r.cap;
+    const int64_t* meta = reinterpret_cast<const int64_t*>(r.local + r.layout.off_meta);
+    const int64_t cnt = meta[2 * src], off = meta[2 * src + 1];
+    if (slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots) {
+      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
+      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
+    }
+  }
+  if (ep_last_cta(reinterpret_cast<int*>(r.local + r.layout.off_done) + 1) && threadIdx.x == 0) {
+    for (int d = 0; d < r.n; ++d)
+      red_release_sys_add(reinterpret_cast<int*>(r.peers.base[d] + r.layout.off_flags) + 32 + r.me, 1);
+  }
+}
+
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
                             const int* tile_rows, int32_t* pad_of_row, cudaStream_t st) {
   pad_rows_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(cu_tiles, HE, tile_row0, tile_rows, pad_of_row);
@@ -135,6 +172,16 @@ cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, in
   const int64_t keys = (int64_t)H * S;
   combine_kernel<<<(unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st>>>(
       P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh,
+                                  const int32_t* tok_rows, int k_fixed, int64_t R, int64_t P_rows, const EpReturn& r,
+                                  cudaStream_t st) {
+  const int64_t keys = (int64_t)r.n * r.cap;
+  const int64_t blocks = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
+  combine_return_kernel<<<(unsigned)blocks, COMBINE_WARPS * 32, 0, st>>>(P, pad_of_row, dh, tok_rows, k_fixed, R,
+                                                                         P_rows, r);
   return cudaGetLastError();
 }
 

@@ -141,7 +141,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
               const uint8_t* xq_in, const uint8_t* xsf_in, const uint8_t* xg_in, int64_t xq_pitch, int64_t xsf_pitch,
-              int64_t xg_pitch) {
+              int64_t xg_pitch, const EpReturn* ret) {
   const int64_t T = (int64_t)S * H;
   FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
   const bool prequant = xq_in != nullptr;
@@ -227,7 +227,10 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     offs_map = w.tok_offsets;
     kf = 0;
   }
-  MHMOE_TRY(launch_combine(w.P, w.pad_of_row, dh, S, H, rows_map, offs_map, kf, R, rows, y, sy_s, sy_h, st));
+  if (ret)
+    MHMOE_TRY(launch_combine_return(w.P, w.pad_of_row, dh, rows_map, kf, R, rows, *ret, st));
+  else
+    MHMOE_TRY(launch_combine(w.P, w.pad_of_row, dh, S, H, rows_map, offs_map, kf, R, rows, y, sy_s, sy_h, st));
   mark(4);
 #undef MHMOE_TRY
   return MHMOE_OK;

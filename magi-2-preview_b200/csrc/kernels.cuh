@@ -12,6 +12,60 @@ namespace mhmoe {
 // Upper bound of 128-row tiles for R rows spread over n_experts groups.
 inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts) { return (R + 127) / 128 + n_experts; }
 
+// ───────── expert-parallel peer buffers (ep_p2p.cu, combine.cu) ─────────
+// Every rank allocates one buffer with this layout and maps every peer's (CUDA IPC):
+//   flags  int32 [2][32]  arrival counters raised by peers: [0][s] records from s landed,
+//                         [1][s] returns from s landed (one increment per layer call)
+//   meta   int64 [32][2]  written by source s before its record flag: {record count,
+//                         offset of this rank's group in s's send order}
+//   done   int32 [8]      this rank's own last-CTA counters
+//   rx     [n][cap][row_bytes]  records from source s at slot s*cap + j
+//   back   [n*cap][dh] bf16     returned sums, row = this rank's send position
+constexpr int EP_MAX_RANKS = 32;
+struct EpLayout {
+  int64_t off_flags, off_meta, off_done, off_rx, off_back, bytes;
+};
+inline EpLayout ep_layout(int n, int64_t cap, int dh, int64_t row_bytes) {
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  EpLayout L;
+  L.off_flags = 0;
+  L.off_meta = 256;
+  L.off_done = 768;
+  L.off_rx = 1024;
+  L.off_back = L.off_rx + up((int64_t)n * cap * row_bytes);
+  L.bytes = L.off_back + up((int64_t)n * cap * dh * 2);
+  return L;
+}
+struct EpPeers {
+  uint8_t* base[EP_MAX_RANKS];
+};
+struct EpReturn {
+  EpPeers peers;     // every rank's buffer base as mapped here (peers.base[me] = local)
+  uint8_t* local;
+  EpLayout layout;
+  int64_t cap;
+  int n, me;
+  int* status;
+};
+
+// Last-CTA detection: every thread's stores (peer stores included) are ordered at system
+// scope before this CTA's increment of *done; returns true in the CTA that completes the
+// grid, after which *done is back to 0.  Called by all threads of the block.
+__device__ __forceinline__ bool ep_last_cta(int* done) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+    if (last) {
+      __threadfence_system();
+      *done = 0;
+    }
+  }
+  __syncthreads();
+  return last != 0;
+}
+
 // permute.cu
 // Sort chunks hold at least min_chunk flat entries (256 by default; larger chunks shrink the
 // histogram scratch).
@@ -67,7 +121,22 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
               const uint8_t* xq_in = nullptr, const uint8_t* xsf_in = nullptr, const uint8_t* xg_in = nullptr,
-              int64_t xq_pitch = 0, int64_t xsf_pitch = 0, int64_t xg_pitch = 0);
+              int64_t xq_pitch = 0, int64_t xsf_pitch = 0, int64_t xg_pitch = 0, const EpReturn* ret = nullptr);
+
+// combine.cu (expert-parallel return)
+cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh,
+                                  const int32_t* tok_rows, int k_fixed, int64_t R, int64_t P_rows, const EpReturn& r,
+                                  cudaStream_t st);
+
+// ep_p2p.cu
+cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                                   const int64_t* idx, const float* probs, int K, int E, int E_loc,
+                                   const int32_t* send_key, const int64_t* send_offsets, int n, int me, int64_t cap,
+                                   const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st);
+cudaError_t launch_ep_wait(const uint8_t* local, int kind, int n, int target, uint64_t timeout_ns, int* status,
+                           cudaStream_t st);
+cudaError_t launch_ep_unpack_slots(const uint8_t* local, int n, int64_t cap, int dh, int K, int E_loc,
+                                   int64_t* idx, float* probs, int* status, cudaStream_t st);
 
 // ep.cu
 int64_t ep_row_bytes(int dh, int K);

@@ -102,14 +102,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
 // (possibly tiny) timeout.
 constexpr uint64_t MHMOE_DRAIN_NS = 2000000000ull;
 
-// Bounded wait for a global flag written by another agent (kernel, peer, host) to reach
-// `expected` or more.  Same contract as mbar_wait.
+// Bounded wait for a global flag written by another agent (kernel, peer GPU, host) to
+// reach `expected` or more; system-scope acquire, so data the writer released before the
+// flag (from another GPU too) is visible afterwards.  Same contract as mbar_wait.
 __device__ __forceinline__ bool flag_wait_geq(const int* flag, int expected, int* err, int code,
                                               uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0;; ++i) {
     int v;
-    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
     if (v >= expected) return true;
     if ((i & 63u) == 63u) {
       if (err && ld_volatile_i32(err) != 0) return false;
@@ -119,6 +120,11 @@ __device__ __forceinline__ bool flag_wait_geq(const int* flag, int expected, int
       }
     }
   }
+}
+
+// System-scope release add (a flag in another GPU's memory, reached over NVLink).
+__device__ __forceinline__ void red_release_sys_add(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_shared() {

@@ -220,7 +220,7 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
     # 4. local experts on the received records
     lidx, lprobs = be.unpack(recv, dh, K, E_loc)
     lg, lps, loffs, linv = be.sort(lprobs.view(1, R_recv, K), lidx.view(1, R_recv, K), E_loc)
-    LAST_STATS.update(rows_received=loffs[-1])     # device scalar: read it after the step, not here
+    LAST_STATS.update(rows_received=loffs[-1], transport="nccl")   # device scalar: read it after the step
     out = be.ffn_records(recv, dh, K, lg, lps, loffs, linv, gu, dn, stage_events=stage_events)
     # 5. per-record partial sums back to their sources; combine in ascending rank order
     if comm_events:
@@ -231,9 +231,171 @@ def ep_moe_layer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, 
     return be.combine(back, S, H, send_slot, ep)
 
 
-def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None) -> torch.Tensor:
+# ───────────────────────── token -> expert EP over peer memory ─────────────────────────
+
+class PeerExchange:
+    """Per-rank exchange buffer mapped on every rank of the group (CUDA IPC).
+
+    Holds records from every source (``n * cap`` slots) and the returned sums of this
+    rank's own records; the kernels store into peers' buffers over NVLink and raise
+    arrival counters there, so a layer call needs no host synchronisation.  Requires
+    every rank on its own GPU of one node (checked at creation)."""
+
+    _cache: dict = {}
+
+    def __init__(self, group, device: torch.device, cap: int, dh: int, K: int):
+        import ctypes as C
+        import socket
+        L = _lib.lib()
+        self.group, self.device, self.cap, self.dh, self.K = group, device, int(cap), int(dh), int(K)
+        self.n = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        ident = (socket.gethostname(), str(torch.cuda.get_device_properties(device).uuid))
+        idents = [None] * self.n
+        dist.all_gather_object(idents, ident, group=group)
+        if len({h for h, _ in idents}) != 1 or len({u for _, u in idents}) != self.n:
+            raise RuntimeError("peer-memory EP needs every rank on its own GPU of one node")
+        size = int(L.mhmoe_ep_sym_bytes(self.n, self.cap, dh, K))
+        ptr = C.c_void_p()
+        handle = (C.c_ubyte * 64)()
+        with torch.cuda.device(device):
+            _lib.check(L.mhmoe_ep_sym_alloc(size, C.byref(ptr), handle), "ep_sym_alloc")
+        handles = [None] * self.n
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        bases, self._opened = [], []
+        with torch.cuda.device(device):
+            for r in range(self.n):
+                if r == self.me:
+                    bases.append(ptr.value)
+                    continue
+                p = C.c_void_p()
+                buf = (C.c_ubyte * 64).from_buffer_copy(handles[r])
+                _lib.check(L.mhmoe_ep_sym_open(buf, C.byref(p)), "ep_sym_open")
+                bases.append(p.value)
+                self._opened.append(p.value)
+        self.local = ptr.value
+        self.peer_bases = (C.c_void_p * self.n)(*bases)
+        offs = (C.c_int64 * 5)()
+        _lib.check(L.mhmoe_ep_sym_offsets(self.n, self.cap, dh, K, offs), "ep_sym_offsets")
+        self.off_back = int(offs[3])
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    @classmethod
+    def get(cls, group, device: torch.device, cap: int, dh: int, K: int) -> "PeerExchange":
+        """The group's exchange on this device, re-created (collectively: every rank passes
+        the same ``cap``) when a larger capacity is needed."""
+        key = (id(group), device.index, int(dh), int(K))
+        px = cls._cache.get(key)
+        if px is None or px.cap < cap:
+            if px is not None:
+                px.close()
+            px = cls(group, device, cap, dh, K)
+            cls._cache[key] = px
+        return px
+
+    def close(self) -> None:
+        """Unmap the peers and free the buffer (collective: all ranks call it)."""
+        L = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                L.mhmoe_ep_sym_close(p)
+            self._opened = []
+            dist.barrier(group=self.group)
+            if self.local:
+                L.mhmoe_ep_sym_free(self.local)
+                self.local = None
+
+
+def _ep_timeout_ns() -> int:
+    import os
+    return int(float(os.environ.get("MHMOE_EP_TIMEOUT_S", "10")) * 1e9)
+
+
+def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn,
+                      group, stage_events=None, comm_events=None) -> torch.Tensor:
+    """Token -> expert EP forward with the exchange fused into the kernels (peer memory).
+
+    Same records and result as ``ep_moe_layer``; the record kernel stores into the
+    destinations' buffers and the receiver's combine stores each record's sum into the
+    source's buffer, each followed by a device-side arrival flag, so there is no count
+    exchange and no host synchronisation.  comm_events (optional, 4): around the record
+    send + wait, and around the wait for the returns.
+    """
+    be = CudaBackend()
+    L = _lib.lib()
+    ep = dist.get_world_size(group)
+    S, H, dh = x_heads.shape
+    K = idx.shape[-1]
+    E = int(num_experts)
+    HE = H * E
+    if HE % ep:
+        raise ValueError(f"H*E ({HE}) must be divisible by ep_size ({ep})")
+    E_loc = HE // ep
+    T = H * S
+    dev = x_heads.device
+    px = PeerExchange.get(group, dev, T, dh, K)
+    st = _lib.stream_ptr(dev)
+    status = _lib.device_status(dev).data_ptr()
+    timeout = _ep_timeout_ns()
+    px.epoch += 1
+    # 1. records, grouped by destination
+    xq, xsf, xg = be.quant_tokens(x_heads)
+    dest = be.dest(idx, E, ep)
+    zeros = torch.zeros(1, T, ep, dtype=torch.float32, device=dev)
+    send_key, _, send_offs, send_slot = be.sort(zeros, dest.view(1, T, ep), ep)
+    if comm_events:
+        comm_events[0].record()
+    _lib.check(L.mhmoe_ep_send_records(xq.data_ptr(), xsf.data_ptr(), xg.data_ptr(), H, S, dh, idx.data_ptr(),
+                                       probs.data_ptr(), K, E, send_key.data_ptr(), send_offs.data_ptr(), ep,
+                                       px.me, px.cap, px.peer_bases, status, st), "ep_send_records")
+    _lib.check(L.mhmoe_ep_wait(px.local, 0, ep, px.epoch, timeout, status, st), "ep_wait(records)")
+    if comm_events:
+        comm_events[1].record()
+    # 2. receiver: every slot -> (local expert, prob) entries, sorted by expert
+    slots = ep * px.cap
+    lidx = torch.empty(slots, K, dtype=torch.int64, device=dev)
+    lprobs = torch.empty(slots, K, dtype=torch.float32, device=dev)
+    _lib.check(L.mhmoe_ep_unpack_slots(px.local, ep, px.cap, dh, K, E_loc, lidx.data_ptr(), lprobs.data_ptr(),
+                                       status, st), "ep_unpack_slots")
+    lg, lps, loffs, linv = be.sort(lprobs.view(1, slots, K), lidx.view(1, slots, K), E_loc)
+    LAST_STATS.update(rows_received=loffs[-1], transport="peer")
+    # 3. FFN on the records in place; its combine returns each record's sum to the source
+    R = slots * K
+    ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, slots, 1, dh, gu.d_expert, E_loc)), dtype=torch.uint8,
+                     device=dev)
+    _lib.check(L.mhmoe_ep_ffn_return(px.local, ep, px.me, px.cap, dh, gu.d_expert, K, E_loc, R, lg.data_ptr(),
+                                     lps.data_ptr(), loffs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(),
+                                     gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(),
+                                     dn.gscale.data_ptr(), linv.data_ptr(), ws.data_ptr(), px.peer_bases, status, 0,
+                                     _events(stage_events), st), "ep_ffn_return")
+    if comm_events:
+        comm_events[2].record()
+    _lib.check(L.mhmoe_ep_wait(px.local, 1, ep, px.epoch, timeout, status, st), "ep_wait(returns)")
+    if comm_events:
+        comm_events[3].record()
+    # 4. source: sum each (head, token)'s returned rows in ascending rank order
+    y = torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
+    _lib.check(L.mhmoe_combine(px.local + px.off_back, slots, None, dh, S, H, send_slot.data_ptr(), None, ep, slots,
+                               y.data_ptr(), y.stride(0), y.stride(1), st), "combine")
+    return y
+
+
+def ep_transport(module) -> str:
+    """'peer' (default when every rank has its own GPU of one node) or 'nccl'
+    (``MHMOE_EP_TRANSPORT=nccl`` or peer buffers unavailable)."""
+    import os
+    want = getattr(module, "ep_transport", None) or os.environ.get("MHMOE_EP_TRANSPORT", "peer")
+    return "nccl" if want == "nccl" else "peer"
+
+
+def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None, comm_events=None) -> torch.Tensor:
     """``CoreMultiHeadMoE`` forward with ``ep_size > 1`` (route locally, EP FFN)."""
     probs, idx = module._route(x_heads)
     gu, dn = module.packed_weights()
+    if ep_transport(module) == "peer":
+        return ep_moe_layer_peer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
+                                 stage_events=stage_events, comm_events=comm_events)
     return ep_moe_layer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
-                        stage_events=stage_events)
+                        stage_events=stage_events, comm_events=comm_events)

@@ -1,5 +1,6 @@
-"""GPU, 2 ranks (needs >= 2 GPUs; skipped otherwise): the expert-parallel MoE module over
-NCCL against the single-GPU module on each rank's own tokens.  The EP layer sums each
+"""GPU, 2 ranks (needs >= 2 GPUs; skipped otherwise): the expert-parallel MoE module, with
+the exchange fused into the kernels (peer memory) and over NCCL, against the single-GPU
+module on each rank's own tokens.  The EP layer sums each
 token's experts per rank (bf16 partial sums) before the source adds the ranks, so the
 outputs agree to that rounding: rel L2 <= 1e-2 (typically ~1e-3); EP runs are
 run-to-run identical."""
@@ -21,13 +22,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, transport):
     import sys
     from datetime import timedelta
     from pathlib import Path
     root = Path(__file__).resolve().parent.parent
     sys.path[:0] = [str(root), str(root / "magi-2-preview_b200")]
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      MHMOE_EP_TRANSPORT=transport, MHMOE_EP_TIMEOUT_S="5")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -54,19 +56,21 @@ def _worker(rank, world, port, q):
         torch.cuda.synchronize()
         _lib.check_device_status(dev)
         err = float((y_ep.float() - y_1.float()).norm() / y_1.float().norm())
-        q.put((rank, err < 1e-2, bool(torch.equal(y_ep, y_ep2)), err))
+        from flash_mh_moe.ep import LAST_STATS
+        q.put((rank, err < 1e-2, bool(torch.equal(y_ep, y_ep2)), err, LAST_STATS.get("transport")))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_module_matches_single_gpu():
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
+def test_ep_module_matches_single_gpu(transport):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -74,6 +78,7 @@ def test_ep_module_matches_single_gpu():
     res = sorted(q.get(timeout=30) for _ in range(world))
     for p in procs:
         assert p.exitcode == 0
-    for rank, same, repeat, err in res:
+    for rank, same, repeat, err, used in res:
+        assert used == transport
         assert repeat, f"rank {rank}: EP output not deterministic"
         assert same, f"rank {rank}: EP output differs from the single-GPU module (rel L2 {err})"
