@@ -45,7 +45,7 @@ CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, sc
 CFG4 = dict(name="config4", S=256, d=3072, H=1, E=128, K=8, de=1024, seed=4, score_func="softmax", layers=4)
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
 # libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, token quantise,
-# row grouping, gate/up GEMM, down GEMM, combine.  EP (records arrive quantised): router,
+# row grouping, gate/up GEMM, down GEMM, combine (atomic scatter: output zeroing instead).  EP (records arrive quantised): router,
 # token quantise, destination mask, send sort x4, pack, unpack, receiver sort x4, tile tables,
 # pad map, row grouping, gate/up GEMM, down GEMM, per-record combine, source-side combine.
 KERNELS_PER_STEP = 12
@@ -156,7 +156,7 @@ def make_layer(cfg, device, rank, ep_group=None):
     return m, x_host
 
 
-def step_explicit(m, x, ev):
+def step_explicit(m, x, ev, deterministic=None):
     """The module forward spelled out, with events between the stages (same kernels)."""
     from flash_mh_moe.fwd import ffn_nvfp4
     from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse, route_fused
@@ -171,7 +171,8 @@ def step_explicit(m, x, ev):
     ev[1].record()
     gids, ps, offs, inv = flash_mh_moe_global_sort_with_inverse(probs, idx, m.num_experts)
     gu, dn = m.packed_weights()
-    return ffn_nvfp4(x_heads, gids, ps, offs, gu, dn, tok_rows=inv, k_fixed=m.topk, stage_events=ev[2:7])
+    return ffn_nvfp4(x_heads, gids, ps, offs, gu, dn, tok_rows=inv, k_fixed=m.topk, stage_events=ev[2:7],
+                     deterministic=deterministic)
 
 
 def step_ep(m, x, ev):
@@ -256,30 +257,42 @@ def run_ours(args, world, rank, local):
     if not args.no_e2e:
         e2e_ms = _e2e(args, m, x_host, dev, world)
     out = _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host)
-    if world == 1 and args.config == 1 and not args.tokens:
-        out["weak_scaling_base"] = _one_gpu_config3(args, m, x)
+    if world == 1:
+        from flash_mh_moe.fwd import _is_deterministic
+        det = _is_deterministic()
+        out["config"]["scatter"] = ("combine (deterministic: partial rows + fp32 combine; the default)" if det else
+                                    "atomic (MHMOE_SCATTER=atomic: bf16 atomics from the down GEMM, the "
+                                    "reference's default scatter)")
+        if not args.tokens and cfg.get("layers", 1) == 1:
+            ms_other = _time_explicit(args, m, x, cfg["S"], deterministic=not det)
+            out["other_scatter"] = {"scatter": "atomic" if det else "combine",
+                                    "value": round(cfg["S"] / (ms_other * 1e-3), 1), "unit": "tokens/s",
+                                    "ms_per_step": round(ms_other, 4)}
+        if args.config == 1 and not args.tokens:
+            S3 = CFG3["S"]
+            ms3 = _time_explicit(args, m, x, S3, deterministic=det)
+            out["weak_scaling_base"] = {
+                "workload": f"config3 per-GPU shape on 1 GPU: {S3} tokens, E=128 local, same scatter as the "
+                            "headline",
+                "value": round(S3 / (ms3 * 1e-3), 1), "unit": "tokens/s", "ms_per_step": round(ms3, 4)}
     return out
 
 
-def _one_gpu_config3(args, m, x):
-    """Config 3's per-GPU shape (8192 tokens, all 128 experts local) on this one GPU: the
-    N=1 point of the expert-parallel weak-scaling series (N>1 runs config 3)."""
+def _time_explicit(args, m, x, S, deterministic):
+    """Device time per step of the 1-GPU layer on the first S tokens of x."""
     import torch
-    S3 = CFG3["S"]
-    xs = x[:S3].contiguous()
+    xs = x[:S].contiguous()
     for _ in range(args.warmup):
-        step_explicit(m, xs, [torch.cuda.Event(enable_timing=True) for _ in range(7)])
+        step_explicit(m, xs, [torch.cuda.Event(enable_timing=True) for _ in range(7)], deterministic)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     t0.record()
     for k in range(args.steps):
-        step_explicit(m, xs, evs[k])
+        step_explicit(m, xs, evs[k], deterministic)
     t1.record()
     torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
-    return {"workload": f"config3 per-GPU shape on 1 GPU: {S3} tokens, E=128 local", "value": round(S3 / (ms * 1e-3), 1),
-            "unit": "tokens/s", "ms_per_step": round(ms, 4)}
+    return t0.elapsed_time(t1) / args.steps
 
 
 def _e2e(args, m, x_host, dev, world):
@@ -358,7 +371,12 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         "clocks": clk.summary(),
     }
     if world > 1:
+        import torch.distributed as dist
         from flash_mh_moe.ep import LAST_STATS
+        every = [None] * world
+        dist.all_gather_object(every, {k: round(v, 4) for k, v in stages.items()})
+        out["stages_ms_min_max_over_ranks"] = {k: [min(e[k] for e in every), max(e[k] for e in every)]
+                                               for k in stages}
         out["config"]["parallelism"] = (f"ep{world} (token->expert records, "
                                         + ("fused NVLink peer stores)" if LAST_STATS.get("transport") == "peer"
                                            else "NCCL all-to-all)"))

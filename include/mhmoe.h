@@ -164,6 +164,19 @@ MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_strid
                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
                     void* const* stage_events, void* stream);
 
+/* mhmoe_ffn_nvfp4 with the reference's default (non-deterministic) scatter: the down
+ * GEMM adds each routed row's bf16(y_acc * prob) into y with bf16 atomics
+ * (_mh_moe_fwd_kernel with deterministic=False, triton/mh_moe_fwd.py:213-221, selected
+ * when MAGI2_DETERMINISTIC is not "1", fwd.py:12-13).  y is zeroed first; no partial
+ * buffer and no combine pass.  Results may differ run to run in the last bf16 bits. */
+MHMOE_API int mhmoe_ffn_nvfp4_atomic(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh,
+                                     int de, int n_experts, int64_t R, const int32_t* gather_ids,
+                                     const float* probs_sorted, const int64_t* expert_offsets, const uint8_t* gu_data,
+                                     const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
+                                     const uint8_t* dn_sf, const float* dn_gscale, void* workspace, void* y,
+                                     int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
+                                     void* const* stage_events, void* stream);
+
 /* The FFN above on rows that are already NVFP4 (per-row scales): row t has its dh/2
  * data bytes at xq + t*xq_pitch, its dh/16 row-major scale bytes at xsf + t*xsf_pitch
  * and its fp32 row scale at xg + t*xg_pitch (byte pitches, 16-B aligned data/scales);

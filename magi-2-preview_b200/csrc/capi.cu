@@ -184,13 +184,13 @@ int mhmoe_pack_weights_nvfp4(int kind, const void* w0, const void* w1, int n_exp
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "pack_weights_nvfp4");
 }
 
-int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
-                    int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
-                    const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
-                    const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
-                    const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
-                    void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
-                    void* const* stage_events, void* stream) {
+static int ffn_entry(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
+                     int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                     const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                     const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                     const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
+                     void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
+                     void* const* stage_events, void* stream, bool atomic, const char* what) {
   MHMOE_REQUIRE(x && y && expert_offsets && gu_data && gu_sf && gu_gscale && dn_data && dn_sf && dn_gscale);
   MHMOE_REQUIRE(S >= 0 && H > 0 && n_experts > 0 && n_experts % H == 0 && R >= 0);
   MHMOE_REQUIRE(dh % 256 == 0 && de % 256 == 0 && dh > 0 && de > 0);
@@ -221,10 +221,34 @@ int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S
                            gather_ids, probs_sorted, expert_offsets, gu_data, gu_sf, gu_gscale, dn_data, dn_sf,
                            dn_gscale, tok_rows, tok_offsets, k_fixed, workspace, static_cast<__nv_bfloat16*>(y),
                            y_stride_s, y_stride_h, dev_status, timeout_ns,
-                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce);
-  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ffn_nvfp4");
+                           reinterpret_cast<cudaEvent_t const*>(stage_events), st, &ce, nullptr, nullptr, nullptr,
+                           0, 0, 0, nullptr, atomic);
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, what);
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
   return rc;
+}
+
+int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
+                    int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                    const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                    const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                    const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, void* workspace,
+                    void* y, int64_t y_stride_s, int64_t y_stride_h, int* dev_status, uint64_t timeout_ns,
+                    void* const* stage_events, void* stream) {
+  return ffn_entry(x, x_stride_s, x_stride_h, S, H, dh, de, n_experts, R, gather_ids, probs_sorted, expert_offsets,
+                   gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, tok_rows, tok_offsets, k_fixed, workspace, y,
+                   y_stride_s, y_stride_h, dev_status, timeout_ns, stage_events, stream, false, "ffn_nvfp4");
+}
+
+int mhmoe_ffn_nvfp4_atomic(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh, int de,
+                           int n_experts, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                           const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                           const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
+                           const float* dn_gscale, void* workspace, void* y, int64_t y_stride_s, int64_t y_stride_h,
+                           int* dev_status, uint64_t timeout_ns, void* const* stage_events, void* stream) {
+  return ffn_entry(x, x_stride_s, x_stride_h, S, H, dh, de, n_experts, R, gather_ids, probs_sorted, expert_offsets,
+                   gu_data, gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, nullptr, nullptr, 0, workspace, y,
+                   y_stride_s, y_stride_h, dev_status, timeout_ns, stage_events, stream, true, "ffn_nvfp4_atomic");
 }
 
 int mhmoe_ffn_nvfp4_quantized(const uint8_t* xq, int64_t xq_pitch, const uint8_t* xsf, int64_t xsf_pitch,

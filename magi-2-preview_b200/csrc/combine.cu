@@ -132,8 +132,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
               srt[warp]);
 }
 
-// Expert-parallel receiver: key = received record slot (source src = key / cap, slot
-// key % cap).  The record's sum goes straight into the source rank's return area, row
+// Expert-parallel receiver: key = received record slot src * cap + slot.  The record's sum goes straight into the source rank's return area, row
 // (source's send position of the record) = meta offset + slot, over NVLink; slots past
 // the source's count are skipped.  The last CTA to finish raises the return flag of
 // this rank in every peer (system-scope release after every CTA's stores).
@@ -142,11 +141,14 @@ __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const
                                       int64_t P_rows, const EpReturn r) {
   __shared__ int srt[COMBINE_WARPS][32];
   const int warp = threadIdx.x >> 5;
-  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;
+  // work item w -> source (w + me) % n, slot w / n: consecutive warps write to different
+  // ranks, so all links carry the returns at once (no rank is the target of everyone)
+  const int64_t w = (int64_t)blockIdx.x * COMBINE_WARPS + warp;
   const int64_t slots = (int64_t)r.n * r.cap;
-  if (key < slots && ld_volatile_i32(r.status) == 0) {
-    const int src = (int)(key / r.cap);
-    const int64_t slot = key % r.cap;
+  if (w < slots && ld_volatile_i32(r.status) == 0) {
+    const int src = (int)((w + r.me) % r.n);
+    const int64_t slot = w / r.n;
+    const int64_t key = (int64_t)src * r.cap + slot;
     const int64_t* meta = reinterpret_cast<const int64_t*>(r.local + r.layout.off_meta);
     const int64_t cnt = meta[2 * src], off = meta[2 * src + 1];
     if (slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots) {
@@ -158,6 +160,22 @@ __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const
     for (int d = 0; d < r.n; ++d)
       red_release_sys_add(reinterpret_cast<int*>(r.peers.base[d] + r.layout.off_flags) + 32 + r.me, 1);
   }
+}
+
+// One warp per (s, h) row, 16-B stores.
+__global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ y, int S, int H, int dh, int64_t sy_s, int64_t sy_h) {
+  const int64_t key = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (key >= (int64_t)S * H) return;
+  const int64_t s = key / H, h = key % H;
+  uint4* row = reinterpret_cast<uint4*>(y + s * sy_s + h * sy_h);
+  for (int c = threadIdx.x & 31; c < dh / 8; c += 32) row[c] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+cudaError_t launch_zero_rows(__nv_bfloat16* y, int S, int H, int dh, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
+  const int64_t rows = (int64_t)S * H;
+  if (rows == 0) return cudaSuccess;
+  zero_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(y, S, H, dh, sy_s, sy_h);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,

@@ -7,7 +7,8 @@
 // arrival counter in every peer.  Buffer layout: EpLayout (kernels.cuh).
 //
 //   ep_send_records_kernel   send row j (grouped by destination d, from the counting sort)
-//                            -> record at d's rx[me*cap + j - send_offsets[d]]; the last
+//                            -> record at d's rx[me*cap + j - send_offsets[d]], destinations
+//                            interleaved across warps; the last
 //                            CTA writes {count, send offset} into d's meta[me] and raises
 //                            d's records flag [0][me].
 //   ep_wait_kernel           bounded wait until every source's flag of one kind reaches
@@ -36,15 +37,20 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
                                        int* status) {
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
-  const int64_t total = send_offsets[n];
-  for (int64_t j = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); j < total; j += (int64_t)gridDim.x * warps) {
-    int d = 0;
-    while (d + 1 < n && send_offsets[d + 1] <= j) ++d;                 // destination of row j
-    const int64_t slot = j - send_offsets[d];
-    if (slot >= cap) {                                                  // more rows than the buffer holds
+  // Work item w -> destination d = (w + me) % n, its k = w / n-th row: consecutive warps
+  // write to different ranks (and each rank starts at a different one), so every link
+  // carries traffic at once instead of all ranks filling one destination after another.
+  const int64_t items = (int64_t)n * cap;
+  for (int64_t w = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); w < items; w += (int64_t)gridDim.x * warps) {
+    const int d = (int)((w + me) % n);
+    const int64_t slot = w / n;
+    const int64_t cnt = send_offsets[d + 1] - send_offsets[d];
+    if (slot >= cnt) continue;
+    if (cnt > cap) {                                                    // more rows than the buffer holds
       if (lane == 0) record_error(status, MHMOE_ERR_CAPACITY);
       continue;
     }
+    const int64_t j = send_offsets[d] + slot;
     const int64_t t = send_key[j];                                      // h*S + s
     const int h = (int)(t / S), s = (int)(t % S);
     const int64_t q = (int64_t)s * H + h;                               // quantised token row
@@ -127,8 +133,8 @@ cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const 
                                    const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st) {
   const int64_t rb = ep_row_bytes(dh, K);
   const EpLayout L = ep_layout(n, cap, dh, rb);
-  const int64_t max_rows = (int64_t)H * S * n;
-  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((max_rows + 7) / 8, 4 * num_sms()));
+  const int64_t items = (int64_t)n * cap;
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, 4 * num_sms()));
   ep_send_records_kernel<<<(unsigned)blocks, 256, 0, st>>>(xq, xsf, xg, H, S, dh, idx, probs, K, E, E_loc, send_key,
                                                            send_offsets, n, me, cap, rb, peers, L, local, status);
   return cudaGetLastError();

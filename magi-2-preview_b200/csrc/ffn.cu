@@ -141,7 +141,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
               const uint8_t* xq_in, const uint8_t* xsf_in, const uint8_t* xg_in, int64_t xq_pitch, int64_t xsf_pitch,
-              int64_t xg_pitch, const EpReturn* ret) {
+              int64_t xg_pitch, const EpReturn* ret, bool atomic_scatter) {
   const int64_t T = (int64_t)S * H;
   FfnWorkspace w = carve(static_cast<uint8_t*>(workspace), R, T, dh, de, HE);
   const bool prequant = xq_in != nullptr;
@@ -214,6 +214,19 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p2.N = dh;
   p2.probs = probs_sorted;
   p2.gs_down = dn_gscale;
+  if (atomic_scatter) {
+    // reference default scatter: bf16 atomics into the zeroed output, no partials / combine
+    p2.y = y;
+    p2.sy_s = sy_s;
+    p2.sy_h = sy_h;
+    p2.gather_ids = gather_ids;
+    p2.experts_per_head = HE / H;
+    MHMOE_TRY(launch_zero_rows(y, S, H, dh, sy_s, sy_h, st));
+    MHMOE_TRY(launch_gemm<EPI_DOWN_ATOMIC>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
+    mark(3);
+    mark(4);
+    return MHMOE_OK;
+  }
   MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
 
   mark(3);

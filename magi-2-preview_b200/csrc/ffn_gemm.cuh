@@ -27,6 +27,9 @@
 //               A operand (data + SF atoms) of the down GEMM.
 //   EPI_DOWN    bf16(acc * s_down * prob) staged in swizzled shared memory and written
 //               with TMA stores into the padded partial buffer P[rows_pad, N].
+//   EPI_DOWN_ATOMIC  the same bf16(acc * s_down * prob) values added into y[token, head]
+//               with bf16 vector atomics (the reference's default, non-deterministic
+//               scatter): no partial buffer, no combine pass.
 //   EPI_RAW     fp32 accumulator written as is (verification only).
 #pragma once
 
@@ -34,7 +37,7 @@
 
 namespace mhmoe {
 
-enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2 };
+enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2, EPI_DOWN_ATOMIC = 3 };
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
@@ -75,9 +78,14 @@ struct FfnGemmParams {
   const float* gs_up;        // [n_experts]
   uint8_t* h_data;           // [128 * n_mtiles, N/4]  (hidden has N/2 columns, 2 per byte)
   uint8_t* h_sf;             // SF atoms of the hidden, K_hidden = N/2
-  // EPI_DOWN
+  // EPI_DOWN, EPI_DOWN_ATOMIC
   const float* probs;        // [R] sorted probs
   const float* gs_down;      // [n_experts]
+  // EPI_DOWN_ATOMIC
+  __nv_bfloat16* y;          // [S, H, N] (strides sy_s, sy_h; unit inner stride), zeroed before
+  int64_t sy_s, sy_h;
+  const int32_t* gather_ids; // [R] sorted row -> token
+  int experts_per_head;
   // EPI_RAW
   float* out_f32;            // [128 * n_mtiles, N]
   int* status;
@@ -306,6 +314,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (lane == 0) {
             tma_store_2d(&tmC, stg_s, nt * GEMM_BN + half * 128 + box * 64, mt * GEMM_BM + q * 32);
             bulk_commit();
+          }
+        }
+      } else if constexpr (EPI == EPI_DOWN_ATOMIC) {
+        if (m < p.tile_rows[mt]) {
+          const int64_t srow = (int64_t)p.tile_row0[mt] + m;
+          const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
+          const float pr = p.probs[srow];
+          const int64_t tok = p.gather_ids[srow];
+          const int h = e / p.experts_per_head;
+          __nv_bfloat16* yrow = p.y + tok * p.sy_s + (int64_t)h * p.sy_h + nt * GEMM_BN + half * 128;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {           // 8 columns (16 B) per vector atomic
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = c * 8 + 2 * j;
+              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
+              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
+              __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+              w[j] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            red_add_bf16x8(yrow + c * 8, w);
           }
         }
       } else {

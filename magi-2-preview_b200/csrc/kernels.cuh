@@ -121,7 +121,11 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
               int k_fixed, void* workspace, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, int* status,
               uint64_t timeout_ns, const cudaEvent_t* events, cudaStream_t st, cudaError_t* cerr,
               const uint8_t* xq_in = nullptr, const uint8_t* xsf_in = nullptr, const uint8_t* xg_in = nullptr,
-              int64_t xq_pitch = 0, int64_t xsf_pitch = 0, int64_t xg_pitch = 0, const EpReturn* ret = nullptr);
+              int64_t xq_pitch = 0, int64_t xsf_pitch = 0, int64_t xg_pitch = 0, const EpReturn* ret = nullptr,
+              bool atomic_scatter = false);
+
+// combine.cu: y[s, h, 0:dh] = 0 for every (s, h)
+cudaError_t launch_zero_rows(__nv_bfloat16* y, int S, int H, int dh, int64_t sy_s, int64_t sy_h, cudaStream_t st);
 
 // combine.cu (expert-parallel return)
 cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh,

@@ -122,6 +122,13 @@ __device__ __forceinline__ bool flag_wait_geq(const int* flag, int expected, int
   }
 }
 
+// y[0..8) += v (8 bf16 as 4 packed pairs), one 16-B vector atomic in L2 (16-B aligned).
+__device__ __forceinline__ void red_add_bf16x8(void* y, const uint32_t (&v)[4]) {
+  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(y), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3])
+               : "memory");
+}
+
 // System-scope release add (a flag in another GPU's memory, reached over NVLink).
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

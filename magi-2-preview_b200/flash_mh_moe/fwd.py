@@ -6,12 +6,17 @@ gate/up GEMM -> SwiGLU7 -> down GEMM -> weighted scatter, here as the NVFP4 B200
 
     per-row NVFP4 quantise of the gathered x  ->  tcgen05 block-scaled grouped GEMM
     (gate|up) with SwiGLU7 and NVFP4 re-quantise fused in its epilogue  ->  grouped
-    GEMM (down) x prob  ->  deterministic combine (fp32 sum in sorted-row order).
+    GEMM (down) x prob  ->  scatter into y.
 
 Weights may be the reference's bf16 parameters (packed to NVFP4 on first use and
 cached per parameter version) or already-packed ``NVFP4GateUp`` / ``NVFP4Down``.
-The combine is deterministic by construction, so ``MAGI2_DETERMINISTIC`` (read by the
-reference to pick its scatter) changes nothing here; it is still honoured as a name.
+Scatter: by default partial rows are written and a combine pass sums each token's rows
+in fp32 in sorted-row order (run-to-run identical, one bf16 rounding) — the reference's
+``MAGI2_DETERMINISTIC=1`` behaviour (``fwd.py:12-13``), and on B200 also the faster one.
+``MHMOE_SCATTER=atomic`` (or ``deterministic=False``) selects the reference's default
+scatter instead: the down GEMM adds its bf16 rows into y with bf16 atomics (bf16
+accumulation in arrival order, not run-to-run reproducible); measured slower here, as
+the 16-B vector atomics saturate L2.
 """
 from __future__ import annotations
 
@@ -24,7 +29,9 @@ from .nvfp4 import NVFP4Down, NVFP4GateUp, pack_down, pack_gate_up
 
 
 def _is_deterministic() -> bool:
-    return os.environ.get("MAGI2_DETERMINISTIC", "0") == "1"
+    """Combine scatter unless MHMOE_SCATTER=atomic (the combine also satisfies the
+    reference's MAGI2_DETERMINISTIC=1)."""
+    return os.environ.get("MHMOE_SCATTER", "combine") != "atomic"
 
 
 _pack_cache: dict[tuple, tuple] = {}
@@ -64,9 +71,12 @@ def clear_pack_cache() -> None:
 def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tensor, expert_offsets: torch.Tensor,
               gu: NVFP4GateUp, dn: NVFP4Down, tok_rows: torch.Tensor | None = None,
               tok_offsets: torch.Tensor | None = None, k_fixed: int = 0,
-              out: torch.Tensor | None = None, stage_events=None) -> torch.Tensor:
+              out: torch.Tensor | None = None, stage_events=None,
+              deterministic: bool | None = None) -> torch.Tensor:
     """NVFP4 expert FFN on x_heads [S, H, dh] bf16 -> y [S, H, dh] bf16.
 
+    ``deterministic``: None -> ``MHMOE_SCATTER`` (default combine); False -> atomic scatter
+    from the down GEMM (tok_rows / tok_offsets / k_fixed unused); True -> partials + combine.
     ``stage_events``: optional 5 ``torch.cuda.Event`` recorded on the current stream
     before the tile tables, gate/up GEMM, down GEMM, combine, and at the end.
     """
@@ -91,13 +101,23 @@ def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tens
     offs = expert_offsets.to(torch.int64).contiguous()
     L = _lib.lib()
     ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, S, H, dh, de, n)), dtype=torch.uint8, device=dev)
+    if deterministic is None:
+        deterministic = _is_deterministic()
     with torch.cuda.device(dev):
-        _lib.check(L.mhmoe_ffn_nvfp4(
-            x.data_ptr(), x.stride(0), x.stride(1), S, H, dh, de, n, R, gids.data_ptr(), ps.data_ptr(),
-            offs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(),
-            dn.sf.data_ptr(), dn.gscale.data_ptr(), _lib.ptr(tok_rows), _lib.ptr(tok_offsets), int(k_fixed),
-            ws.data_ptr(), y.data_ptr(), y.stride(0), y.stride(1), _lib.device_status(dev).data_ptr(), 0,
-            _events(stage_events), _lib.stream_ptr(dev)), "flash_mh_moe_fwd")
+        if deterministic:
+            _lib.check(L.mhmoe_ffn_nvfp4(
+                x.data_ptr(), x.stride(0), x.stride(1), S, H, dh, de, n, R, gids.data_ptr(), ps.data_ptr(),
+                offs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(),
+                dn.sf.data_ptr(), dn.gscale.data_ptr(), _lib.ptr(tok_rows), _lib.ptr(tok_offsets), int(k_fixed),
+                ws.data_ptr(), y.data_ptr(), y.stride(0), y.stride(1), _lib.device_status(dev).data_ptr(), 0,
+                _events(stage_events), _lib.stream_ptr(dev)), "flash_mh_moe_fwd")
+        else:
+            _lib.check(L.mhmoe_ffn_nvfp4_atomic(
+                x.data_ptr(), x.stride(0), x.stride(1), S, H, dh, de, n, R, gids.data_ptr(), ps.data_ptr(),
+                offs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(), gu.gscale.data_ptr(), dn.data.data_ptr(),
+                dn.sf.data_ptr(), dn.gscale.data_ptr(), ws.data_ptr(), y.data_ptr(), y.stride(0), y.stride(1),
+                _lib.device_status(dev).data_ptr(), 0, _events(stage_events), _lib.stream_ptr(dev)),
+                "flash_mh_moe_fwd")
     return y
 
 

@@ -34,9 +34,13 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("scatter", ["combine", "atomic"])
 @pytest.mark.parametrize("S,H,dh,de,E,K,seed,skew", CASES)
-def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew):
+def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew, scatter, monkeypatch):
+    """combine: partial rows + fp32 combine (the oracle's order, ~0 error); atomic: bf16
+    atomics from the down GEMM (bf16 accumulation in arrival order)."""
     from flash_mh_moe import flash_mh_moe_fwd
+    monkeypatch.setenv("MHMOE_SCATTER", scatter)
     x, gate, Wg, Wu, Wd = seeded_moe(S, H, dh, de, E, K, seed)
     gids, ps, offs = _route(x, gate, S, H, dh, E, K, skew)
     xh = x.reshape(S, H, dh)
@@ -57,8 +61,10 @@ def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew):
     print(f"rel L2 vs oracle {err:.2e}; vs bf16 reference (NVFP4 quantisation error) {rel_l2(got, bf):.3f}")
 
 
-def test_ffn_deterministic_and_empty():
+@pytest.mark.parametrize("scatter", ["combine", "atomic"])
+def test_ffn_deterministic_and_empty(scatter, monkeypatch):
     from flash_mh_moe import flash_mh_moe_fwd
+    monkeypatch.setenv("MHMOE_SCATTER", scatter)
     S, H, dh, de, E, K = 300, 1, 256, 256, 8, 2
     x, gate, Wg, Wu, Wd = seeded_moe(S, H, dh, de, E, K, 9)
     gids, ps, offs = _route(x, gate, S, H, dh, E, K)
@@ -66,7 +72,10 @@ def test_ffn_deterministic_and_empty():
             torch.from_numpy(offs).cuda(), bf16_tensor(Wg), bf16_tensor(Wu), bf16_tensor(Wd))
     y1 = flash_mh_moe_fwd(*args)
     y2 = flash_mh_moe_fwd(*args)
-    assert torch.equal(y1, y2)
+    if scatter == "combine":
+        assert torch.equal(y1, y2)
+    else:   # atomic order may differ run to run: bf16 rounding only
+        assert rel_l2(to_np(y1), to_np(y2)) < 1e-2
     # no routed rows -> zeros (reference mh_moe_fwd.py:297-298)
     z = flash_mh_moe_fwd(args[0], torch.empty(0, dtype=torch.int32, device="cuda"),
                          torch.empty(0, device="cuda"), torch.zeros(E + 1, dtype=torch.int64, device="cuda"),

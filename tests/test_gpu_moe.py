@@ -19,8 +19,10 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("scatter", ["combine", "atomic"])
 @pytest.mark.parametrize("S,H,dh,de,E,K,score,scale,use_bias", CASES)
-def test_module_forward_matches_oracle(S, H, dh, de, E, K, score, scale, use_bias):
+def test_module_forward_matches_oracle(S, H, dh, de, E, K, score, scale, use_bias, scatter, monkeypatch):
+    monkeypatch.setenv("MHMOE_SCATTER", scatter)
     from flash_mh_moe import _lib
     from flash_mh_moe.moe import CoreMultiHeadMoE, CoreMultiHeadMoEConfig, init_moe_params_
     from flash_mh_moe.route import route_fused
@@ -38,7 +40,10 @@ def test_module_forward_matches_oracle(S, H, dh, de, E, K, score, scale, use_bia
     y2 = torch.ops.magi2_b200.mh_moe(x, m._moe_key)
     torch.cuda.synchronize()
     _lib.check_device_status(dev)
-    assert torch.equal(y, y2)
+    if scatter == "combine":
+        assert torch.equal(y, y2)
+    else:   # bf16 atomics: the summation order may change the last bits
+        assert rel_l2(y.float().cpu().numpy(), y2.float().cpu().numpy()) < 1e-2
     # oracle on the same logits the fused router computes
     planes, nsplit = m.router_planes()
     bias = m.router.expert_bias.view(H, E) if use_bias else None
