@@ -1,6 +1,7 @@
 // Host orchestration of the NVFP4 expert FFN: workspace carving, TMA descriptors and
 // the launch sequence  tile tables -> gather/quantise -> gate/up GEMM (+SwiGLU7,
 // hidden quantise) -> down GEMM (x prob) -> token map -> combine.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -31,7 +32,7 @@ static PFN_encodeTiled get_encode_fn() {
 // 2-D tensor map over [rows, inner] elements with the given row stride, 128-B swizzle.
 cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                            uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
-                           uint32_t box_rows) {
+                           uint32_t box_rows, bool swizzle128) {
   PFN_encodeTiled fn = get_encode_fn();
   if (!fn) return cudaErrorNotSupported;
   const cuuint64_t dims[2] = {inner, rows};
@@ -40,7 +41,8 @@ cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataTy
   const cuuint32_t estr[2] = {1, 1};
   (void)elem_bytes;
   const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
@@ -57,6 +59,42 @@ int num_sms() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n > 0 ? n : 148;
+}
+
+// SF atom array of `bytes` bytes as [bytes/256, 256] u8 rows, box 256 x 8 (one 2 KB m/n-tile stage).
+static cudaError_t encode_sf_map(CUtensorMap* map, const void* base, uint64_t bytes) {
+  return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, bytes / 256, 256, 256, 8, false);
+}
+
+// The CTA-pair GEMM is used unless MHMOE_GEMM_PAIR=0.
+static bool use_pair_gemm() {
+  const char* v = std::getenv("MHMOE_GEMM_PAIR");
+  return !(v && v[0] == '0');
+}
+
+template <int EPI>
+static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                                    const CUtensorMap& tsfa, const CUtensorMap& tsfb, const FfnGemmParams& p,
+                                    int64_t max_work, cudaStream_t st) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int max_clusters = 0;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(ffn_gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    gemmp_smem_bytes(EPI));
+    if (attr_err != cudaSuccess) return;
+    // the kernel's cluster shape (2, 1, 1) is compiled in, so the query config names none
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = gemmp_smem_bytes(EPI);
+    attr_err = cudaOccupancyMaxActiveClusters(&max_clusters, ffn_gemm_pair_kernel<EPI>, &cfg);
+    if (attr_err == cudaSuccess && max_clusters <= 0) attr_err = cudaErrorInvalidConfiguration;
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(max_clusters, max_work));
+  ffn_gemm_pair_kernel<EPI><<<2 * clusters, GEMM_THREADS, gemmp_smem_bytes(EPI), st>>>(ta, tb, tc, tsfa, tsfb, p);
+  return cudaGetLastError();
 }
 
 template <int EPI>
@@ -101,7 +139,7 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 static FfnWorkspace carve(uint8_t* base, int64_t R, int64_t T, int dh, int de, int HE) {
   FfnWorkspace w{};
-  const int64_t mt = mtiles_upper_bound(R, HE);
+  const int64_t mt = mtiles_upper_bound(R, HE, 2);     // covers both tile alignments
   const int64_t rows = mt * 128;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -153,7 +191,8 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     xsf_pitch = dh / 16;
     xg_pitch = sizeof(float);
   }
-  const int64_t max_mt = mtiles_upper_bound(R, HE);
+  const bool pair = use_pair_gemm();
+  const int64_t max_mt = mtiles_upper_bound(R, HE, 2);
   const int64_t rows = max_mt * 128;
   cudaError_t e;
 #define MHMOE_TRY(call)        \
@@ -170,7 +209,7 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   };
   mark(0);
   MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
-                               status, st));
+                               status, st, pair ? 2 : 1));
   MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
   if (!prequant) MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
   MHMOE_TRY(launch_group_rows(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H, HE / H, gather_ids, w.cu_tiles,
@@ -184,6 +223,15 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
       encode_tmap_2d_u8(&tb2, dn_data, de / 2, (uint64_t)HE * dh, 128, 256) != cudaSuccess ||
       encode_tmap_2d(&tc2, w.P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, dh, rows, (uint64_t)dh * 2, 64, 32) !=
           cudaSuccess)
+    return MHMOE_ERR_DRIVER;
+  // CTA-pair operands: B tiles of 128 rows, SF atoms through TMA
+  CUtensorMap tb1p, tb2p, tsfa1, tsfb1, tsfa2, tsfb2;
+  if (pair && (encode_tmap_2d_u8(&tb1p, gu_data, dh / 2, (uint64_t)HE * 2 * de, 128, 128) != cudaSuccess ||
+               encode_tmap_2d_u8(&tb2p, dn_data, de / 2, (uint64_t)HE * dh, 128, 128) != cudaSuccess ||
+               encode_sf_map(&tsfa1, w.a_sf, (uint64_t)rows * dh / 16) != cudaSuccess ||
+               encode_sf_map(&tsfb1, gu_sf, (uint64_t)HE * 2 * de * dh / 16) != cudaSuccess ||
+               encode_sf_map(&tsfa2, w.h_sf, (uint64_t)rows * de / 16) != cudaSuccess ||
+               encode_sf_map(&tsfb2, dn_sf, (uint64_t)HE * dh * de / 16) != cudaSuccess))
     return MHMOE_ERR_DRIVER;
 
   mark(1);
@@ -204,7 +252,10 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   p1.h_sf = w.h_sf;
   p1.status = status;
   p1.timeout_ns = timeout_ns;
-  MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, ta1, p1, max_mt * (2 * de / GEMM_BN), st));
+  if (pair)
+    MHMOE_TRY(launch_gemm_pair<EPI_SWIGLU>(ta1, tb1p, ta1, tsfa1, tsfb1, p1, max_mt / 2 * (2 * de / GEMM_BN), st));
+  else
+    MHMOE_TRY(launch_gemm<EPI_SWIGLU>(ta1, tb1, ta1, p1, max_mt * (2 * de / GEMM_BN), st));
 
   mark(2);
   FfnGemmParams p2 = p1;
@@ -222,12 +273,18 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     p2.gather_ids = gather_ids;
     p2.experts_per_head = HE / H;
     MHMOE_TRY(launch_zero_rows(y, S, H, dh, sy_s, sy_h, st));
-    MHMOE_TRY(launch_gemm<EPI_DOWN_ATOMIC>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
+    if (pair)
+      MHMOE_TRY(launch_gemm_pair<EPI_DOWN_ATOMIC>(ta2, tb2p, tc2, tsfa2, tsfb2, p2, max_mt / 2 * (dh / GEMM_BN), st));
+    else
+      MHMOE_TRY(launch_gemm<EPI_DOWN_ATOMIC>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
     mark(3);
     mark(4);
     return MHMOE_OK;
   }
-  MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
+  if (pair)
+    MHMOE_TRY(launch_gemm_pair<EPI_DOWN>(ta2, tb2p, tc2, tsfa2, tsfb2, p2, max_mt / 2 * (dh / GEMM_BN), st));
+  else
+    MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
 
   mark(3);
   const int32_t* rows_map = tok_rows;

@@ -59,6 +59,17 @@ __host__ __device__ constexpr int gemm_smem_bytes(int epi) {
   return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
 }
 
+// CTA-pair variant (cluster of 2, cta_group::2): M = 256 rows per pair (128 per CTA), each
+// CTA stages its own A rows, HALF of the 256-row B tile and the full B scale factors, so
+// B crosses L2 -> SM once per pair instead of once per CTA.
+constexpr int GEMMP_B_BYTES = (GEMM_BN / 2) * GEMM_BK / 2;    // 16384
+constexpr int GEMMP_STAGE_TX = GEMM_A_BYTES + GEMMP_B_BYTES + GEMM_SFA_BYTES + GEMM_SFB_BYTES;   // per CTA
+constexpr int GEMMP_STAGE_BYTES = GEMMP_STAGE_TX;
+__host__ __device__ constexpr int gemmp_stages(int epi) { return epi == EPI_DOWN ? 4 : 5; }
+__host__ __device__ constexpr int gemmp_smem_bytes(int epi) {
+  return gemmp_stages(epi) * GEMMP_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
+}
+
 // Static second-level scale of the SwiGLU7 hidden: |swiglu7| <= 7 * 8 = 56, 56 / 2688.
 constexpr float HIDDEN_GSCALE = 56.0f / 2688.0f;
 
@@ -97,6 +108,105 @@ __device__ __forceinline__ float swiglu7(float g, float u) {
   u = fminf(fmaxf(u, -7.0f), 7.0f);
   const float sig = __frcp_rn(1.0f + __expf(-1.702f * g));
   return g * sig * (u + 1.0f);
+}
+
+// Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
+// accumulator columns [128*half, 128*half + 128) already in registers (r), TMEM released.
+// stg: this warp's 4 KB store staging (EPI_DOWN).
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const CUtensorMap* tmC,
+                                                   const uint32_t (&r)[128], int mt, int nt, int m, int q, int half,
+                                                   int lane, uint8_t* stg) {
+  const int e = p.tile_expert[mt];
+  const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
+  if constexpr (EPI == EPI_SWIGLU) {
+    const float gr = p.row_gscale[prow];
+    const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
+    const float s_up = __fmul_rn(gr, p.gs_up[e]);
+    const int hid_cols = p.N / 2;
+    uint32_t words[8];
+    uint32_t sfw = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float hv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float g = __fmul_rn(__uint_as_float(r[c * 32 + i]), s_gate);
+        const float u = __fmul_rn(__uint_as_float(r[c * 32 + 16 + i]), s_up);
+        hv[i] = swiglu7(g, u);
+      }
+      uint32_t w2[2];
+      const uint32_t sf = quant_block16(hv, HIDDEN_GSCALE, w2);
+      words[2 * c] = w2[0];
+      words[2 * c + 1] = w2[1];
+      sfw |= sf << (8 * c);
+    }
+    const int hcol0 = nt * (GEMM_BN / 2) + half * 64;          // first hidden column of this thread
+    uint4* dst = reinterpret_cast<uint4*>(p.h_data + prow * (size_t)(hid_cols / 2) + hcol0 / 2);
+    dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+    dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    *reinterpret_cast<uint32_t*>(p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols)) =
+        sfw;
+  } else if constexpr (EPI == EPI_DOWN) {
+    const int nrows = p.tile_rows[mt];
+    const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
+    const float pr = m < nrows ? p.probs[p.tile_row0[mt] + m] : 0.0f;
+    const uint32_t stg_s = smem_u32(stg);
+#pragma unroll
+    for (int box = 0; box < 2; ++box) {
+      // the previous box's TMA store must have finished reading the staging buffer
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {            // 16-B chunk c of this row: columns box*64 + 8c .. +7
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = box * 64 + c * 8 + 2 * j;
+          const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
+          const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+          w[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        // 128-B swizzle: chunk c of row `lane` sits at chunk c ^ (lane & 7)
+        *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, stg_s, nt * GEMM_BN + half * 128 + box * 64, mt * GEMM_BM + q * 32);
+        bulk_commit();
+      }
+    }
+  } else if constexpr (EPI == EPI_DOWN_ATOMIC) {
+    if (m < p.tile_rows[mt]) {
+      const int64_t srow = (int64_t)p.tile_row0[mt] + m;
+      const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
+      const float pr = p.probs[srow];
+      const int64_t tok = p.gather_ids[srow];
+      const int h = e / p.experts_per_head;
+      __nv_bfloat16* yrow = p.y + tok * p.sy_s + (int64_t)h * p.sy_h + nt * GEMM_BN + half * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {           // 8 columns (16 B) per vector atomic
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int col = c * 8 + 2 * j;
+          const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
+          const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
+          w[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        red_add_bf16x8(yrow + c * 8, w);
+      }
+    }
+  } else {
+    float4* dst = reinterpret_cast<float4*>(p.out_f32 + prow * (size_t)p.N + nt * GEMM_BN + half * 128);
+#pragma unroll
+    for (int v = 0; v < 32; ++v)
+      dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                           __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+  }
 }
 
 // tmA: grouped A operand [128 * n_mtiles, K/2], box 128 x 128.
@@ -254,97 +364,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
 
-      const int e = p.tile_expert[mt];
-      const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
-      if constexpr (EPI == EPI_SWIGLU) {
-        const float gr = p.row_gscale[prow];
-        const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
-        const float s_up = __fmul_rn(gr, p.gs_up[e]);
-        const int hid_cols = p.N / 2;
-        uint32_t words[8];
-        uint32_t sfw = 0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float hv[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float g = __fmul_rn(__uint_as_float(r[c * 32 + i]), s_gate);
-            const float u = __fmul_rn(__uint_as_float(r[c * 32 + 16 + i]), s_up);
-            hv[i] = swiglu7(g, u);
-          }
-          uint32_t w2[2];
-          const uint32_t sf = quant_block16(hv, HIDDEN_GSCALE, w2);
-          words[2 * c] = w2[0];
-          words[2 * c + 1] = w2[1];
-          sfw |= sf << (8 * c);
-        }
-        const int hcol0 = nt * (GEMM_BN / 2) + half * 64;          // first hidden column of this thread
-        uint4* dst = reinterpret_cast<uint4*>(p.h_data + prow * (size_t)(hid_cols / 2) + hcol0 / 2);
-        dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-        dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-        *reinterpret_cast<uint32_t*>(p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols)) =
-            sfw;
-      } else if constexpr (EPI == EPI_DOWN) {
-        const int nrows = p.tile_rows[mt];
-        const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
-        const float pr = m < nrows ? p.probs[p.tile_row0[mt] + m] : 0.0f;
-        uint8_t* stg = sSTG + (warp - 2) * (32 * 128);
-        const uint32_t stg_s = smem_u32(stg);
-#pragma unroll
-        for (int box = 0; box < 2; ++box) {
-          // the previous box's TMA store must have finished reading the staging buffer
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {            // 16-B chunk c of this row: columns box*64 + 8c .. +7
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = box * 64 + c * 8 + 2 * j;
-              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
-              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-              w[j] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            // 128-B swizzle: chunk c of row `lane` sits at chunk c ^ (lane & 7)
-            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmC, stg_s, nt * GEMM_BN + half * 128 + box * 64, mt * GEMM_BM + q * 32);
-            bulk_commit();
-          }
-        }
-      } else if constexpr (EPI == EPI_DOWN_ATOMIC) {
-        if (m < p.tile_rows[mt]) {
-          const int64_t srow = (int64_t)p.tile_row0[mt] + m;
-          const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
-          const float pr = p.probs[srow];
-          const int64_t tok = p.gather_ids[srow];
-          const int h = e / p.experts_per_head;
-          __nv_bfloat16* yrow = p.y + tok * p.sy_s + (int64_t)h * p.sy_h + nt * GEMM_BN + half * 128;
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {           // 8 columns (16 B) per vector atomic
-            uint32_t w[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int col = c * 8 + 2 * j;
-              const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
-              const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
-              __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
-              w[j] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            red_add_bf16x8(yrow + c * 8, w);
-          }
-        }
-      } else {
-        float4* dst = reinterpret_cast<float4*>(p.out_f32 + prow * (size_t)p.N + nt * GEMM_BN + half * 128);
-#pragma unroll
-        for (int v = 0; v < 32; ++v)
-          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-      }
+      gemm_epilogue_tile<EPI>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();     // stores complete before the CTA exits
@@ -362,6 +382,202 @@ done:
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, GEMM_TMEM_COLS);
+  }
+}
+
+// ───────────────────────────── CTA-pair kernel ─────────────────────────────
+// Work item = (pair of m-tiles 2*pt, 2*pt+1 of one expert, n-tile).  CTA rank r of the
+// cluster owns m-tile 2*pt + r.  Roles as in the single-CTA kernel, except:
+//   producer (both CTAs): TMA loads into its own shared memory (A rows, B rows
+//     [nt*256 + 128*r, +128), SFA, full SFB) that signal the LEADER's full barrier; the
+//     leader's producer posts the expected bytes of both CTAs.
+//   MMA (leader only): tcgen05.cp / tcgen05.mma with cta_group::2 (each CTA's shared memory
+//     at the same offsets -> its own TMEM), commits to the stage's empty barrier of both
+//     CTAs and, per tile, to both CTAs' accumulator-full barrier.
+//   epilogue (both CTAs): its own 128 rows; releases the accumulator on the leader's
+//     barrier (16 arrivals per tile).
+// tmSFA / tmSFB: the SF atom arrays viewed as [bytes/256, 256] u8, box 256 x 8 (2 KB).
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    ffn_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmSFA,
+                         const __grid_constant__ CUtensorMap tmSFB, const FfnGemmParams p) {
+  constexpr int STAGES = gemmp_stages(EPI);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + STAGES * GEMM_A_BYTES;
+  uint8_t* sSFA = sB + STAGES * GEMMP_B_BYTES;
+  uint8_t* sSFB = sSFA + STAGES * GEMM_SFA_BYTES;
+  uint8_t* sSTG = sSFB + STAGES * GEMM_SFB_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSTG + (EPI == EPI_DOWN ? GEMM_STG_BYTES : 0));
+  uint64_t* full_bar = bars;                       // [STAGES] (leader's are used)
+  uint64_t* empty_bar = bars + STAGES;             // [STAGES]
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = tfull_bar + 1;            // (leader's is used)
+  uint64_t* drain_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    mbar_init(smem_u32(tfull_bar), 1);
+    mbar_init(smem_u32(tempty_bar), 16);
+    mbar_init(smem_u32(drain_bar), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmSFA);
+    tma_prefetch_desc(&tmSFB);
+    if (EPI == EPI_DOWN) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), GEMM_TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();                                  // barriers initialised, TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_mtiles = p.n_mtiles_dev ? min(*p.n_mtiles_dev, p.n_mtiles_host) : p.n_mtiles_host;
+  const int n_pairs = n_mtiles / 2;
+  const int n_ntiles = p.N / GEMM_BN;
+  const int n_kblk = p.K / GEMM_BK;
+  const int total = n_pairs * n_ntiles;
+  const int cluster_id = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+  const uint64_t timeout = p.timeout_ns ? p.timeout_ns : 2000000000ull;
+
+  if (warp == 0) {
+    // ───────── producer (both CTAs; whole warp waits, lane 0 issues) ─────────
+    int stage = 0;
+    uint32_t phase = 0;
+    int64_t issued = 0;
+    bool ok = true;
+    const int k_atoms = p.K / 64;
+    const int64_t sfb_rows_per_expert = (int64_t)p.N * (p.K / 16) / 256;
+    for (int t = cluster_id; ok && t < total; t += n_clusters) {
+      const int pt = t / n_ntiles, nt = t % n_ntiles;
+      const int mt = 2 * pt + (int)crank;
+      const int e = p.tile_expert[mt];
+      const int brow = e * p.N + nt * GEMM_BN + (int)crank * (GEMM_BN / 2);
+      for (int kb = 0; kb < n_kblk; ++kb) {
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const uint32_t fb_local = smem_u32(&full_bar[stage]);
+          const uint32_t fb = mapa_shared(fb_local, 0);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2u * GEMMP_STAGE_TX);
+          tma_load_2d_pair(smem_u32(sA + stage * GEMM_A_BYTES), &tmA, fb, kb * (GEMM_BK / 2), mt * GEMM_BM);
+          tma_load_2d_pair(smem_u32(sB + stage * GEMMP_B_BYTES), &tmB, fb, kb * (GEMM_BK / 2), brow);
+          tma_load_2d_pair(smem_u32(sSFA + stage * GEMM_SFA_BYTES), &tmSFA, fb, 0, (mt * k_atoms + kb * 4) * 2);
+#pragma unroll
+          for (int nb = 0; nb < 2; ++nb)
+            tma_load_2d_pair(smem_u32(sSFB + stage * GEMM_SFB_BYTES + nb * 2048), &tmSFB, fb, 0,
+                             (int)(e * sfb_rows_per_expert + ((nt * 2 + nb) * k_atoms + kb * 4) * 2));
+        }
+        __syncwarp();
+        ++issued;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    // The leader's full barriers count both CTAs' bytes: once the last STAGES of them
+    // completed, every copy of the pair has landed (returns at once on the normal path).
+    if (leader)
+      for (int64_t i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
+        mbar_wait(smem_u32(&full_bar[i % STAGES]), (uint32_t)((i / STAGES) & 1), nullptr, 0, MHMOE_DRAIN_NS);
+  } else if (warp == 1) {
+    // ───────── MMA issuer: the leader CTA only ─────────
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      constexpr uint32_t idesc = idesc_nvf4(2 * GEMM_BM, GEMM_BN);
+      for (int t = cluster_id; t < total; t += n_clusters) {
+        if (!mbar_wait(smem_u32(tempty_bar), acc_phase ^ 1, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        tc_fence_after();
+        for (int kb = 0; kb < n_kblk; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
+            const uint32_t tsfb = tsfa + 16;
+            const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
+            const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tc_cp_32x128b_warpx4_pair(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
+              tc_cp_32x128b_warpx4_pair(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
+              tc_cp_32x128b_warpx4_pair(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
+            }
+            const uint32_t a_s = smem_u32(sA + stage * GEMM_A_BYTES);
+            const uint32_t b_s = smem_u32(sB + stage * GEMMP_B_BYTES);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              mma_nvf4_pair(tmem_base, sdesc_kmajor_sw128(a_s + j * 32), sdesc_kmajor_sw128(b_s + j * 32), idesc,
+                            tsfa + j * 4, tsfb + j * 8, (kb | j) != 0 ? 1u : 0u);
+            const uint32_t eb = smem_u32(&empty_bar[stage]);
+            tc_commit_pair(mapa_shared(eb, 0));
+            tc_commit_pair(mapa_shared(eb, 1));
+          }
+          __syncwarp();
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (lane == 0) {
+          tc_commit_pair(mapa_shared(smem_u32(tfull_bar), 0));
+          tc_commit_pair(mapa_shared(smem_u32(tfull_bar), 1));
+        }
+        __syncwarp();
+        acc_phase ^= 1;
+      }
+    }
+  } else {
+    // ───────── epilogue warps 2..9 (both CTAs, own 128 rows) ─────────
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int m = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty_bar), 0);
+    uint32_t acc_phase = 0;
+    for (int t = cluster_id; t < total; t += n_clusters) {
+      const int pt = t / n_ntiles, nt = t % n_ntiles;
+      const int mt = 2 * pt + (int)crank;
+      if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
+      acc_phase ^= 1;
+      tc_fence_after();
+      uint32_t r[128];
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 128);
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 0, (r + 0));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 32, (r + 32));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 64, (r + 64));
+      MHMOE_TMEM_LD_32x32b_X32(taddr + 96, (r + 96));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader);
+      gemm_epilogue_tile<EPI>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+    }
+    if constexpr (EPI == EPI_DOWN) {
+      if (lane == 0) bulk_wait_all();
+    }
+  }
+done:
+  if (leader && warp == 1 && lane == 0) {
+    tc_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+    mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
+  }
+  tc_fence_before();
+  cluster_sync();                                  // neither CTA leaves while the pair still uses it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, GEMM_TMEM_COLS);
   }
 }
 

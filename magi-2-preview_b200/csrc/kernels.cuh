@@ -10,7 +10,10 @@
 namespace mhmoe {
 
 // Upper bound of 128-row tiles for R rows spread over n_experts groups.
-inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts) { return (R + 127) / 128 + n_experts; }
+// align: tiles per expert rounded up to a multiple of align (2 for the CTA-pair GEMM).
+inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts, int align = 1) {
+  return (R + 127) / 128 + (int64_t)align * n_experts;
+}
 
 // ───────── expert-parallel peer buffers (ep_p2p.cu, combine.cu) ─────────
 // Every rank allocates one buffer with this layout and maps every peer's (CUDA IPC):
@@ -75,7 +78,8 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
                                int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
                                int32_t* row_of_flat, int* status, cudaStream_t st, int min_chunk = 256);
 cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
-                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st);
+                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st,
+                               int align = 1);
 size_t token_rows_ws_bytes(int64_t T);
 cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, const int* cu_tiles, int HE, int E,
                               int S, int H, const int* tile_expert, const int* tile_row0, const int* tile_rows,
@@ -160,7 +164,7 @@ cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner
                               uint32_t box_inner, uint32_t box_rows);
 cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
                            uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
-                           uint32_t box_rows);
+                           uint32_t box_rows, bool swizzle128 = true);
 
 // wait_selftest.cu
 cudaError_t launch_wait_selftest(const int* flag, int expected, int mode, uint64_t timeout_ns, int* status,

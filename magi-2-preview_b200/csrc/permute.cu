@@ -64,7 +64,8 @@ __global__ void sort_colscan_kernel(int* __restrict__ hist, int nchunks, int HE,
 __global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t* __restrict__ offsets_in,
                                    int HE, int64_t* __restrict__ offsets_out, int* __restrict__ cu_tiles,
                                    int* __restrict__ tile_expert, int* __restrict__ tile_row0,
-                                   int* __restrict__ tile_rows, int64_t max_mtiles, int* __restrict__ status) {
+                                   int* __restrict__ tile_rows, int64_t max_mtiles, int* __restrict__ status,
+                                   int align) {
   __shared__ int64_t s_carry_rows;
   __shared__ int s_carry_tiles;
   __shared__ int64_t s_rows[1024];
@@ -82,7 +83,7 @@ __global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t
       record_error(status, MHMOE_ERR_ARGS);
       cnt = 0;
     }
-    const int nt = (int)((cnt + 127) / 128);
+    const int nt = (int)(((cnt + 127) / 128 + align - 1) / align * align);
     s_rows[threadIdx.x] = cnt;
     s_tiles[threadIdx.x] = nt;
     __syncthreads();
@@ -112,7 +113,8 @@ __global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t
         }
         tile_expert[tile_excl + j] = g;
         tile_row0[tile_excl + j] = (int)(row0 + 128 * j);
-        tile_rows[tile_excl + j] = (int)(cnt - 128 * j < 128 ? cnt - 128 * j : 128);
+        const int64_t left = cnt - 128 * (int64_t)j;           // <= 0 on alignment padding tiles
+        tile_rows[tile_excl + j] = (int)(left < 0 ? 0 : left < 128 ? left : 128);
       }
     }
     __syncthreads();
@@ -298,7 +300,7 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   sort_hist_kernel<<<nchunks, 256, shb, st>>>(idx, R, S * K, E, HE, chunk, hist, status);
   sort_colscan_kernel<<<(HE + 7) / 8, 256, 0, st>>>(hist, nchunks, HE, total);
   tile_tables_kernel<<<1, 1024, 0, st>>>(total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
-                                         tile_rows, mtiles_upper_bound(R, HE), status);
+                                         tile_rows, mtiles_upper_bound(R, HE), status, 1);
   sort_scatter_kernel<<<nchunks, 32, shb, st>>>(idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
                                                 gather_ids, probs_sorted, row_of_flat);
   return cudaGetLastError();
@@ -313,9 +315,10 @@ size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk) {
 }
 
 cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
-                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st) {
+                               int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st,
+                               int align) {
   tile_tables_kernel<<<1, 1024, 0, st>>>(nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert, tile_row0,
-                                         tile_rows, max_tiles, status);
+                                         tile_rows, max_tiles, status, align);
   return cudaGetLastError();
 }
 

@@ -34,13 +34,16 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("gemm", ["pair", "single"])
 @pytest.mark.parametrize("scatter", ["combine", "atomic"])
 @pytest.mark.parametrize("S,H,dh,de,E,K,seed,skew", CASES)
-def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew, scatter, monkeypatch):
+def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew, scatter, gemm, monkeypatch):
     """combine: partial rows + fp32 combine (the oracle's order, ~0 error); atomic: bf16
-    atomics from the down GEMM (bf16 accumulation in arrival order)."""
+    atomics from the down GEMM (bf16 accumulation in arrival order).  pair: the CTA-pair
+    (cta_group::2) GEMMs, the default; single: one CTA per tile (MHMOE_GEMM_PAIR=0)."""
     from flash_mh_moe import flash_mh_moe_fwd
     monkeypatch.setenv("MHMOE_SCATTER", scatter)
+    monkeypatch.setenv("MHMOE_GEMM_PAIR", "1" if gemm == "pair" else "0")
     x, gate, Wg, Wu, Wd = seeded_moe(S, H, dh, de, E, K, seed)
     gids, ps, offs = _route(x, gate, S, H, dh, E, K, skew)
     xh = x.reshape(S, H, dh)
