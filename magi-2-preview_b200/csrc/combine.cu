@@ -6,6 +6,8 @@
 // deterministic _scatter_back (:229-255).  P already holds bf16(y_acc * prob) per
 // sorted row, exactly the values the reference scatters; the sum is taken in fp32
 // in a fixed order, so the result is run-to-run identical.
+#include <cstdlib>
+
 #include "kernels.cuh"
 
 namespace mhmoe {
@@ -136,10 +138,13 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
 // (source's send position of the record) = meta offset + slot, over NVLink; slots past
 // the source's count are skipped.  The last CTA to finish raises the return flag of
 // this rank in every peer (system-scope release after every CTA's stores).
+// bulk != 0: the sum is built in shared memory and sent with one bulk copy per record
+// (dynamic shared memory: COMBINE_WARPS * dh bf16); else stored directly from registers.
 __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
                                       int dh, const int32_t* __restrict__ tok_rows, int k_fixed, int64_t R,
-                                      int64_t P_rows, const EpReturn r) {
+                                      int64_t P_rows, const EpReturn r, int bulk) {
   __shared__ int srt[COMBINE_WARPS][32];
+  extern __shared__ __align__(128) uint8_t stage_raw[];
   const int warp = threadIdx.x >> 5;
   // work item w -> source (w + me) % n, slot w / n: consecutive warps write to different
   // ranks, so all links carry the returns at once (no rank is the target of everyone)
@@ -153,7 +158,21 @@ __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const
     const int64_t cnt = meta[2 * src], off = meta[2 * src + 1];
     if (slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots) {
       __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
-      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
+      if (bulk) {
+        __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(stage_raw) + (size_t)warp * dh;
+        combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, srow, srt[warp]);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) {
+          bulk_store(yrow, smem_u32(srow), (uint32_t)dh * 2);
+          bulk_commit();
+          bulk_wait_all();                 // written at the destination before the flag release
+          fence_proxy_async_global();
+        }
+        __syncwarp();
+      } else {
+        combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
+      }
     }
   }
   if (ep_last_cta(reinterpret_cast<int*>(r.local + r.layout.off_done) + 1) && threadIdx.x == 0) {
@@ -198,8 +217,12 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
                                   cudaStream_t st) {
   const int64_t keys = (int64_t)r.n * r.cap;
   const int64_t blocks = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
-  combine_return_kernel<<<(unsigned)blocks, COMBINE_WARPS * 32, 0, st>>>(P, pad_of_row, dh, tok_rows, k_fixed, R,
-                                                                         P_rows, r);
+  // bulk copies when MHMOE_EP_BULK=1 and a row is at most 8 KB
+  const char* env = std::getenv("MHMOE_EP_BULK");
+  const int bulk = (env && env[0] == '1') && dh * 2 <= 8192 ? 1 : 0;
+  const size_t smem = bulk ? (size_t)COMBINE_WARPS * dh * 2 : 0;
+  combine_return_kernel<<<(unsigned)blocks, COMBINE_WARPS * 32, smem, st>>>(P, pad_of_row, dh, tok_rows, k_fixed, R,
+                                                                            P_rows, r, bulk);
   return cudaGetLastError();
 }
 

@@ -66,10 +66,12 @@ static cudaError_t encode_sf_map(CUtensorMap* map, const void* base, uint64_t by
   return encode_tmap_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 256, bytes / 256, 256, 256, 8, false);
 }
 
-// The CTA-pair GEMM is used unless MHMOE_GEMM_PAIR=0.
+// The CTA-pair GEMM is used when MHMOE_GEMM_PAIR=1.  It is correct but measured slower
+// than one CTA per tile here: the tcgen05 pipe (scale-factor copies + MMAs) and load
+// latency limit both, the pair pads every expert to 256 rows and couples two SMs.
 static bool use_pair_gemm() {
   const char* v = std::getenv("MHMOE_GEMM_PAIR");
-  return !(v && v[0] == '0');
+  return v && v[0] == '1';
 }
 
 template <int EPI>

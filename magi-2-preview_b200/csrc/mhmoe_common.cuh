@@ -168,6 +168,19 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 // Wait until every committed bulk store of this thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Untiled bulk copy shared -> global (any GPU's memory mapped here, no multicast); both
+// addresses 16-B aligned, bytes % 16 == 0.  Completes with the thread's bulk group.
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+
+// Orders this thread's completed async-proxy global writes (bulk stores) with its later
+// generic-proxy operations (e.g. a release of a flag).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Untiled bulk copy global -> shared; both addresses 16-B aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),

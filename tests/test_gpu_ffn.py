@@ -39,8 +39,8 @@ CASES = [
 @pytest.mark.parametrize("S,H,dh,de,E,K,seed,skew", CASES)
 def test_ffn_nvfp4_matches_oracle(S, H, dh, de, E, K, seed, skew, scatter, gemm, monkeypatch):
     """combine: partial rows + fp32 combine (the oracle's order, ~0 error); atomic: bf16
-    atomics from the down GEMM (bf16 accumulation in arrival order).  pair: the CTA-pair
-    (cta_group::2) GEMMs, the default; single: one CTA per tile (MHMOE_GEMM_PAIR=0)."""
+    atomics from the down GEMM (bf16 accumulation in arrival order).  single: one CTA per
+    tile, the default; pair: the CTA-pair (cta_group::2) GEMMs (MHMOE_GEMM_PAIR=1)."""
     from flash_mh_moe import flash_mh_moe_fwd
     monkeypatch.setenv("MHMOE_SCATTER", scatter)
     monkeypatch.setenv("MHMOE_GEMM_PAIR", "1" if gemm == "pair" else "0")
