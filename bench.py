@@ -177,14 +177,18 @@ def step_explicit(m, x, ev, deterministic=None):
 
 def step_ep(m, x, ev):
     """The expert-parallel module forward spelled out, with events between the stages."""
-    from flash_mh_moe.ep import ep_moe_layer, ep_moe_layer_peer, ep_transport
+    from flash_mh_moe.ep import ep_chunks, ep_moe_layer, ep_moe_layer_peer_pipelined, ep_transport
     x_heads = x.view(-1, m.num_heads, m.d_head)
     ev[0].record()
     probs, idx = m._route(x_heads)
     ev[1].record()
     gu, dn = m.packed_weights()
-    layer = ep_moe_layer_peer if ep_transport(m) == "peer" else ep_moe_layer
-    y = layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7], comm_events=ev[8:12])
+    if ep_transport(m) == "peer":
+        y = ep_moe_layer_peer_pipelined(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, chunks=ep_chunks(),
+                                        stage_events=ev[2:7], comm_events=ev[8:12])
+    else:
+        y = ep_moe_layer(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, stage_events=ev[2:7],
+                         comm_events=ev[8:12])
     ev[7].record()
     return y
 
@@ -378,7 +382,8 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
         out["stages_ms_min_max_over_ranks"] = {k: [min(e[k] for e in every), max(e[k] for e in every)]
                                                for k in stages}
         out["config"]["parallelism"] = (f"ep{world} (token->expert records, "
-                                        + ("fused NVLink peer stores)" if LAST_STATS.get("transport") == "peer"
+                                        + (f"fused NVLink peer stores, {ep_chunks()}-chunk pipeline)"
+                                           if LAST_STATS.get("transport") == "peer"
                                            else "NCCL all-to-all)"))
         if LAST_STATS.get("transport") == "nccl":
             bd, br = LAST_STATS.get("dispatch_remote_bytes", 0), LAST_STATS.get("return_remote_bytes", 0)

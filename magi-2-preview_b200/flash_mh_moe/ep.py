@@ -282,10 +282,10 @@ class PeerExchange:
         dist.barrier(group=group)
 
     @classmethod
-    def get(cls, group, device: torch.device, cap: int, dh: int, K: int) -> "PeerExchange":
-        """The group's exchange on this device, re-created (collectively: every rank passes
-        the same ``cap``) when a larger capacity is needed."""
-        key = (id(group), device.index, int(dh), int(K))
+    def get(cls, group, device: torch.device, cap: int, dh: int, K: int, slot: int = 0) -> "PeerExchange":
+        """The group's exchange on this device (one per pipeline slot), re-created
+        (collectively: every rank passes the same ``cap``) when a larger capacity is needed."""
+        key = (id(group), device.index, int(dh), int(K), int(slot))
         px = cls._cache.get(key)
         if px is None or px.cap < cap:
             if px is not None:
@@ -314,14 +314,16 @@ def _ep_timeout_ns() -> int:
 
 
 def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn,
-                      group, stage_events=None, comm_events=None) -> torch.Tensor:
+                      group, stage_events=None, comm_events=None, slot: int = 0,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
     """Token -> expert EP forward with the exchange fused into the kernels (peer memory).
 
     Same records and result as ``ep_moe_layer``; the record kernel stores into the
     destinations' buffers and the receiver's combine stores each record's sum into the
     source's buffer, each followed by a device-side arrival flag, so there is no count
     exchange and no host synchronisation.  comm_events (optional, 4): around the record
-    send + wait, and around the wait for the returns.
+    send + wait, and around the wait for the returns.  slot: which exchange buffer
+    (pipeline chunk) to use; out: optional [S, H, dh] bf16 destination.
     """
     be = CudaBackend()
     L = _lib.lib()
@@ -335,7 +337,7 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     E_loc = HE // ep
     T = H * S
     dev = x_heads.device
-    px = PeerExchange.get(group, dev, T, dh, K)
+    px = PeerExchange.get(group, dev, T, dh, K, slot)
     st = _lib.stream_ptr(dev)
     status = _lib.device_status(dev).data_ptr()
     timeout = _ep_timeout_ns()
@@ -360,7 +362,8 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     _lib.check(L.mhmoe_ep_unpack_slots(px.local, ep, px.cap, dh, K, E_loc, lidx.data_ptr(), lprobs.data_ptr(),
                                        status, st), "ep_unpack_slots")
     lg, lps, loffs, linv = be.sort(lprobs.view(1, slots, K), lidx.view(1, slots, K), E_loc)
-    LAST_STATS.update(rows_received=loffs[-1], transport="peer")
+    prev = LAST_STATS.get("rows_received") if slot > 0 else None
+    LAST_STATS.update(rows_received=loffs[-1] if prev is None else prev + loffs[-1], transport="peer")
     # 3. FFN on the records in place; its combine returns each record's sum to the source
     R = slots * K
     ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, slots, 1, dh, gu.d_expert, E_loc)), dtype=torch.uint8,
@@ -376,9 +379,55 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     if comm_events:
         comm_events[3].record()
     # 4. source: sum each (head, token)'s returned rows in ascending rank order
-    y = torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
+    y = out if out is not None else torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
     _lib.check(L.mhmoe_combine(px.local + px.off_back, slots, None, dh, S, H, send_slot.data_ptr(), None, ep, slots,
                                y.data_ptr(), y.stride(0), y.stride(1), st), "combine")
+    return y
+
+
+_side_streams: dict = {}
+
+
+def ep_chunks() -> int:
+    """Pipeline depth of the peer-memory EP layer (``MHMOE_EP_CHUNKS``, default 2)."""
+    import os
+    return max(1, int(os.environ.get("MHMOE_EP_CHUNKS", "2")))
+
+
+def ep_moe_layer_peer_pipelined(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int,
+                                gu, dn, group, chunks: int = 2, stage_events=None,
+                                comm_events=None) -> torch.Tensor:
+    """The peer-memory EP layer over ``chunks`` token chunks, each on its own stream with its
+    own exchange buffer: one chunk's returns (link-bound) overlap the next chunk's expert
+    GEMMs (tensor-bound).  Each token's result is computed exactly as unchunked (the same
+    records, experts and summation order).  Events, if given, time chunk 0.
+    """
+    S, H, dh = x_heads.shape
+    if chunks <= 1 or S < 2 * chunks:
+        return ep_moe_layer_peer(x_heads, probs, idx, num_experts, gu, dn, group, stage_events, comm_events)
+    dev = x_heads.device
+    main = torch.cuda.current_stream(dev)
+    streams = _side_streams.setdefault(dev.index, [])
+    while len(streams) < chunks:
+        streams.append(torch.cuda.Stream(device=dev))
+    y = torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
+    ready = torch.cuda.Event()
+    ready.record(main)
+    bounds = [(S * c) // chunks for c in range(chunks + 1)]
+    done = []
+    for c in range(chunks):
+        a, b = bounds[c], bounds[c + 1]
+        s = streams[c]
+        s.wait_event(ready)
+        with torch.cuda.stream(s):
+            ep_moe_layer_peer(x_heads[a:b], probs[:, a:b].contiguous(), idx[:, a:b].contiguous(), num_experts, gu,
+                              dn, group, stage_events if c == 0 else None, comm_events if c == 0 else None,
+                              slot=c, out=y[a:b])
+            ev = torch.cuda.Event()
+            ev.record(s)
+        done.append(ev)
+    for ev in done:
+        main.wait_event(ev)
     return y
 
 
@@ -395,7 +444,7 @@ def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None, comm_events
     probs, idx = module._route(x_heads)
     gu, dn = module.packed_weights()
     if ep_transport(module) == "peer":
-        return ep_moe_layer_peer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
-                                 stage_events=stage_events, comm_events=comm_events)
+        return ep_moe_layer_peer_pipelined(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
+                                           chunks=ep_chunks(), stage_events=stage_events, comm_events=comm_events)
     return ep_moe_layer(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
                         stage_events=stage_events, comm_events=comm_events)

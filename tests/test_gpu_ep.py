@@ -1,5 +1,6 @@
 """GPU, 2 ranks (needs >= 2 GPUs; skipped otherwise): the expert-parallel MoE module, with
-the exchange fused into the kernels (peer memory) and over NCCL, against the single-GPU
+the exchange fused into the kernels (peer memory; unchunked and as a 2-chunk pipeline) and
+over NCCL, against the single-GPU
 module on each rank's own tokens.  The EP layer sums each
 token's experts per rank (bf16 partial sums) before the source adds the ranks, so the
 outputs agree to that rounding: rel L2 <= 1e-2 (typically ~1e-3); EP runs are
@@ -22,14 +23,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, transport):
+def _worker(rank, world, port, q, transport, chunks):
     import sys
     from datetime import timedelta
     from pathlib import Path
     root = Path(__file__).resolve().parent.parent
     sys.path[:0] = [str(root), str(root / "magi-2-preview_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
-                      MHMOE_EP_TRANSPORT=transport, MHMOE_EP_TIMEOUT_S="5")
+                      MHMOE_EP_TRANSPORT=transport, MHMOE_EP_TIMEOUT_S="5", MHMOE_EP_CHUNKS=str(chunks))
     import torch.distributed as dist
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -64,13 +65,13 @@ def _worker(rank, world, port, q, transport):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport", ["peer", "nccl"])
-def test_ep_module_matches_single_gpu(transport):
+@pytest.mark.parametrize("transport,chunks", [("peer", 1), ("peer", 2), ("nccl", 1)])
+def test_ep_module_matches_single_gpu(transport, chunks):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, transport)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, transport, chunks)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
