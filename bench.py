@@ -13,8 +13,13 @@ packed to NVFP4 at load).  Inputs are larger than L2 (0.68 GB of NVFP4 weights a
 
 Rank 0 prints one JSON line.  Under torchrun (N>1) the job is BASELINE config 3: the
 expert-parallel layer with E=128 experts sharded contiguously over the N GPUs (128/N
-each), 8192 tokens per GPU (weak scaling), NVFP4 token rows dispatched to their experts
-and results returned over NCCL all-to-all (flash_mh_moe/ep.py).
+each), 8192 tokens per GPU (weak scaling): NVFP4 token records stored straight into the
+expert ranks' buffers over NVLink and per-record sums stored back by the receivers'
+combine kernel, as a token-chunk pipeline (flash_mh_moe/ep.py; MHMOE_EP_TRANSPORT=nccl
+selects the NCCL all-to-all variant).
+
+--no-extras skips the extra timings the 1-GPU line also reports (the other scatter
+mode and the 8192-token shape), e.g. for a launch-list capture of the headline step.
 
 `--impl reference` times the reference's CPU path for the same layer (router fp32
 einsum, route.py top-k and global sort, and the bf16 FFN of mh_moe_fwd.py restated in
@@ -267,12 +272,12 @@ def run_ours(args, world, rank, local):
         out["config"]["scatter"] = ("combine (deterministic: partial rows + fp32 combine; the default)" if det else
                                     "atomic (MHMOE_SCATTER=atomic: bf16 atomics from the down GEMM, the "
                                     "reference's default scatter)")
-        if not args.tokens and cfg.get("layers", 1) == 1:
+        if not args.tokens and not args.no_extras and cfg.get("layers", 1) == 1:
             ms_other = _time_explicit(args, m, x, cfg["S"], deterministic=not det)
             out["other_scatter"] = {"scatter": "atomic" if det else "combine",
                                     "value": round(cfg["S"] / (ms_other * 1e-3), 1), "unit": "tokens/s",
                                     "ms_per_step": round(ms_other, 4)}
-        if args.config == 1 and not args.tokens:
+        if args.config == 1 and not args.tokens and not args.no_extras:
             S3 = CFG3["S"]
             ms3 = _time_explicit(args, m, x, S3, deterministic=det)
             out["weak_scaling_base"] = {
@@ -536,6 +541,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the other-scatter and 8192-token timings (profiling runs)")
     ap.add_argument("--config", type=int, choices=[1, 2, 4], default=1,
                     help="BASELINE config at N=1 (1: headline; 2: Zipf-skewed routing; 4: 4-layer small batch)")
     ap.add_argument("--release-master", action="store_true",

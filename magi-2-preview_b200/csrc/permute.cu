@@ -11,6 +11,7 @@
 //   4. ordered scatter    one warp per chunk walks its entries in order; lanes that
 //                         share a key get consecutive slots via __match_any_sync, so
 //                         equal keys keep their flat order (stability).
+// Up to 8192 entries the same result comes from one single-CTA kernel (sort_small_kernel).
 #include "kernels.cuh"
 
 namespace mhmoe {
@@ -173,6 +174,81 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
   }
 }
 
+// Small problems (R <= SORT_SMALL_MAX entries, H*E <= 1024): the whole stable sort in one
+// CTA of 1024 threads — keys staged in shared memory, counts by shared atomics, one scan,
+// then one warp per key walks the keys in flat order (ballot + prefix popcount), so equal
+// keys keep their flat order.  Replaces four launches whose latency dominates at small R.
+constexpr int SORT_SMALL_MAX = 8192;
+
+__global__ void __launch_bounds__(1024, 1)
+    sort_small_kernel(const int64_t* __restrict__ idx, const float* __restrict__ probs, int R, int S, int K, int E,
+                      int HE, int64_t* __restrict__ expert_offsets, int32_t* __restrict__ gather_ids,
+                      float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat, int* __restrict__ status) {
+  __shared__ int key[SORT_SMALL_MAX];
+  __shared__ int cnt[1024];
+  __shared__ int off[1024];
+  __shared__ int wsum[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  cnt[tid] = 0;
+  __syncthreads();
+  const int SK = S * K;
+  for (int f = tid; f < R; f += 1024) {
+    const int64_t e = idx[f];
+    int g = -1;
+    if (e >= E) record_error(status, MHMOE_ERR_ARGS);
+    else if (e >= 0) g = (f / SK) * E + (int)e;
+    key[f] = g;
+    if (g >= 0) atomicAdd(&cnt[g], 1);
+    else if (row_of_flat) row_of_flat[f] = -1;
+  }
+  __syncthreads();
+  // exclusive scan of cnt[0..1024): warp scans, then a scan of the warp sums
+  const int v = cnt[tid];
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = wsum[lane];
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    wsum[lane] = wi - w;
+  }
+  __syncthreads();
+  const int excl = wsum[warp] + incl - v;
+  off[tid] = excl;
+  if (tid < HE) expert_offsets[tid] = excl;
+  if (tid == HE - 1) expert_offsets[HE] = excl + v;
+  __syncthreads();
+  // one warp per key, entries in flat order
+  for (int g = warp; g < HE; g += 32) {
+    const int total = cnt[g];
+    if (total == 0) continue;
+    const int base = off[g];
+    int run = 0;
+    for (int f0 = 0; f0 < R && run < total; f0 += 32) {
+      const int f = f0 + lane;
+      const bool hit = f < R && key[f] == g;
+      const unsigned b = __ballot_sync(0xffffffffu, hit);
+      if (hit) {
+        const int pos = base + run + __popc(b & ((1u << lane) - 1u));
+        gather_ids[pos] = (int32_t)((f / K) % S);
+        probs_sorted[pos] = probs[f];
+        if (row_of_flat) row_of_flat[f] = pos;
+      }
+      run += __popc(b);
+    }
+  }
+}
+
 // ───────────── token -> rows map for arbitrary (gather_ids, expert_offsets) ─────────────
 
 // counts[h*S + s] += 1 for every row; one CTA per m-tile of the tile tables.
@@ -296,6 +372,11 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   int* tile_expert = cu_tiles + HE + 1;
   int* tile_row0 = tile_expert + mt;
   int* tile_rows = tile_row0 + mt;
+  if (R <= SORT_SMALL_MAX && HE <= 1024) {
+    sort_small_kernel<<<1, 1024, 0, st>>>(idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids, probs_sorted,
+                                          row_of_flat, status);
+    return cudaGetLastError();
+  }
   const size_t shb = (size_t)HE * sizeof(int);
   sort_hist_kernel<<<nchunks, 256, shb, st>>>(idx, R, S * K, E, HE, chunk, hist, status);
   sort_colscan_kernel<<<(HE + 7) / 8, 256, 0, st>>>(hist, nchunks, HE, total);
