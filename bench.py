@@ -261,6 +261,14 @@ def run_ours(args, world, rank, local):
                   "gemm_gate_up_ms": avg(3, 4), "gemm_down_ms": avg(4, 5), "local_combine_ms": avg(5, 6),
                   "return_combine_ms": avg(6, 7), "a2a_records_ms": avg(8, 9), "a2a_return_ms": avg(10, 11)}
 
+    if world > 1:
+        # one untimed extra step that also counts the remote bytes of chunk 0 (peer transport)
+        import flash_mh_moe.ep as epmod
+        epmod.COLLECT_STATS = True
+        step(m, x, [torch.cuda.Event(enable_timing=True) for _ in range(nev)])
+        torch.cuda.synchronize()
+        epmod.COLLECT_STATS = False
+
     # end-to-end through the public module API, host buffers, copies inside the timed region
     e2e_ms = float("nan")
     if not args.no_e2e:
@@ -381,7 +389,7 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
     }
     if world > 1:
         import torch.distributed as dist
-        from flash_mh_moe.ep import LAST_STATS
+        from flash_mh_moe.ep import LAST_STATS, ep_chunks
         every = [None] * world
         dist.all_gather_object(every, {k: round(v, 4) for k, v in stages.items()})
         out["stages_ms_min_max_over_ranks"] = {k: [min(e[k] for e in every), max(e[k] for e in every)]
@@ -400,9 +408,17 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
                              "note": "rank 0: bytes it sends to other ranks / device time of that all-to-all "
                                      "(NCCL; includes waiting for the slowest peer); peak = measured peer copy"}
         else:
-            out["nvlink"] = {"note": "records are stored to peers by the send kernel and sums by the receiver's "
-                                     "combine (fused); a2a_records_ms = send kernel + wait for every source, "
-                                     "a2a_return_ms = wait for the returns after this rank's own combine"}
+            bd = int(LAST_STATS["records_remote_bytes"].item()) if "records_remote_bytes" in LAST_STATS else 0
+            br = int(LAST_STATS["return_remote_bytes"].item()) if "return_remote_bytes" in LAST_STATS else 0
+            td, tr = stages["a2a_records_ms"], stages["local_combine_ms"]
+            out["nvlink"] = {"records_remote_bytes": bd, "return_remote_bytes": br,
+                             "records_GBps": round(bd / (td * 1e-3) / 1e9, 1) if td > 0 else None,
+                             "return_GBps": round(br / (tr * 1e-3) / 1e9, 1) if tr > 0 else None,
+                             "peak": 770.0, "unit": "GB/s per direction per GPU",
+                             "note": "rank 0, pipeline chunk 0: remote bytes of the record kernel over its time "
+                                     "plus the wait for every source (a2a_records_ms), and remote bytes of the "
+                                     "fused combine-and-return kernel over its time (local_combine_ms, which "
+                                     "also reads the partial rows); peak = measured peer copy"}
     if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == 1:
         out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
     return out

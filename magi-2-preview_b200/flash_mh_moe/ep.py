@@ -156,6 +156,7 @@ class CudaBackend:
 
 
 LAST_STATS: dict = {}   # records / rows moved by the last ep_moe_layer call on this process
+COLLECT_STATS = False   # peer transport: also count chunk 0's remote records (extra small reductions)
 
 
 def _a2a_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group) -> torch.Tensor:
@@ -364,6 +365,11 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     lg, lps, loffs, linv = be.sort(lprobs.view(1, slots, K), lidx.view(1, slots, K), E_loc)
     prev = LAST_STATS.get("rows_received") if slot > 0 else None
     LAST_STATS.update(rows_received=loffs[-1] if prev is None else prev + loffs[-1], transport="peer")
+    if COLLECT_STATS and slot == 0:     # device scalars; read them after the step
+        own = send_offs[px.me + 1] - send_offs[px.me]
+        rb = be.row_bytes(dh, K)
+        LAST_STATS.update(records_remote_bytes=(send_offs[-1] - own) * rb,
+                          return_remote_bytes=((lidx[:, 0] >= 0).sum() - own) * (dh * 2))
     # 3. FFN on the records in place; its combine returns each record's sum to the source
     R = slots * K
     ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, slots, 1, dh, gu.d_expert, E_loc)), dtype=torch.uint8,
