@@ -11,7 +11,8 @@
 //   4. ordered scatter    one warp per chunk walks its entries in order; lanes that
 //                         share a key get consecutive slots via __match_any_sync, so
 //                         equal keys keep their flat order (stability).
-// Up to 8192 entries the same result comes from one single-CTA kernel (sort_small_kernel).
+// Up to 8192 entries and 256 keys the same result comes from one single-CTA kernel
+// (sort_small_kernel).
 #include "kernels.cuh"
 
 namespace mhmoe {
@@ -174,36 +175,55 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
   }
 }
 
-// Small problems (R <= SORT_SMALL_MAX entries, H*E <= 1024): the whole stable sort in one
-// CTA of 1024 threads — keys staged in shared memory, counts by shared atomics, one scan,
-// then one warp per key walks the keys in flat order (ballot + prefix popcount), so equal
-// keys keep their flat order.  Replaces four launches whose latency dominates at small R.
+// Small problems (R <= SORT_SMALL_MAX entries, H*E <= SORT_SMALL_MAX_KEYS): the same
+// stable counting sort in one CTA of 1024 threads — warp w owns a contiguous chunk of the
+// flat entries; per-warp key histograms in shared memory, a column scan over the 32 warps
+// and a key scan give every (warp, key) its first slot; each warp then walks its chunk in
+// order and lanes sharing a key take consecutive slots (__match_any_sync), so equal keys
+// keep their flat order.  Keys and probs are staged in shared memory.  One launch instead
+// of four, whose latency dominates at small R.
 constexpr int SORT_SMALL_MAX = 8192;
+constexpr int SORT_SMALL_MAX_KEYS = 256;
+constexpr int SORT_SMALL_SMEM = (32 * SORT_SMALL_MAX_KEYS + 2 * SORT_SMALL_MAX) * 4;   // 96 KB
 
 __global__ void __launch_bounds__(1024, 1)
     sort_small_kernel(const int64_t* __restrict__ idx, const float* __restrict__ probs, int R, int S, int K, int E,
                       int HE, int64_t* __restrict__ expert_offsets, int32_t* __restrict__ gather_ids,
                       float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat, int* __restrict__ status) {
-  __shared__ int key[SORT_SMALL_MAX];
-  __shared__ int cnt[1024];
-  __shared__ int off[1024];
+  extern __shared__ int sort_small_smem[];
+  int* hist = sort_small_smem;                                   // [32][HE]: count, then first slot
+  int* key = hist + 32 * SORT_SMALL_MAX_KEYS;                   // [R]
+  float* prob = reinterpret_cast<float*>(key + SORT_SMALL_MAX);  // [R]
+  __shared__ int tot[1024];
   __shared__ int wsum[32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  cnt[tid] = 0;
+  for (int i = tid; i < 32 * HE; i += 1024) hist[i] = 0;
   __syncthreads();
   const int SK = S * K;
-  for (int f = tid; f < R; f += 1024) {
+  const int chunk = (R + 31) / 32;
+  const int f0 = warp * chunk, f1 = min(f0 + chunk, R);
+  int* my = hist + warp * HE;
+  for (int f = f0 + lane; f < f1; f += 32) {
     const int64_t e = idx[f];
     int g = -1;
     if (e >= E) record_error(status, MHMOE_ERR_ARGS);
     else if (e >= 0) g = (f / SK) * E + (int)e;
     key[f] = g;
-    if (g >= 0) atomicAdd(&cnt[g], 1);
-    else if (row_of_flat) row_of_flat[f] = -1;
+    prob[f] = probs[f];
+    if (g >= 0) atomicAdd(&my[g], 1);
   }
   __syncthreads();
-  // exclusive scan of cnt[0..1024): warp scans, then a scan of the warp sums
-  const int v = cnt[tid];
+  // column scan over warps: hist[w][g] <- entries of key g in warps before w
+  int total = 0;
+  if (tid < HE) {
+    for (int w = 0; w < 32; ++w) {
+      const int c = hist[w * HE + tid];
+      hist[w * HE + tid] = total;
+      total += c;
+    }
+  }
+  // exclusive scan of the key totals (tid < 1024 covers HE <= 256)
+  const int v = total;
   int incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -224,27 +244,31 @@ __global__ void __launch_bounds__(1024, 1)
   }
   __syncthreads();
   const int excl = wsum[warp] + incl - v;
-  off[tid] = excl;
+  tot[tid] = excl;
   if (tid < HE) expert_offsets[tid] = excl;
   if (tid == HE - 1) expert_offsets[HE] = excl + v;
   __syncthreads();
-  // one warp per key, entries in flat order
-  for (int g = warp; g < HE; g += 32) {
-    const int total = cnt[g];
-    if (total == 0) continue;
-    const int base = off[g];
-    int run = 0;
-    for (int f0 = 0; f0 < R && run < total; f0 += 32) {
-      const int f = f0 + lane;
-      const bool hit = f < R && key[f] == g;
-      const unsigned b = __ballot_sync(0xffffffffu, hit);
-      if (hit) {
-        const int pos = base + run + __popc(b & ((1u << lane) - 1u));
-        gather_ids[pos] = (int32_t)((f / K) % S);
-        probs_sorted[pos] = probs[f];
-        if (row_of_flat) row_of_flat[f] = pos;
-      }
-      run += __popc(b);
+  for (int i = tid; i < 32 * HE; i += 1024) hist[i] += tot[i % HE];
+  __syncthreads();
+  // ordered scatter, each warp over its own chunk
+  for (int fb = f0; fb < f1; fb += 32) {
+    const int f = fb + lane;
+    const int g = f < f1 ? key[f] : -1;
+    const bool valid = g >= 0;
+    const unsigned peers = __match_any_sync(0xffffffffu, valid ? g : -1 - lane);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    int base = 0;
+    if (valid) base = my[g];
+    __syncwarp();
+    if (valid && rank == 0) my[g] = base + __popc(peers);
+    __syncwarp();
+    if (valid) {
+      const int pos = base + rank;
+      gather_ids[pos] = (int32_t)((f / K) % S);
+      probs_sorted[pos] = prob[f];
+      if (row_of_flat) row_of_flat[f] = pos;
+    } else if (f < f1 && row_of_flat) {
+      row_of_flat[f] = -1;
     }
   }
 }
@@ -372,9 +396,12 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   int* tile_expert = cu_tiles + HE + 1;
   int* tile_row0 = tile_expert + mt;
   int* tile_rows = tile_row0 + mt;
-  if (R <= SORT_SMALL_MAX && HE <= 1024) {
-    sort_small_kernel<<<1, 1024, 0, st>>>(idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids, probs_sorted,
-                                          row_of_flat, status);
+  if (R <= SORT_SMALL_MAX && HE <= SORT_SMALL_MAX_KEYS) {
+    static cudaError_t attr = cudaFuncSetAttribute(sort_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   SORT_SMALL_SMEM);
+    if (attr != cudaSuccess) return attr;
+    sort_small_kernel<<<1, 1024, SORT_SMALL_SMEM, st>>>(idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids,
+                                                        probs_sorted, row_of_flat, status);
     return cudaGetLastError();
   }
   const size_t shb = (size_t)HE * sizeof(int);
