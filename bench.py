@@ -446,10 +446,24 @@ def run_stack(args, cfg, dev):
     torch.cuda.synchronize()
     _lib.check_device_status(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # eager (host launches every step)
+    t0.record()
+    for _ in range(args.steps):
+        fwd(x0)
+    t1.record()
+    torch.cuda.synchronize()
+    ms_eager = t0.elapsed_time(t1) / args.steps
+    # the same stack replayed as one CUDA graph (flash_mh_moe.graph): the timed value
+    from flash_mh_moe.graph import CapturedForward
+    g = CapturedForward(fwd, x0, warmup=args.warmup)
+    for _ in range(args.warmup):
+        g(x0)
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
     with ClockSampler(0) as clk:
         t0.record()
         for _ in range(args.steps):
-            fwd(x0)
+            g(x0)
         t1.record()
         torch.cuda.synchronize()
     ms = t0.elapsed_time(t1) / args.steps
@@ -464,7 +478,10 @@ def run_stack(args, cfg, dev):
             "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
             "data": "synthetic (seeded, config-4 distributions)",
             "config": {"workload": f"config4: {cfg['S']} tokens, {cfg['layers']} stacked MoE layers + bf16 residual, "
-                                   "d=3072, E=128, top-8, de=1024", "tokens_per_gpu": cfg["S"]},
+                                   "d=3072, E=128, top-8, de=1024", "tokens_per_gpu": cfg["S"],
+                       "launch": "the 4-layer stack replayed as one CUDA graph (flash_mh_moe.graph.CapturedForward)"},
+            "eager": {"ms_per_step": round(ms_eager, 4), "value": round(cfg["S"] / (ms_eager * 1e-3), 1),
+                      "hbm_gbs": round(total_bytes / (ms_eager * 1e-3) / 1e9, 1)},
             "roofline": {"kernel": "whole 4-layer stack (weight streaming)", "bound": "hbm",
                          "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": None,
