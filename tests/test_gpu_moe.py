@@ -71,3 +71,44 @@ def test_module_fake_meta():
         xf = torch.empty(64, 256, dtype=torch.bfloat16, device="cuda")
         yf = torch.ops.magi2_b200.mh_moe(xf, m._moe_key)
         assert yf.shape == xf.shape and yf.dtype == xf.dtype
+
+
+def test_production_head_split_matches_oracle():
+    """MAGI-2's production routing shape (configs/magi2_preview.json: 12 heads of 256,
+    top-6 sigmoid with expert bias, route_scale 4.9, expert FFN dim 1280) with 16 experts
+    per head instead of 256 so the CPU oracle stays fast.  The oracle runs on the weights
+    the GPU packed (the GPU packer is checked byte-exact against the oracle packer in
+    test_gpu_nvfp4)."""
+    from flash_mh_moe import _lib
+    from flash_mh_moe.moe import CoreMultiHeadMoE, CoreMultiHeadMoEConfig, init_moe_params_
+    from flash_mh_moe.route import route_fused
+    dev = torch.device("cuda", 0)
+    S, H, dh, de, E, K, scale = 128, 12, 256, 1280, 16, 6, 4.9
+    cfg = CoreMultiHeadMoEConfig(hidden_size=H * dh, num_heads=H, num_experts=E, top_k=K,
+                                 expert_intermediate_size=de, num_layers=1, params_dtype=torch.bfloat16,
+                                 score_func="sigmoid", route_norm=True, route_scale=scale)
+    m = CoreMultiHeadMoE(cfg).to(dev)
+    init_moe_params_(m, seed=77, device=dev)
+    with torch.no_grad():
+        m.router.expert_bias.copy_(torch.randn(H * E, generator=torch.Generator().manual_seed(4)) * 0.01)
+    x = torch.randn(S, H * dh, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16).to(dev)
+    y = m(x)
+    torch.cuda.synchronize()
+    _lib.check_device_status(dev)
+    planes, nsplit = m.router_planes()
+    bias = m.router.expert_bias.view(H, E)
+    _, _, logits = route_fused(x.view(S, H, dh), planes, nsplit, E, K, "sigmoid", bias, True, 1e-12, scale,
+                               return_logits=True)
+    p, i = route_ref.compute_topk_probs_and_indices(logits.cpu().numpy(), K, "sigmoid", bias.cpu().numpy())
+    p = (p * np.float32(scale)).astype(np.float32)
+    g, ps, o = route_ref.flash_mh_moe_global_sort(p, i, E)
+    gu, dn = m.packed_weights()
+    gu_pack = {"data": gu.data.cpu().numpy(), "sf_atoms": gu.sf.cpu().numpy(),
+               "gscale_gate": gu.gscale[0].cpu().numpy(), "gscale_up": gu.gscale[1].cpu().numpy(),
+               "N": 2 * de, "K": dh, "de": de}
+    dn_pack = {"data": dn.data.cpu().numpy(), "sf_atoms": dn.sf.cpu().numpy(), "gscale": dn.gscale.cpu().numpy(),
+               "N": dh, "K": de}
+    ref = ffn_ref.mh_moe_fwd_nvfp4_ref(x.float().cpu().numpy().reshape(S, H, dh), g, ps, o, gu_pack, dn_pack)
+    got = y.float().cpu().numpy().reshape(S, H, dh)
+    err = rel_l2(got, ref)
+    assert np.isfinite(got).all() and err < 1e-2, err
