@@ -285,6 +285,25 @@ def run_ours(args, world, rank, local):
             out["other_scatter"] = {"scatter": "atomic" if det else "combine",
                                     "value": round(cfg["S"] / (ms_other * 1e-3), 1), "unit": "tokens/s",
                                     "ms_per_step": round(ms_other, 4)}
+        if not args.tokens and not args.no_extras and cfg.get("layers", 1) == 1 and not cfg.get("zipf"):
+            # the same layer forward replayed as one CUDA graph (no per-kernel host launches)
+            from flash_mh_moe.graph import CapturedForward
+            xs = x.contiguous()
+            g = CapturedForward(m, xs, warmup=args.warmup)
+            for _ in range(args.warmup):
+                g(xs)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(args.steps):
+                g(xs)
+            e1.record()
+            torch.cuda.synchronize()
+            msg = e0.elapsed_time(e1) / args.steps
+            out["graph_replay"] = {"value": round(cfg["S"] / (msg * 1e-3), 1), "unit": "tokens/s",
+                                   "ms_per_step": round(msg, 4),
+                                   "note": "module forward captured once (flash_mh_moe.graph.CapturedForward)"}
+            del g
         if args.config == 1 and not args.tokens and not args.no_extras:
             S3 = CFG3["S"]
             ms3 = _time_explicit(args, m, x, S3, deterministic=det)

@@ -72,12 +72,14 @@ def _rand_operand(rng, rows, K, unit_scale):
     return codes, sf
 
 
-@pytest.mark.parametrize("unit_scale", [True, False])
-def test_gemm_raw_matches_dequantised_product(unit_scale):
+@pytest.mark.parametrize("unit_scale,N,K,n_mt", [(True, 512, 512, 3), (False, 512, 512, 3),
+                                                  (False, 1536, 512, 3),    # 6 n-tiles: a full and a partial unit
+                                                  (False, 512, 4096, 2)])   # K > 3072: A scales per stage
+def test_gemm_raw_matches_dequantised_product(unit_scale, N, K, n_mt):
     L = _lib()
     rng = np.random.default_rng(1 if unit_scale else 2)
-    n_mt, n_exp, N, K = 3, 2, 512, 512
-    tile_expert = np.array([0, 1, 1], np.int32)
+    n_exp = 2
+    tile_expert = np.array([0, 1, 1][:n_mt], np.int32)
     a_codes, a_sf = _rand_operand(rng, n_mt * 128, K, unit_scale)
     b = [_rand_operand(rng, N, K, unit_scale) for _ in range(n_exp)]
     a_data = torch.from_numpy(nv.pack_codes(a_codes)).cuda()
