@@ -88,14 +88,14 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
     // the kernel's cluster shape (2, 1, 1) is compiled in, so the query config names none
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
-    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.blockDim = dim3(GEMMP_THREADS);
     cfg.dynamicSmemBytes = gemmp_smem_bytes(EPI);
     attr_err = cudaOccupancyMaxActiveClusters(&max_clusters, ffn_gemm_pair_kernel<EPI>, &cfg);
     if (attr_err == cudaSuccess && max_clusters <= 0) attr_err = cudaErrorInvalidConfiguration;
   });
   if (attr_err != cudaSuccess) return attr_err;
   const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(max_clusters, max_work));
-  ffn_gemm_pair_kernel<EPI><<<2 * clusters, GEMM_THREADS, gemmp_smem_bytes(EPI), st>>>(ta, tb, tc, tsfa, tsfb, p);
+  ffn_gemm_pair_kernel<EPI><<<2 * clusters, GEMMP_THREADS, gemmp_smem_bytes(EPI), st>>>(ta, tb, tc, tsfa, tsfb, p);
   return cudaGetLastError();
 }
 

@@ -6,16 +6,24 @@
 //
 //   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
 //
-// Warp roles (320 threads):
+// Warp roles (352 threads):
 //   warp 0      TMA producer into a 4-stage (EPI_DOWN: 3-stage) shared-memory ring, one
 //               stage = 256 K-elements: A tile (128 x 256 FP4 = 16 KB) and B tile
 //               (256 x 256 FP4 = 32 KB), 128-B swizzle, plus their UE4M3 scale atoms
 //               (2 KB + 4 KB, untiled bulk copies).  The whole warp waits; lane 0 issues.
-//   warp 1      TMEM owner + MMA issuer: per stage copies the scale atoms into TMEM
-//               (tcgen05.cp 32x128b.warpx4) and issues 4 x tcgen05.mma
-//               kind::mxf4nvf4 block16 (M128 N256 K64).
+//   warp 1      TMEM owner + MMA issuer: per stage, once the stage's scale factors are in
+//               TMEM, issues 4 x tcgen05.mma kind::mxf4nvf4 block16 (M128 N256 K64).
 //   warps 2-9   epilogue: drain the accumulator with tcgen05.ld into registers,
 //               release TMEM, then apply the fused epilogue and store.
+//   warp 10     scale-factor copier: per stage copies the 12 scale atoms into TMEM
+//               (tcgen05.cp 32x128b.warpx4) and commits to the stage's sf-full barrier.
+//               The copies cost the tcgen05 pipe more than the MMAs do; issued from their
+//               own warp they run ahead of and beside the MMAs instead of between them.
+//
+// Ordering: the copier overwrites TMEM scale slot s only after full[s] of the next round,
+// which the producer posts only after empty[s], which the MMA warp commits after the MMAs
+// that read slot s; the MMA warp's empty[s] commit follows its wait on sf-full[s], so the
+// copies' shared-memory reads are done before the stage is refilled.
 //
 // TMEM columns: [0,256) accumulator, [256 + 48*s, 256 + 48*(s+1)) the scale
 // factors of stage s (16 columns SFA = 4 MMAs x 4, 32 columns SFB = 4 MMAs x 8).
@@ -42,7 +50,8 @@ enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2, EPI_DOWN_ATOMIC = 3 };
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
 constexpr int GEMM_BK = 256;          // FP4 elements per stage = 128 bytes per row
-constexpr int GEMM_THREADS = 320;
+constexpr int GEMM_THREADS = 352;          // single-CTA kernel: warps 0-9 + the scale-factor copier
+constexpr int GEMMP_THREADS = 320;         // CTA-pair kernel
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK / 2;          // 16384
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK / 2;          // 32768
 constexpr int GEMM_SFA_BYTES = GEMM_BM * GEMM_BK / 16;       // 2048
@@ -230,7 +239,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;         // accumulator ready
   uint64_t* tempty_bar = tfull_bar + 1;            // accumulator drained
   uint64_t* drain_bar = tfull_bar + 2;             // all issued tcgen05 ops retired
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* sff_bar = tfull_bar + 3;               // [STAGES] scale factors of the stage in TMEM
+  uint64_t* drain2_bar = sff_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain2_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -243,6 +254,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     mbar_init(smem_u32(tfull_bar), 1);
     mbar_init(smem_u32(tempty_bar), 8);
     mbar_init(smem_u32(drain_bar), 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&sff_bar[s]), 1);
+    mbar_init(smem_u32(drain2_bar), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -314,18 +327,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       for (int kb = 0; kb < n_kblk; ++kb) {
         if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        if (!mbar_wait(smem_u32(&sff_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
           const uint32_t tsfb = tsfa + 16;
-          const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
-          const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tc_cp_32x128b_warpx4(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
-            tc_cp_32x128b_warpx4(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
-            tc_cp_32x128b_warpx4(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
-          }
           const uint32_t a_s = smem_u32(sA + stage * GEMM_A_BYTES);
           const uint32_t b_s = smem_u32(sB + stage * GEMM_B_BYTES);
 #pragma unroll
@@ -341,6 +347,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (lane == 0) tc_commit(smem_u32(tfull_bar));
       __syncwarp();
       acc_phase ^= 1;
+    }
+  } else if (warp == 10) {
+    // ───────── scale-factor copier (whole warp waits; lane 0 issues) ─────────
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      for (int kb = 0; kb < n_kblk; ++kb) {
+        if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
+          const uint32_t tsfb = tsfa + 16;
+          const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
+          const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            tc_cp_32x128b_warpx4(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
+            tc_cp_32x128b_warpx4(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
+            tc_cp_32x128b_warpx4(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
+          }
+          tc_commit(smem_u32(&sff_bar[stage]));
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
     }
   } else {
     // ───────── epilogue warps 2..9 ─────────
@@ -377,6 +408,10 @@ done:
     tc_commit(smem_u32(drain_bar));
     mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
+  if (warp == 10 && lane == 0) {
+    tc_commit(smem_u32(drain2_bar));
+    mbar_wait(smem_u32(drain2_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -398,7 +433,7 @@ done:
 //     barrier (16 arrivals per tile).
 // tmSFA / tmSFB: the SF atom arrays viewed as [bytes/256, 256] u8, box 256 x 8 (2 KB).
 template <int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
     ffn_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmSFA,
                          const __grid_constant__ CUtensorMap tmSFB, const FfnGemmParams p) {
