@@ -212,11 +212,31 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   mark(0);
   MHMOE_TRY(launch_tile_tables(expert_offsets, HE, max_mt, w.cu_tiles, w.tile_expert, w.tile_row0, w.tile_rows,
                                status, st, pair ? 2 : 1));
-  MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
-  if (!prequant) MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
-  MHMOE_TRY(launch_group_rows(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H, HE / H, gather_ids, w.cu_tiles,
-                              HE, max_mt, w.tile_expert, w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale,
-                              status, st));
+  // key (h, s) -> its sorted rows: the caller's inverse map, else built from the tile tables
+  const int32_t* rows_map = tok_rows;
+  const int32_t* offs_map = tok_offsets;
+  int kf = k_fixed;
+  if (!tok_rows) {
+    MHMOE_TRY(launch_token_rows(gather_ids, max_mt, w.cu_tiles, HE, HE / H, S, H, w.tile_expert, w.tile_row0,
+                                w.tile_rows, w.tok_ws, w.tok_offsets, w.tok_rows, status, st));
+    rows_map = w.tok_rows;
+    offs_map = w.tok_offsets;
+    kf = 0;
+  }
+  // Local tokens are quantised once and written straight into their grouped rows; tokens
+  // that arrive pre-quantised (expert-parallel receive) are grouped by copy.
+  const bool fused = !prequant && dh <= quant_scatter_max_dh();
+  MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st, dh,
+                            fused ? w.a_data : nullptr, w.a_sf, w.a_gscale));
+  if (fused) {
+    MHMOE_TRY(launch_quant_scatter(x, sx_s, sx_h, S, H, dh, rows_map, offs_map, kf, R, w.pad_of_row, rows, w.a_data,
+                                   w.a_sf, w.a_gscale, status, st));
+  } else {
+    if (!prequant) MHMOE_TRY(launch_quant_tokens(x, sx_s, sx_h, S, H, dh, w.xq, w.xsf, w.xg, st));
+    MHMOE_TRY(launch_group_rows(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H, HE / H, gather_ids, w.cu_tiles,
+                                HE, max_mt, w.tile_expert, w.tile_row0, w.tile_rows, w.a_data, w.a_sf, w.a_gscale,
+                                status, st));
+  }
 
   CUtensorMap ta1, tb1, ta2, tb2, tc2;
   if (encode_tmap_2d_u8(&ta1, w.a_data, dh / 2, rows, 128, 128) != cudaSuccess ||
@@ -289,16 +309,6 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
     MHMOE_TRY(launch_gemm<EPI_DOWN>(ta2, tb2, tc2, p2, max_mt * (dh / GEMM_BN), st));
 
   mark(3);
-  const int32_t* rows_map = tok_rows;
-  const int32_t* offs_map = tok_offsets;
-  int kf = k_fixed;
-  if (!tok_rows) {
-    MHMOE_TRY(launch_token_rows(gather_ids, max_mt, w.cu_tiles, HE, HE / H, S, H, w.tile_expert, w.tile_row0,
-                                w.tile_rows, w.tok_ws, w.tok_offsets, w.tok_rows, status, st));
-    rows_map = w.tok_rows;
-    offs_map = w.tok_offsets;
-    kf = 0;
-  }
   if (ret)
     MHMOE_TRY(launch_combine_return(w.P, w.pad_of_row, dh, rows_map, kf, R, rows, *ret, st));
   else

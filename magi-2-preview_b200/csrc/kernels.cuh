@@ -91,6 +91,13 @@ cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t
                               const int32_t* gather_ids, const int* cu_tiles, int HE, int64_t max_mtiles,
                               const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
                               uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st);
+// Fused quantise + group of x into the padded A operand through the inverse map (tok_rows
+// with tok_offsets or k_fixed); dh <= quant_scatter_max_dh(), dh % 64 == 0.
+int quant_scatter_max_dh();
+cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
+                                 const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
+                                 const int32_t* pad_of_row, int64_t rows, uint8_t* a_data, uint8_t* a_sf,
+                                 float* a_gscale, int* status, cudaStream_t st);
 cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
                                 uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st);
 cudaError_t launch_quantize_rows(const __nv_bfloat16* x, int64_t pitch, int64_t M, int K, uint8_t* data, uint8_t* sf,
@@ -106,8 +113,10 @@ cudaError_t launch_topk(const float* logits, const float* bias, int H, int S, in
                         cudaStream_t st);
 
 // combine.cu
+// sorted row -> padded row; with a_data, also zero-fills the A operand's padding rows
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
-                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st);
+                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st, int dh = 0,
+                            uint8_t* a_data = nullptr, uint8_t* a_sf = nullptr, float* a_gscale = nullptr);
 cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh, int S, int H,
                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
                            int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st);

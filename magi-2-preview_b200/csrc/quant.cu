@@ -109,6 +109,99 @@ __global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   warp_quant_row(x + s * sx_s + h * sx_h, dh, (uint64_t)t, xq, xsf, xg, lane, true);
 }
 
+// Fused quantise + group (local path, inverse map known): one warp per key (h, s)
+// quantises x[s, h, :] once and writes the NVFP4 row (data, scale atoms, row scale) to
+// each of the key's padded rows of the grouped A operand, so the per-token intermediate
+// never exists.  Lane l owns the 16-element blocks b = l + 32 i: every data store of a
+// destination row is 256 contiguous bytes per warp, and the four scales of a 64-element
+// chunk (lanes 4c'..4c'+3) are packed into one word with two shuffles.  The op sequence per
+// block is quant_block16 with g = amax / 2688, as in warp_quant_row.
+template <int MAXNB>
+__global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
+                                     int dh, const int32_t* __restrict__ tok_rows,
+                                     const int32_t* __restrict__ tok_offsets, int k_fixed, int64_t R,
+                                     const int32_t* __restrict__ pad_of_row, int64_t rows, uint8_t* __restrict__ a_data,
+                                     uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
+                                     int* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t key = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // key = h * S + s
+  if (key >= (int64_t)H * S) return;
+  const int64_t h = key / S, s = key % S;
+  const __nv_bfloat16* src = x + s * sx_s + h * sx_h;
+  const int nblk = dh / 16;
+  uint4 raw[MAXNB][2];
+#pragma unroll
+  for (int i = 0; i < MAXNB; ++i) {
+    const int b = lane + 32 * i;
+    if (b < nblk) {
+      raw[i][0] = *reinterpret_cast<const uint4*>(src + 16 * b);
+      raw[i][1] = *reinterpret_cast<const uint4*>(src + 16 * b + 8);
+    } else {
+      raw[i][0] = raw[i][1] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXNB; ++i) {
+    float f[16];
+    load8_bf16(reinterpret_cast<const __nv_bfloat16*>(&raw[i][0]), f);
+    load8_bf16(reinterpret_cast<const __nv_bfloat16*>(&raw[i][1]), f + 8);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float g = amax > 0.f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  uint32_t codes[MAXNB][2], sfw[MAXNB];
+#pragma unroll
+  for (int i = 0; i < MAXNB; ++i) {
+    float f[16];
+    load8_bf16(reinterpret_cast<const __nv_bfloat16*>(&raw[i][0]), f);
+    load8_bf16(reinterpret_cast<const __nv_bfloat16*>(&raw[i][1]), f + 8);
+    uint32_t sf = quant_block16(f, g, codes[i]);
+    // lane 4c' collects the scales of lanes 4c'..4c'+3 (bytes 0..3 of the chunk's word)
+    sf |= __shfl_down_sync(0xffffffffu, sf, 1) << 8;
+    sf |= __shfl_down_sync(0xffffffffu, sf, 2) << 16;
+    sfw[i] = sf;
+  }
+  int64_t begin;
+  int cnt;
+  if (tok_offsets) {
+    begin = tok_offsets[key];
+    cnt = tok_offsets[key + 1] - (int)begin;
+  } else {
+    begin = key * k_fixed;
+    cnt = k_fixed;
+  }
+  for (int j0 = 0; j0 < cnt; j0 += 32) {
+    int64_t mine = -1;
+    if (j0 + lane < cnt) {
+      const int r = tok_rows[begin + j0 + lane];
+      if (r >= 0 && r < R) {
+        const int32_t pr = pad_of_row[r];
+        if (pr >= 0 && pr < rows) mine = pr;
+      }
+      if (mine < 0) record_error(status, MHMOE_ERR_ARGS);
+    }
+    const int n = min(32, cnt - j0);
+    for (int j = 0; j < n; ++j) {
+      const int64_t prow = __shfl_sync(0xffffffffu, mine, j);
+      if (prow < 0) continue;
+      uint8_t* drow = a_data + prow * (int64_t)(dh / 2);
+#pragma unroll
+      for (int i = 0; i < MAXNB; ++i) {
+        const int b = lane + 32 * i;
+        if (b < nblk) {
+          *reinterpret_cast<uint2*>(drow + 8 * b) = make_uint2(codes[i][0], codes[i][1]);
+          if ((lane & 3) == 0)
+            *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)b, (uint32_t)dh)) = sfw[i];
+        }
+      }
+      if (lane == 0) a_gscale[prow] = g;
+    }
+  }
+}
+
 __global__ void quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t pitch, int64_t M, int K,
                                      uint8_t* __restrict__ data, uint8_t* __restrict__ sf,
                                      float* __restrict__ gscale) {
@@ -195,6 +288,29 @@ cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx
                                 uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st) {
   const int64_t T = (int64_t)S * H;
   quant_tokens_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, xq, xsf, xg);
+  return cudaGetLastError();
+}
+
+int quant_scatter_max_dh() { return 16 * 512; }
+
+cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
+                                 const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
+                                 const int32_t* pad_of_row, int64_t rows, uint8_t* a_data, uint8_t* a_sf,
+                                 float* a_gscale, int* status, cudaStream_t st) {
+  const int64_t keys = (int64_t)S * H;
+  const unsigned grid = (unsigned)((keys + 7) / 8);
+  const int nb = (dh / 16 + 31) / 32;
+#define MHMOE_QS(NB) \
+  quant_scatter_kernel<NB><<<grid, 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, k_fixed, R, \
+                                                 pad_of_row, rows, a_data, a_sf, a_gscale, status)
+  if (nb <= 2) MHMOE_QS(2);
+  else if (nb <= 4) MHMOE_QS(4);
+  else if (nb <= 6) MHMOE_QS(6);
+  else if (nb <= 8) MHMOE_QS(8);
+  else if (nb <= 12) MHMOE_QS(12);
+  else if (nb <= 16) MHMOE_QS(16);
+  else return cudaErrorInvalidValue;
+#undef MHMOE_QS
   return cudaGetLastError();
 }
 
