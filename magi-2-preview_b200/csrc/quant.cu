@@ -117,7 +117,8 @@ __global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t
 // chunk (lanes 4c'..4c'+3) are packed into one word with two shuffles.  The op sequence per
 // block is quant_block16 with g = amax / 2688, as in warp_quant_row.
 template <int MAXNB>
-__global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
+__global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
+    quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
                                      int dh, const int32_t* __restrict__ tok_rows,
                                      const int32_t* __restrict__ tok_offsets, int k_fixed, int64_t R,
                                      const int32_t* __restrict__ pad_of_row, int64_t rows, uint8_t* __restrict__ a_data,
@@ -129,6 +130,18 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
   const int64_t h = key / S, s = key % S;
   const __nv_bfloat16* src = x + s * sx_s + h * sx_h;
   const int nblk = dh / 16;
+  // destinations first (two dependent lookups), so their latency hides under the x loads
+  int64_t begin;
+  int cnt;
+  if (tok_offsets) {
+    begin = tok_offsets[key];
+    cnt = tok_offsets[key + 1] - (int)begin;
+  } else {
+    begin = key * k_fixed;
+    cnt = k_fixed;
+  }
+  int r0 = -1;
+  if (lane < cnt) r0 = tok_rows[begin + lane];
   uint4 raw[MAXNB][2];
 #pragma unroll
   for (int i = 0; i < MAXNB; ++i) {
@@ -149,6 +162,8 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
 #pragma unroll
     for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
   }
+  int32_t p0 = -1;
+  if (r0 >= 0 && r0 < R) p0 = pad_of_row[r0];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   const float g = amax > 0.f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
@@ -164,23 +179,15 @@ __global__ void quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_
     sf |= __shfl_down_sync(0xffffffffu, sf, 2) << 16;
     sfw[i] = sf;
   }
-  int64_t begin;
-  int cnt;
-  if (tok_offsets) {
-    begin = tok_offsets[key];
-    cnt = tok_offsets[key + 1] - (int)begin;
-  } else {
-    begin = key * k_fixed;
-    cnt = k_fixed;
-  }
   for (int j0 = 0; j0 < cnt; j0 += 32) {
     int64_t mine = -1;
     if (j0 + lane < cnt) {
-      const int r = tok_rows[begin + j0 + lane];
-      if (r >= 0 && r < R) {
-        const int32_t pr = pad_of_row[r];
-        if (pr >= 0 && pr < rows) mine = pr;
+      int32_t pr = p0;
+      if (j0 > 0) {
+        const int r = tok_rows[begin + j0 + lane];
+        pr = r >= 0 && r < R ? pad_of_row[r] : -1;
       }
+      if (pr >= 0 && pr < rows) mine = pr;
       if (mine < 0) record_error(status, MHMOE_ERR_ARGS);
     }
     const int n = min(32, cnt - j0);

@@ -21,6 +21,7 @@ the 16-B vector atomics saturate L2.
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -34,33 +35,32 @@ def _is_deterministic() -> bool:
     return os.environ.get("MHMOE_SCATTER", "combine") != "atomic"
 
 
-_pack_cache: dict[tuple, tuple] = {}
+# Packed operands keyed by their source tensors' (address, version, shape, dtype, device).
+# An entry lives only as long as every source tensor object it was packed from: a weakref
+# callback evicts it when one dies, so a new tensor later allocated at the same address
+# (same version 0, same shape) can never pick up another tensor's packed weights.
+_pack_cache: dict[tuple, object] = {}
 
 
 def _key(t: torch.Tensor) -> tuple:
     return (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device)
 
 
+def _cached_pack(tag: str, srcs: tuple, pack):
+    k = (tag,) + tuple(x for t in srcs for x in _key(t))
+    hit = _pack_cache.get(k)
+    if hit is None:
+        hit = pack(*srcs)
+        _pack_cache[k] = hit
+        for t in srcs:
+            weakref.finalize(t, _pack_cache.pop, k, None)
+    return hit
+
+
 def packed_weights(W_gate, W_up, W_down) -> tuple[NVFP4GateUp, NVFP4Down]:
     """Return NVFP4 operands for the given weights, packing (and caching) bf16 ones."""
-    if isinstance(W_gate, NVFP4GateUp):
-        gu = W_gate
-    else:
-        k = ("gu",) + _key(W_gate) + _key(W_up)
-        hit = _pack_cache.get(k)
-        if hit is None:
-            hit = (pack_gate_up(W_gate, W_up),)
-            _pack_cache[k] = hit
-        gu = hit[0]
-    if isinstance(W_down, NVFP4Down):
-        dn = W_down
-    else:
-        k = ("dn",) + _key(W_down)
-        hit = _pack_cache.get(k)
-        if hit is None:
-            hit = (pack_down(W_down),)
-            _pack_cache[k] = hit
-        dn = hit[0]
+    gu = W_gate if isinstance(W_gate, NVFP4GateUp) else _cached_pack("gu", (W_gate, W_up), pack_gate_up)
+    dn = W_down if isinstance(W_down, NVFP4Down) else _cached_pack("dn", (W_down,), pack_down)
     return gu, dn
 
 

@@ -29,6 +29,13 @@ from .route import (compute_topk_probs_and_indices, flash_mh_moe_global_sort_wit
                     fused_router_supported, route_fused, router_logits, router_prepare)
 
 
+def _same_key(a, b) -> bool:
+    """Keys are tuples of (parameter object, address, version): same objects (identity, not
+    tensor equality), same addresses and versions."""
+    return a is not None and len(a) == len(b) and all(
+        x[0] is y[0] and x[1:] == y[1:] for x, y in zip(a, b))
+
+
 @dataclass
 class CoreMultiHeadMoEConfig:
     hidden_size: int
@@ -86,13 +93,15 @@ class CoreMultiHeadMoE(nn.Module):
 
     # ── NVFP4 weights (quantise on load) ──
     def _weights_key(self):
-        return tuple((p.data_ptr(), p._version) for p in (self.W_gate, self.W_up, self.W_down))
+        # the parameter objects themselves are part of the key (held by the key, so a
+        # replaced parameter cannot be freed and its address reused while the key exists)
+        return tuple((p, p.data_ptr(), p._version) for p in (self.W_gate, self.W_up, self.W_down))
 
     def packed_weights(self) -> tuple[NVFP4GateUp, NVFP4Down]:
         if self._masters_released:
             return self._packed
         key = self._weights_key()
-        if self._packed is None or self._packed_key != key:
+        if self._packed is None or not _same_key(self._packed_key, key):
             with torch.no_grad():
                 self._packed = (pack_gate_up(self.W_gate, self.W_up), pack_down(self.W_down))
             self._packed_key = key
@@ -118,8 +127,8 @@ class CoreMultiHeadMoE(nn.Module):
         self._masters_released = False       # new masters: pack again at first use
 
     def router_planes(self) -> tuple[torch.Tensor, int]:
-        key = (self.gate.data_ptr(), self.gate._version)
-        if self._router_planes is None or self._router_key != key:
+        key = ((self.gate, self.gate.data_ptr(), self.gate._version),)
+        if self._router_planes is None or not _same_key(self._router_key, key):
             self._router_planes = router_prepare(self.gate)
             self._router_key = key
         return self._router_planes
