@@ -15,8 +15,15 @@
 // K' = nsplit * dh, iterated as (dh block of 64, plane) so each x tile is re-read from L2
 // right after its first load.  Warp 0: TMA producer (x tile 128x64 bf16, gate tile
 // Nx64 bf16, 128-B swizzle, 4 stages); warp 1: TMEM owner + MMA issuer
-// (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-5: epilogue, one token row per thread,
-// top-k kept in registers by branch-free insertion (8 entries for K <= 8, else 16).
+// (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-17: epilogue.  Epilogue warp w reads
+// TMEM lane quarter q = w % 4 (rows 32q..32q+31, one per lane) and column group
+// g = (w - 2) / 4, a contiguous quarter of the 32-column chunks, so each row's scoring is
+// spread over four warps: partial row max and softmax sums are combined through shared
+// memory in group order, each warp keeps a top-k list of its columns in registers
+// (branch-free insertion; 8 entries for K <= 8, else 16), and the four lists of a row are
+// merged in two rounds (group 1 into 0 and 3 into 2, then 2 into 0) — lower groups hold
+// lower experts, so the merge keeps the order (score desc, expert asc) of one sequential
+// pass.
 #include <mutex>
 
 #include "kernels.cuh"
@@ -26,8 +33,13 @@ namespace mhmoe {
 constexpr int RT_BM = 128;
 constexpr int RT_BK = 64;                // bf16 elements per stage row (128 B)
 constexpr int RT_MAX_STAGES = 4;
-constexpr int RT_SCRATCH_BYTES = 2 * 32 * 128 * 4;
-constexpr int RT_THREADS = 192;
+constexpr int RT_EPI_WARPS = 16;
+constexpr int RT_THREADS = 64 + 32 * RT_EPI_WARPS;
+// shared scratch after the barriers: row max and softmax partials [4 groups][128 rows] fp32,
+// then the merge buffer [4 quarters][2 slots][KM][32 lanes] x (value, expert, score)
+constexpr int RT_RED_BYTES = 2 * 4 * 128 * 4;
+__host__ __device__ constexpr int rt_merge_bytes(int km) { return 4 * 2 * km * 32 * 12; }
+
 
 struct RouterParams {
   const float* logit_bias; // [H*E] or null: added to the logits before scoring
@@ -79,8 +91,13 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
   uint64_t* tfull_bar = bars + 2 * RT_MAX_STAGES;
   uint64_t* tempty_bar = tfull_bar + 1;
   uint64_t* drain_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  float* scratch = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // 2 x [32][128] fp32
+  uint64_t* qbar = drain_bar + 1;                  // [4] the four epilogue warps of a lane quarter
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qbar + 4);
+  float* red_max = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // [4][128]
+  float* red_sum = red_max + 4 * 128;                                                  // [4][128]
+  float* mg_v = red_sum + 4 * 128;                                                     // [4][2][KM][32]
+  int* mg_e = reinterpret_cast<int*>(mg_v + 4 * 2 * KM * 32);
+  float* mg_s = reinterpret_cast<float*>(mg_e + 4 * 2 * KM * 32);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t tcols = p.Npad <= 32 ? 32 : p.Npad <= 64 ? 64 : p.Npad <= 128 ? 128 : 256;
@@ -90,8 +107,9 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     mbar_init(smem_u32(tfull_bar), 1);
-    mbar_init(smem_u32(tempty_bar), 4);
+    mbar_init(smem_u32(tempty_bar), RT_EPI_WARPS);
     mbar_init(smem_u32(drain_bar), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&qbar[i]), 128);
     fence_mbar_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmG);
@@ -167,13 +185,21 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       acc_phase ^= 1;
     }
   } else {
-    // epilogue: one token row per thread (TMEM lane = row)
+    // epilogue: lane quarter q, column group g; one token row per lane
     const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
     const int m = q * 32 + lane;
     const int nchunk = p.Npad / 32 + (p.Npad % 32 ? 1 : 0);
-    float* sv = scratch + (threadIdx.x - 64);          // [32][128] selection values of this thread
-    float* ss = sv + 32 * 128;                          // [32][128] unbiased scores
-    uint32_t acc_phase = 0;
+    const int cpg = (nchunk + 3) / 4;                    // chunks per group (contiguous)
+    const int c0 = min(nchunk, g * cpg), c1 = min(nchunk, c0 + cpg);
+    uint32_t acc_phase = 0, q_phase = 0;
+    // every thread of the quarter's four warps arrives, then waits (bounded) for the rest
+    auto quarter_sync = [&]() -> bool {
+      mbar_arrive(smem_u32(&qbar[q]));
+      const bool ok = mbar_wait(smem_u32(&qbar[q]), q_phase, p.status, MHMOE_ERR_TIMEOUT, timeout);
+      q_phase ^= 1;
+      return ok;
+    };
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int h = t / mtiles, mt = t % mtiles;
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
@@ -185,9 +211,9 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
       const float* lb = p.logit_bias ? p.logit_bias + (int64_t)h * p.E : nullptr;
       uint32_t r[32];
-      // pass 1: max (softmax) and optional logits output
+      // pass 1: row max over this group's columns (and the optional logits output)
       float mx = -INFINITY;
-      for (int c = 0; c < nchunk; ++c) {
+      for (int c = c0; c < c1; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
@@ -200,21 +226,30 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           }
         }
       }
-      // pass 2: softmax denominator (ascending expert order)
+      red_max[g * 128 + m] = mx;
+      if (!quarter_sync()) break;
+      mx = fmaxf(fmaxf(red_max[m], red_max[128 + m]), fmaxf(red_max[256 + m], red_max[384 + m]));
+      // pass 2: softmax denominator, ascending experts within the group, groups in order
       float sum = 0.f;
       if (p.score_func == 0) {
-        for (int c = 0; c < nchunk; ++c) {
+        float part = 0.f;
+        for (int c = c0; c < c1; ++c) {
           MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int e = c * 32 + i;
-            if (e < p.E) sum += expf((lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i])) - mx);
+            if (e < p.E) part += expf((lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i])) - mx);
           }
         }
+        red_sum[g * 128 + m] = part;
+        if (!quarter_sync()) break;
+        sum = red_sum[m];
+        sum += red_sum[128 + m];
+        sum += red_sum[256 + m];
+        sum += red_sum[384 + m];
       }
-      // pass 3: scores of a 32-column chunk go to this thread's column of the shared
-      // scratch, then a compact loop inserts them into the top-KM list (branch-free).
+      // pass 3: scores and selection values, inserted into this group's top-KM list
       float tv[KM], ts[KM];
       int ti[KM];
 #pragma unroll
@@ -223,7 +258,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         ts[j] = 0.f;
         ti[j] = 0;
       }
-      for (int c = 0; c < nchunk; ++c) {
+      for (int c = c0; c < c1; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
@@ -235,30 +270,53 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
             sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
             v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
           }
-          sv[i * 128] = v;
-          ss[i * 128] = sc;
+          topk_insert<KM>(v, e, sc, tv, ti, ts);
         }
-#pragma unroll 2
-        for (int i = 0; i < 32; ++i) topk_insert<KM>(sv[i * 128], c * 32 + i, ss[i * 128], tv, ti, ts);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
-      if (valid) {
-        float nrm = 1.f;
-        if (p.route_norm) {
-          float a = 0.f;
-#pragma unroll
-          for (int j = 0; j < KM; ++j)
-            if (j < p.K) a += fabsf(ts[j]);
-          nrm = fmaxf(a, p.norm_eps);
-        }
+      // merge: round 1 (1 -> 0, 3 -> 2), round 2 (2 -> 0); slot index [q][slot][j][lane]
+      auto put = [&](int slot) {
 #pragma unroll
         for (int j = 0; j < KM; ++j) {
-          if (j < p.K) {
-            const float pr = p.route_norm ? __fdiv_rn(ts[j], nrm) : ts[j];
-            p.probs[row * p.K + j] = __fmul_rn(pr, p.route_scale);
-            p.idx[row * p.K + j] = ti[j];
+          const int o = ((q * 2 + slot) * KM + j) * 32 + lane;
+          mg_v[o] = tv[j];
+          mg_e[o] = ti[j];
+          mg_s[o] = ts[j];
+        }
+      };
+      auto take = [&](int slot) {
+#pragma unroll
+        for (int j = 0; j < KM; ++j) {
+          const int o = ((q * 2 + slot) * KM + j) * 32 + lane;
+          topk_insert<KM>(mg_v[o], mg_e[o], mg_s[o], tv, ti, ts);
+        }
+      };
+      if (g & 1) put(g >> 1);
+      if (!quarter_sync()) break;
+      if (!(g & 1)) take(g >> 1);
+      if (!quarter_sync()) break;
+      if (g == 2) put(0);
+      if (!quarter_sync()) break;
+      if (g == 0) {
+        take(0);
+        if (valid) {
+          float nrm = 1.f;
+          if (p.route_norm) {
+            float a = 0.f;
+#pragma unroll
+            for (int j = 0; j < KM; ++j)
+              if (j < p.K) a += fabsf(ts[j]);
+            nrm = fmaxf(a, p.norm_eps);
+          }
+#pragma unroll
+          for (int j = 0; j < KM; ++j) {
+            if (j < p.K) {
+              const float pr = p.route_norm ? __fdiv_rn(ts[j], nrm) : ts[j];
+              p.probs[row * p.K + j] = __fmul_rn(pr, p.route_scale);
+              p.idx[row * p.K + j] = ti[j];
+            }
           }
         }
       }
@@ -345,7 +403,7 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   p.route_scale = route_scale;
   p.status = status;
   const int stage_bytes = RT_BM * RT_BK * 2 + Npad * RT_BK * 2;
-  const int fixed = 256 + RT_SCRATCH_BYTES + 1024;
+  const int fixed = 256 + RT_RED_BYTES + rt_merge_bytes(K <= 8 ? 8 : 16) + 1024;
   p.stages = std::min(RT_MAX_STAGES, (227 * 1024 - fixed) / stage_bytes);
   const int smem = p.stages * stage_bytes + fixed;
   // top-K lists of 8 entries cover K <= 8; 16 entries otherwise (K <= 16)
