@@ -14,7 +14,7 @@
 // GEMM shape per tile: M = 128 tokens (one head), N = E rounded up to 16 (<= 256),
 // K' = nsplit * dh, iterated as (dh block of 64, plane) so each x tile is re-read from L2
 // right after its first load.  Warp 0: TMA producer (x tile 128x64 bf16, gate tile
-// Nx64 bf16, 128-B swizzle, 4 stages); warp 1: TMEM owner + MMA issuer
+// Nx64 bf16, 128-B swizzle, up to 8 stages); warp 1: TMEM owner + MMA issuer
 // (tcgen05.mma kind::f16, M128 N<=256 K16); warps 2-17: epilogue.  Epilogue warp w reads
 // TMEM lane quarter q = w % 4 (rows 32q..32q+31, one per lane) and column group
 // g = (w - 2) / 4, a contiguous quarter of the 32-column chunks, so each row's scoring is
@@ -32,7 +32,7 @@ namespace mhmoe {
 
 constexpr int RT_BM = 128;
 constexpr int RT_BK = 64;                // bf16 elements per stage row (128 B)
-constexpr int RT_MAX_STAGES = 4;
+constexpr int RT_MAX_STAGES = 8;        // as many as shared memory holds (6 at N = 128)
 constexpr int RT_EPI_WARPS = 16;
 constexpr int RT_THREADS = 64 + 32 * RT_EPI_WARPS;
 // shared scratch after the barriers: row max and softmax partials [4 groups][128 rows] fp32,
