@@ -109,24 +109,27 @@ __global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   warp_quant_row(x + s * sx_s + h * sx_h, dh, (uint64_t)t, xq, xsf, xg, lane, true);
 }
 
-// Fused quantise + group (local path, inverse map known): one warp per key (h, s)
+// Fused quantise + group (local path, inverse map known): a pair of warps per key (h, s)
 // quantises x[s, h, :] once and writes the NVFP4 row (data, scale atoms, row scale) to
 // each of the key's padded rows of the grouped A operand, so the per-token intermediate
-// never exists.  Lane l owns the 16-element blocks b = l + 32 i: every data store of a
-// destination row is 256 contiguous bytes per warp, and the four scales of a 64-element
-// chunk (lanes 4c'..4c'+3) are packed into one word with two shuffles.  The op sequence per
-// block is quant_block16 with g = amax / 2688, as in warp_quant_row.
+// never exists.  Lane l of warp half w owns the 16-element blocks b = 32 w + l + 64 i:
+// every data store of a destination row is 256 contiguous bytes per warp, and the four
+// scales of a 64-element chunk (lanes 4c'..4c'+3 of one warp) are packed into one word
+// with two shuffles; the two warps' partial row amax meet in shared memory.  The op
+// sequence per block is quant_block16 with g = amax / 2688, as in warp_quant_row.
 template <int MAXNB>
-__global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
-    quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
-                                     int dh, const int32_t* __restrict__ tok_rows,
-                                     const int32_t* __restrict__ tok_offsets, int k_fixed, int64_t R,
-                                     const int32_t* __restrict__ pad_of_row, int64_t rows, uint8_t* __restrict__ a_data,
-                                     uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
-                                     int* __restrict__ status) {
+__global__ void __launch_bounds__(256, MAXNB <= 3 ? 4 : 2)
+    quant_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
+                         const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets, int k_fixed,
+                         int64_t R, const int32_t* __restrict__ pad_of_row, int64_t rows,
+                         uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
+                         int* __restrict__ status) {
+  __shared__ float pair_amax[4][2];
   const int lane = threadIdx.x & 31;
-  const int64_t key = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);   // key = h * S + s
-  if (key >= (int64_t)H * S) return;
+  const int warp = threadIdx.x >> 5;
+  const int pair = warp >> 1, half = warp & 1;
+  const int64_t key = (int64_t)blockIdx.x * 4 + pair;   // key = h * S + s
+  if (key >= (int64_t)H * S) return;                    // both warps of a pair leave together
   const int64_t h = key / S, s = key % S;
   const __nv_bfloat16* src = x + s * sx_s + h * sx_h;
   const int nblk = dh / 16;
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
   uint4 raw[MAXNB][2];
 #pragma unroll
   for (int i = 0; i < MAXNB; ++i) {
-    const int b = lane + 32 * i;
+    const int b = 32 * half + lane + 64 * i;
     if (b < nblk) {
       raw[i][0] = *reinterpret_cast<const uint4*>(src + 16 * b);
       raw[i][1] = *reinterpret_cast<const uint4*>(src + 16 * b + 8);
@@ -166,6 +169,9 @@ __global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
   if (r0 >= 0 && r0 < R) p0 = pad_of_row[r0];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if (lane == 0) pair_amax[pair][half] = amax;
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");     // the pair's two warps
+  amax = fmaxf(pair_amax[pair][0], pair_amax[pair][1]);
   const float g = amax > 0.f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
   uint32_t codes[MAXNB][2], sfw[MAXNB];
 #pragma unroll
@@ -188,7 +194,7 @@ __global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
         pr = r >= 0 && r < R ? pad_of_row[r] : -1;
       }
       if (pr >= 0 && pr < rows) mine = pr;
-      if (mine < 0) record_error(status, MHMOE_ERR_ARGS);
+      if (mine < 0 && half == 0) record_error(status, MHMOE_ERR_ARGS);
     }
     const int n = min(32, cnt - j0);
     for (int j = 0; j < n; ++j) {
@@ -197,14 +203,14 @@ __global__ void __launch_bounds__(256, MAXNB <= 6 ? 2 : 1)
       uint8_t* drow = a_data + prow * (int64_t)(dh / 2);
 #pragma unroll
       for (int i = 0; i < MAXNB; ++i) {
-        const int b = lane + 32 * i;
+        const int b = 32 * half + lane + 64 * i;
         if (b < nblk) {
           *reinterpret_cast<uint2*>(drow + 8 * b) = make_uint2(codes[i][0], codes[i][1]);
           if ((lane & 3) == 0)
             *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)b, (uint32_t)dh)) = sfw[i];
         }
       }
-      if (lane == 0) a_gscale[prow] = g;
+      if (lane == 0 && half == 0) a_gscale[prow] = g;
     }
   }
 }
@@ -305,17 +311,17 @@ cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t s
                                  const int32_t* pad_of_row, int64_t rows, uint8_t* a_data, uint8_t* a_sf,
                                  float* a_gscale, int* status, cudaStream_t st) {
   const int64_t keys = (int64_t)S * H;
-  const unsigned grid = (unsigned)((keys + 7) / 8);
-  const int nb = (dh / 16 + 31) / 32;
+  const unsigned grid = (unsigned)((keys + 3) / 4);      // 4 keys (warp pairs) per 256-thread block
+  const int nb = (dh / 16 + 63) / 64;                    // blocks per lane
 #define MHMOE_QS(NB) \
   quant_scatter_kernel<NB><<<grid, 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, k_fixed, R, \
                                                  pad_of_row, rows, a_data, a_sf, a_gscale, status)
-  if (nb <= 2) MHMOE_QS(2);
+  if (nb <= 1) MHMOE_QS(1);
+  else if (nb <= 2) MHMOE_QS(2);
+  else if (nb <= 3) MHMOE_QS(3);
   else if (nb <= 4) MHMOE_QS(4);
   else if (nb <= 6) MHMOE_QS(6);
   else if (nb <= 8) MHMOE_QS(8);
-  else if (nb <= 12) MHMOE_QS(12);
-  else if (nb <= 16) MHMOE_QS(16);
   else return cudaErrorInvalidValue;
 #undef MHMOE_QS
   return cudaGetLastError();
