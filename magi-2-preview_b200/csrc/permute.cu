@@ -39,24 +39,33 @@ __global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int
   for (int g = threadIdx.x; g < HE; g += blockDim.x) row[g] = sh[g];
 }
 
-// One warp per key: exclusive prefix over the chunk histograms, 32 chunks per step.
+// One warp per key: exclusive prefix over the chunk histograms, 32 chunks per step; the
+// loads of 16 steps are issued together so their latencies overlap.
 __global__ void sort_colscan_kernel(int* __restrict__ hist, int nchunks, int HE, int* __restrict__ total) {
+  constexpr int U = 16;
   const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (g >= HE) return;
   int run = 0;
-  for (int c0 = 0; c0 < nchunks; c0 += 32) {
-    const int c = c0 + lane;
-    int* ptr = hist + (size_t)c * HE + g;
-    const int v = c < nchunks ? *ptr : 0;
-    int incl = v;
+  for (int c0 = 0; c0 < nchunks; c0 += 32 * U) {
+    int v[U];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + 32 * u + lane;
+      v[u] = c < nchunks ? hist[(size_t)c * HE + g] : 0;
     }
-    if (c < nchunks) *ptr = run + incl - v;
-    run += __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + 32 * u + lane;
+      int incl = v[u];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (c < nchunks) hist[(size_t)c * HE + g] = run + incl - v[u];
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
   }
   if (lane == 0) total[g] = run;
 }
@@ -132,7 +141,8 @@ __global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t
   }
 }
 
-// One warp per chunk; entries of the chunk are visited in flat order, 32 at a time.
+// One warp per chunk; entries of the chunk are visited in flat order, 32 at a time, the
+// ids and probs of 8 steps loaded together so their latencies overlap.
 __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float* __restrict__ probs, int64_t R,
                                     int S, int K, int E, int HE, int chunk, const int* __restrict__ hist,
                                     const int64_t* __restrict__ offsets, int32_t* __restrict__ gather_ids,
@@ -144,33 +154,45 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
   const int* row = hist + (size_t)blockIdx.x * HE;
   for (int g = lane; g < HE; g += 32) cursor[g] = (int)offsets[g] + row[g];
   __syncwarp();
+  constexpr int U = 8;
   const int SK = S * K;
   const int64_t f0 = (int64_t)blockIdx.x * chunk;
   const int64_t f1 = min(f0 + chunk, R);
-  for (int64_t fb = f0; fb < f1; fb += 32) {
-    const int64_t f = fb + lane;
-    int g = -1 - lane;   // distinct sentinel per invalid lane
-    bool ok = false;
-    if (f < f1) {
-      const int64_t e = idx[f];
-      ok = e >= 0 && e < E;
-      if (ok) g = (int)(f / SK) * E + (int)e;
+  for (int64_t fb0 = f0; fb0 < f1; fb0 += 32 * U) {
+    int64_t ev[U];
+    float pv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t f = fb0 + 32 * u + lane;
+      ev[u] = f < f1 ? idx[f] : -1;
+      pv[u] = f < f1 ? probs[f] : 0.f;
     }
-    const bool valid_key = ok;
-    const unsigned peers = __match_any_sync(0xffffffffu, g);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    int base = 0;
-    if (valid_key) base = cursor[g];
-    __syncwarp();
-    if (valid_key && rank == 0) cursor[g] = base + __popc(peers);
-    __syncwarp();
-    if (valid_key) {
-      const int pos = base + rank;
-      gather_ids[pos] = (int32_t)((f / K) % S);
-      probs_sorted[pos] = probs[f];
-      if (row_of_flat) row_of_flat[f] = pos;
-    } else if (f < f1 && row_of_flat) {
-      row_of_flat[f] = -1;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t f = fb0 + 32 * u + lane;
+      int g = -1 - lane;   // distinct sentinel per invalid lane
+      bool ok = false;
+      if (f < f1) {
+        const int64_t e = ev[u];
+        ok = e >= 0 && e < E;
+        if (ok) g = (int)(f / SK) * E + (int)e;
+      }
+      const bool valid_key = ok;
+      const unsigned peers = __match_any_sync(0xffffffffu, g);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      int base = 0;
+      if (valid_key) base = cursor[g];
+      __syncwarp();
+      if (valid_key && rank == 0) cursor[g] = base + __popc(peers);
+      __syncwarp();
+      if (valid_key) {
+        const int pos = base + rank;
+        gather_ids[pos] = (int32_t)((f / K) % S);
+        probs_sorted[pos] = pv[u];
+        if (row_of_flat) row_of_flat[f] = pos;
+      } else if (f < f1 && row_of_flat) {
+        row_of_flat[f] = -1;
+      }
     }
   }
 }
