@@ -19,6 +19,8 @@ __global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const 
                                 const int* __restrict__ tile_rows, int32_t* __restrict__ pad_of_row, int dh,
                                 uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf,
                                 float* __restrict__ a_gscale) {
+  pdl_wait();
+  pdl_trigger();
   const int mt = blockIdx.x;
   if (mt >= cu_tiles[HE]) return;
   const int m = threadIdx.x;
@@ -130,6 +132,8 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
                                const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
                                int k_fixed, int64_t R, int64_t P_rows, __nv_bfloat16* __restrict__ y, int64_t sy_s,
                                int64_t sy_h) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int srt[COMBINE_WARPS][32];
   const int warp = threadIdx.x >> 5;
   const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
@@ -197,6 +201,8 @@ __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const
 
 // One warp per (s, h) row, 16-B stores.
 __global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ y, int S, int H, int dh, int64_t sy_s, int64_t sy_h) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t key = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (key >= (int64_t)S * H) return;
   const int64_t s = key / H, h = key % H;
@@ -207,14 +213,14 @@ __global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ y, int S, int H, in
 cudaError_t launch_zero_rows(__nv_bfloat16* y, int S, int H, int dh, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
   const int64_t rows = (int64_t)S * H;
   if (rows == 0) return cudaSuccess;
-  zero_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(y, S, H, dh, sy_s, sy_h);
+  MHMOE_LAUNCH_PDL(zero_rows_kernel, (unsigned)((rows + 7) / 8), 256, 0, st, y, S, H, dh, sy_s, sy_h);
   return cudaGetLastError();
 }
 
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
                             const int* tile_rows, int32_t* pad_of_row, cudaStream_t st, int dh, uint8_t* a_data,
                             uint8_t* a_sf, float* a_gscale) {
-  pad_rows_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(cu_tiles, HE, tile_row0, tile_rows, pad_of_row, dh, a_data,
+  MHMOE_LAUNCH_PDL(pad_rows_kernel, (unsigned)max_mtiles, 128, 0, st, cu_tiles, HE, tile_row0, tile_rows, pad_of_row, dh, a_data,
                                                         a_sf, a_gscale);
   return cudaGetLastError();
 }
@@ -223,7 +229,7 @@ cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, in
                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
                            int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
   const int64_t keys = (int64_t)H * S;
-  combine_kernel<<<(unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st>>>(
+  MHMOE_LAUNCH_PDL(combine_kernel, (unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st, 
       P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
   return cudaGetLastError();
 }

@@ -225,6 +225,8 @@ template <int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const FfnGemmParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int STAGES = gemm_stages(EPI);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));

@@ -11,6 +11,30 @@ namespace mhmoe {
 
 // Upper bound of 128-row tiles for R rows spread over n_experts groups.
 // align: tiles per expert rounded up to a multiple of align (2 for the CTA-pair GEMM).
+// Launch with programmatic stream serialization (see pdl_wait / pdl_trigger).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// launch_pdl from a function returning cudaError_t: returns the launch error, if any.
+#define MHMOE_LAUNCH_PDL(kernel, grid, block, smem, st, ...)                                              \
+  do {                                                                                                     \
+    const cudaError_t mhmoe_le_ = launch_pdl(kernel, dim3(grid), dim3(block), (size_t)(smem), st, __VA_ARGS__); \
+    if (mhmoe_le_ != cudaSuccess) return mhmoe_le_;                                                        \
+  } while (0)
+
 inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts, int align = 1) {
   return (R + 127) / 128 + (int64_t)align * n_experts;
 }

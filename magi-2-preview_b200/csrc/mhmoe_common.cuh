@@ -54,6 +54,14 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
+// Programmatic dependent launch.  Every hot-path kernel starts with pdl_wait() (the
+// results of the kernel before it in the stream are complete and visible; a no-op when the
+// kernel was launched without the attribute) and then pdl_trigger(), which lets the next
+// kernel's CTAs be scheduled once all of this kernel's CTAs have started — they park in
+// their own pdl_wait(), so the launch latency of each kernel boundary is hidden.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

@@ -19,6 +19,8 @@ namespace mhmoe {
 
 __global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int SK, int E, int HE, int chunk,
                                  int* __restrict__ hist, int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sh[];
   for (int g = threadIdx.x; g < HE; g += blockDim.x) sh[g] = 0;
   __syncthreads();
@@ -42,6 +44,8 @@ __global__ void sort_hist_kernel(const int64_t* __restrict__ idx, int64_t R, int
 // One warp per key: exclusive prefix over the chunk histograms, 32 chunks per step; the
 // loads of 16 steps are issued together so their latencies overlap.
 __global__ void sort_colscan_kernel(int* __restrict__ hist, int nchunks, int HE, int* __restrict__ total) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int U = 16;
   const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -77,6 +81,8 @@ __global__ void tile_tables_kernel(const int* __restrict__ counts, const int64_t
                                    int* __restrict__ tile_expert, int* __restrict__ tile_row0,
                                    int* __restrict__ tile_rows, int64_t max_mtiles, int* __restrict__ status,
                                    int align) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int64_t s_carry_rows;
   __shared__ int s_carry_tiles;
   __shared__ int64_t s_rows[1024];
@@ -147,6 +153,8 @@ __global__ void sort_scatter_kernel(const int64_t* __restrict__ idx, const float
                                     int S, int K, int E, int HE, int chunk, const int* __restrict__ hist,
                                     const int64_t* __restrict__ offsets, int32_t* __restrict__ gather_ids,
                                     float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat) {
+  pdl_wait();
+  pdl_trigger();
   // Entries with a negative ("no expert") or out-of-range id get no slot; their
   // row_of_flat entry is -1.
   extern __shared__ int cursor[];
@@ -212,6 +220,8 @@ __global__ void __launch_bounds__(1024, 1)
     sort_small_kernel(const int64_t* __restrict__ idx, const float* __restrict__ probs, int R, int S, int K, int E,
                       int HE, int64_t* __restrict__ expert_offsets, int32_t* __restrict__ gather_ids,
                       float* __restrict__ probs_sorted, int32_t* __restrict__ row_of_flat, int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sort_small_smem[];
   int* hist = sort_small_smem;                                   // [32][HE]: count, then first slot
   int* key = hist + 32 * SORT_SMALL_MAX_KEYS;                   // [R]
@@ -302,6 +312,8 @@ __global__ void tok_count_kernel(const int32_t* __restrict__ gather_ids, const i
                                  int HE, int E, int S, const int* __restrict__ tile_expert,
                                  const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
                                  int* __restrict__ tok_count, int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int mt = blockIdx.x;
   if (mt >= cu_tiles[HE]) return;
   const int m = threadIdx.x;
@@ -319,6 +331,8 @@ __global__ void tok_count_kernel(const int32_t* __restrict__ gather_ids, const i
 // Exclusive scan, pass 1: per-block scan of 4096 entries, block sums out.
 __global__ void scan_block_kernel(const int* __restrict__ in, int n, int* __restrict__ out,
                                   int* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int sh[1024];
   const int base = blockIdx.x * 4096 + threadIdx.x * 4;
   int v[4], s = 0;
@@ -347,6 +361,8 @@ __global__ void scan_block_kernel(const int* __restrict__ in, int n, int* __rest
 // Pass 2: exclusive scan of the block sums in place (single CTA, serial carry) and
 // the grand total into out_total.
 __global__ void scan_sums_kernel(int* __restrict__ block_sums, int nblocks, int* __restrict__ out_total) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int sh[1024];
   __shared__ int carry;
   if (threadIdx.x == 0) carry = 0;
@@ -372,6 +388,8 @@ __global__ void scan_sums_kernel(int* __restrict__ block_sums, int nblocks, int*
 
 // Pass 3: add block offsets.
 __global__ void scan_add_kernel(int* __restrict__ out, int n, const int* __restrict__ block_sums) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] += block_sums[i / 4096];
 }
@@ -381,6 +399,8 @@ __global__ void tok_fill_kernel(const int32_t* __restrict__ gather_ids, const in
                                 const int* __restrict__ tile_row0, const int* __restrict__ tile_rows,
                                 const int* __restrict__ tok_offsets, int* __restrict__ tok_cursor,
                                 int32_t* __restrict__ tok_rows) {
+  pdl_wait();
+  pdl_trigger();
   const int mt = blockIdx.x;
   if (mt >= cu_tiles[HE]) return;
   const int m = threadIdx.x;
@@ -422,16 +442,16 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
     static cudaError_t attr = cudaFuncSetAttribute(sort_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SORT_SMALL_SMEM);
     if (attr != cudaSuccess) return attr;
-    sort_small_kernel<<<1, 1024, SORT_SMALL_SMEM, st>>>(idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids,
+    MHMOE_LAUNCH_PDL(sort_small_kernel, 1, 1024, SORT_SMALL_SMEM, st, idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids,
                                                         probs_sorted, row_of_flat, status);
     return cudaGetLastError();
   }
   const size_t shb = (size_t)HE * sizeof(int);
-  sort_hist_kernel<<<nchunks, 256, shb, st>>>(idx, R, S * K, E, HE, chunk, hist, status);
-  sort_colscan_kernel<<<(HE + 7) / 8, 256, 0, st>>>(hist, nchunks, HE, total);
-  tile_tables_kernel<<<1, 1024, 0, st>>>(total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
+  MHMOE_LAUNCH_PDL(sort_hist_kernel, nchunks, 256, shb, st, idx, R, S * K, E, HE, chunk, hist, status);
+  MHMOE_LAUNCH_PDL(sort_colscan_kernel, (HE + 7) / 8, 256, 0, st, hist, nchunks, HE, total);
+  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
                                          tile_rows, mtiles_upper_bound(R, HE), status, 1);
-  sort_scatter_kernel<<<nchunks, 32, shb, st>>>(idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
+  MHMOE_LAUNCH_PDL(sort_scatter_kernel, nchunks, 32, shb, st, idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
                                                 gather_ids, probs_sorted, row_of_flat);
   return cudaGetLastError();
 }
@@ -447,7 +467,7 @@ size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk) {
 cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
                                int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st,
                                int align) {
-  tile_tables_kernel<<<1, 1024, 0, st>>>(nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert, tile_row0,
+  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert, tile_row0,
                                          tile_rows, max_tiles, status, align);
   return cudaGetLastError();
 }
@@ -466,12 +486,12 @@ cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, con
   int* bsums = cursor + T;
   const int nblk = (int)((T + 4095) / 4096);
   cudaMemsetAsync(cnt, 0, (size_t)(2 * T) * sizeof(int), st);
-  tok_count_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
+  MHMOE_LAUNCH_PDL(tok_count_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
                                                          tile_rows, cnt, status);
-  scan_block_kernel<<<nblk, 1024, 0, st>>>(cnt, (int)T, tok_offsets, bsums);
-  scan_sums_kernel<<<1, 1024, 0, st>>>(bsums, nblk, tok_offsets + T);
-  scan_add_kernel<<<(unsigned)((T + 255) / 256), 256, 0, st>>>(tok_offsets, (int)T, bsums);
-  tok_fill_kernel<<<(unsigned)max_mtiles, 128, 0, st>>>(gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
+  MHMOE_LAUNCH_PDL(scan_block_kernel, nblk, 1024, 0, st, cnt, (int)T, tok_offsets, bsums);
+  MHMOE_LAUNCH_PDL(scan_sums_kernel, 1, 1024, 0, st, bsums, nblk, tok_offsets + T);
+  MHMOE_LAUNCH_PDL(scan_add_kernel, (unsigned)((T + 255) / 256), 256, 0, st, tok_offsets, (int)T, bsums);
+  MHMOE_LAUNCH_PDL(tok_fill_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
                                                         tile_rows, tok_offsets, cursor, tok_rows);
   return cudaGetLastError();
 }

@@ -72,6 +72,8 @@ __global__ void group_rows_kernel(const uint8_t* __restrict__ xq, int64_t xq_pit
                                   const int* __restrict__ tile_rows, uint8_t* __restrict__ a_data,
                                   uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
                                   int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t prow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int mt = (int)(prow >> 7);
@@ -102,6 +104,8 @@ __global__ void group_rows_kernel(const uint8_t* __restrict__ xq, int64_t xq_pit
 __global__ void quant_tokens_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
                                     int dh, uint8_t* __restrict__ xq, uint8_t* __restrict__ xsf,
                                     float* __restrict__ xg) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= (int64_t)S * H) return;
@@ -124,6 +128,8 @@ __global__ void __launch_bounds__(256, MAXNB <= 3 ? 4 : 2)
                          int64_t R, const int32_t* __restrict__ pad_of_row, int64_t rows,
                          uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
                          int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float pair_amax[4][2];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -290,7 +296,7 @@ cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t
                               const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
                               uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
   const int64_t rows = max_mtiles * 128;
-  group_rows_kernel<<<(unsigned)(rows / 8), 256, 0, st>>>(xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H,
+  MHMOE_LAUNCH_PDL(group_rows_kernel, (unsigned)(rows / 8), 256, 0, st, xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H,
                                                           E_per_head, gather_ids, cu_tiles,
                                                           HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
                                                           a_gscale, status);
@@ -300,7 +306,7 @@ cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t
 cudaError_t launch_quant_tokens(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, int dh,
                                 uint8_t* xq, uint8_t* xsf, float* xg, cudaStream_t st) {
   const int64_t T = (int64_t)S * H;
-  quant_tokens_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, xq, xsf, xg);
+  MHMOE_LAUNCH_PDL(quant_tokens_kernel, (unsigned)((T + 7) / 8), 256, 0, st, x, sx_s, sx_h, S, H, dh, xq, xsf, xg);
   return cudaGetLastError();
 }
 
@@ -314,7 +320,7 @@ cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t s
   const unsigned grid = (unsigned)((keys + 3) / 4);      // 4 keys (warp pairs) per 256-thread block
   const int nb = (dh / 16 + 63) / 64;                    // blocks per lane
 #define MHMOE_QS(NB) \
-  quant_scatter_kernel<NB><<<grid, 256, 0, st>>>(x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, k_fixed, R, \
+  MHMOE_LAUNCH_PDL(quant_scatter_kernel<NB>, grid, 256, 0, st, x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, k_fixed, R, \
                                                  pad_of_row, rows, a_data, a_sf, a_gscale, status)
   if (nb <= 1) MHMOE_QS(1);
   else if (nb <= 2) MHMOE_QS(2);

@@ -78,6 +78,8 @@ template <int KM>
 __global__ void __launch_bounds__(RT_THREADS, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
                      const RouterParams p) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int a_bytes = RT_BM * RT_BK * 2;
@@ -421,8 +423,7 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   }
   const int tiles = ((S + RT_BM - 1) / RT_BM) * H;
   const int grid = std::max(1, std::min(tiles, num_sms()));
-  kernel<<<grid, RT_THREADS, smem, st>>>(tx, tg, p);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(kernel, dim3(grid), dim3(RT_THREADS), (size_t)smem, st, tx, tg, p);
   if (e != cudaSuccess) {
     *cerr = e;
     return MHMOE_ERR_LAUNCH;
