@@ -220,8 +220,8 @@ cudaError_t launch_zero_rows(__nv_bfloat16* y, int S, int H, int dh, int64_t sy_
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
                             const int* tile_rows, int32_t* pad_of_row, cudaStream_t st, int dh, uint8_t* a_data,
                             uint8_t* a_sf, float* a_gscale) {
-  MHMOE_LAUNCH_PDL(pad_rows_kernel, (unsigned)max_mtiles, 128, 0, st, cu_tiles, HE, tile_row0, tile_rows, pad_of_row, dh, a_data,
-                                                        a_sf, a_gscale);
+  MHMOE_LAUNCH_PDL(pad_rows_kernel, (unsigned)max_mtiles, 128, 0, st, cu_tiles, HE, tile_row0, tile_rows, pad_of_row,
+                   dh, a_data, a_sf, a_gscale);
   return cudaGetLastError();
 }
 
@@ -229,8 +229,8 @@ cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, in
                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
                            int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
   const int64_t keys = (int64_t)H * S;
-  MHMOE_LAUNCH_PDL(combine_kernel, (unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st, 
-      P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
+  MHMOE_LAUNCH_PDL(combine_kernel, (unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st,
+                   P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
   return cudaGetLastError();
 }
 

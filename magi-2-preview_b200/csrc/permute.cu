@@ -442,17 +442,17 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
     static cudaError_t attr = cudaFuncSetAttribute(sort_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    SORT_SMALL_SMEM);
     if (attr != cudaSuccess) return attr;
-    MHMOE_LAUNCH_PDL(sort_small_kernel, 1, 1024, SORT_SMALL_SMEM, st, idx, probs, (int)R, S, K, E, HE, expert_offsets, gather_ids,
-                                                        probs_sorted, row_of_flat, status);
+    MHMOE_LAUNCH_PDL(sort_small_kernel, 1, 1024, SORT_SMALL_SMEM, st, idx, probs, (int)R, S, K, E, HE, expert_offsets,
+                     gather_ids, probs_sorted, row_of_flat, status);
     return cudaGetLastError();
   }
   const size_t shb = (size_t)HE * sizeof(int);
   MHMOE_LAUNCH_PDL(sort_hist_kernel, nchunks, 256, shb, st, idx, R, S * K, E, HE, chunk, hist, status);
   MHMOE_LAUNCH_PDL(sort_colscan_kernel, (HE + 7) / 8, 256, 0, st, hist, nchunks, HE, total);
-  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, total, nullptr, HE, expert_offsets, cu_tiles, tile_expert, tile_row0,
-                                         tile_rows, mtiles_upper_bound(R, HE), status, 1);
+  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, total, nullptr, HE, expert_offsets, cu_tiles, tile_expert,
+                   tile_row0, tile_rows, mtiles_upper_bound(R, HE), status, 1);
   MHMOE_LAUNCH_PDL(sort_scatter_kernel, nchunks, 32, shb, st, idx, probs, R, S, K, E, HE, chunk, hist, expert_offsets,
-                                                gather_ids, probs_sorted, row_of_flat);
+                   gather_ids, probs_sorted, row_of_flat);
   return cudaGetLastError();
 }
 
@@ -467,8 +467,8 @@ size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk) {
 cudaError_t launch_tile_tables(const int64_t* expert_offsets, int HE, int64_t max_tiles, int* cu_tiles,
                                int* tile_expert, int* tile_row0, int* tile_rows, int* status, cudaStream_t st,
                                int align) {
-  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert, tile_row0,
-                                         tile_rows, max_tiles, status, align);
+  MHMOE_LAUNCH_PDL(tile_tables_kernel, 1, 1024, 0, st, nullptr, expert_offsets, HE, nullptr, cu_tiles, tile_expert,
+                   tile_row0, tile_rows, max_tiles, status, align);
   return cudaGetLastError();
 }
 
@@ -486,13 +486,13 @@ cudaError_t launch_token_rows(const int32_t* gather_ids, int64_t max_mtiles, con
   int* bsums = cursor + T;
   const int nblk = (int)((T + 4095) / 4096);
   cudaMemsetAsync(cnt, 0, (size_t)(2 * T) * sizeof(int), st);
-  MHMOE_LAUNCH_PDL(tok_count_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
-                                                         tile_rows, cnt, status);
+  MHMOE_LAUNCH_PDL(tok_count_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert,
+                   tile_row0, tile_rows, cnt, status);
   MHMOE_LAUNCH_PDL(scan_block_kernel, nblk, 1024, 0, st, cnt, (int)T, tok_offsets, bsums);
   MHMOE_LAUNCH_PDL(scan_sums_kernel, 1, 1024, 0, st, bsums, nblk, tok_offsets + T);
   MHMOE_LAUNCH_PDL(scan_add_kernel, (unsigned)((T + 255) / 256), 256, 0, st, tok_offsets, (int)T, bsums);
-  MHMOE_LAUNCH_PDL(tok_fill_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert, tile_row0,
-                                                        tile_rows, tok_offsets, cursor, tok_rows);
+  MHMOE_LAUNCH_PDL(tok_fill_kernel, (unsigned)max_mtiles, 128, 0, st, gather_ids, cu_tiles, HE, E, S, tile_expert,
+                   tile_row0, tile_rows, tok_offsets, cursor, tok_rows);
   return cudaGetLastError();
 }
 

@@ -296,10 +296,9 @@ cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t
                               const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
                               uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
   const int64_t rows = max_mtiles * 128;
-  MHMOE_LAUNCH_PDL(group_rows_kernel, (unsigned)(rows / 8), 256, 0, st, xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T, dh, H,
-                                                          E_per_head, gather_ids, cu_tiles,
-                                                          HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
-                                                          a_gscale, status);
+  MHMOE_LAUNCH_PDL(group_rows_kernel, (unsigned)(rows / 8), 256, 0, st, xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T,
+                   dh, H, E_per_head, gather_ids, cu_tiles, HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
+                   a_gscale, status);
   return cudaGetLastError();
 }
 
@@ -319,9 +318,9 @@ cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t s
   const int64_t keys = (int64_t)S * H;
   const unsigned grid = (unsigned)((keys + 3) / 4);      // 4 keys (warp pairs) per 256-thread block
   const int nb = (dh / 16 + 63) / 64;                    // blocks per lane
-#define MHMOE_QS(NB) \
-  MHMOE_LAUNCH_PDL(quant_scatter_kernel<NB>, grid, 256, 0, st, x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, k_fixed, R, \
-                                                 pad_of_row, rows, a_data, a_sf, a_gscale, status)
+#define MHMOE_QS(NB)                                                                                       \
+  MHMOE_LAUNCH_PDL(quant_scatter_kernel<NB>, grid, 256, 0, st, x, sx_s, sx_h, S, H, dh, tok_rows, tok_offsets, \
+                   k_fixed, R, pad_of_row, rows, a_data, a_sf, a_gscale, status)
   if (nb <= 1) MHMOE_QS(1);
   else if (nb <= 2) MHMOE_QS(2);
   else if (nb <= 3) MHMOE_QS(3);
