@@ -16,27 +16,13 @@ constexpr int COMBINE_WARPS = 4;
 
 // pad_of_row[r] = padded row of sorted row r: mt * 128 + m for tile rows m < tile_rows[mt].
 __global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const int* __restrict__ tile_row0,
-                                const int* __restrict__ tile_rows, int32_t* __restrict__ pad_of_row, int dh,
-                                uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf,
-                                float* __restrict__ a_gscale) {
+                                const int* __restrict__ tile_rows, int32_t* __restrict__ pad_of_row) {
   pdl_wait();
   pdl_trigger();
   const int mt = blockIdx.x;
   if (mt >= cu_tiles[HE]) return;
   const int m = threadIdx.x;
-  const int nrows = tile_rows[mt];
-  if (m < nrows) pad_of_row[tile_row0[mt] + m] = mt * 128 + m;
-  if (a_data == nullptr || nrows >= 128) return;
-  // A operand padding rows [nrows, 128) of this m-tile: zero codes and scales, row scale 1
-  const int64_t row0 = (int64_t)mt * 128;
-  uint4* d = reinterpret_cast<uint4*>(a_data + (row0 + nrows) * (int64_t)(dh / 2));
-  const int n16 = (128 - nrows) * (dh / 32);
-  for (int i = m; i < n16; i += blockDim.x) d[i] = make_uint4(0, 0, 0, 0);
-  const int nch = dh / 64;
-  for (int i = m; i < (128 - nrows) * nch; i += blockDim.x)
-    *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)(row0 + nrows + i / nch), (uint32_t)(4 * (i % nch)),
-                                                       (uint32_t)dh)) = 0u;
-  if (m >= nrows) a_gscale[row0 + m] = 1.0f;
+  if (m < tile_rows[mt]) pad_of_row[tile_row0[mt] + m] = mt * 128 + m;
 }
 
 // Sum of one key's rows (cnt ids at tok_rows[begin..]) into yrow, one warp.
@@ -218,10 +204,8 @@ cudaError_t launch_zero_rows(__nv_bfloat16* y, int S, int H, int dh, int64_t sy_
 }
 
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
-                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st, int dh, uint8_t* a_data,
-                            uint8_t* a_sf, float* a_gscale) {
-  MHMOE_LAUNCH_PDL(pad_rows_kernel, (unsigned)max_mtiles, 128, 0, st, cu_tiles, HE, tile_row0, tile_rows, pad_of_row,
-                   dh, a_data, a_sf, a_gscale);
+                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st) {
+  MHMOE_LAUNCH_PDL(pad_rows_kernel, (unsigned)max_mtiles, 128, 0, st, cu_tiles, HE, tile_row0, tile_rows, pad_of_row);
   return cudaGetLastError();
 }
 

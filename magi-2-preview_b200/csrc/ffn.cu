@@ -226,8 +226,9 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   // Local tokens are quantised once and written straight into their grouped rows; tokens
   // that arrive pre-quantised (expert-parallel receive) are grouped by copy.
   const bool fused = !prequant && dh <= quant_scatter_max_dh();
-  MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st, dh,
-                            fused ? w.a_data : nullptr, w.a_sf, w.a_gscale));
+  // (the A operand's padding rows stay unwritten: each row's GEMM results depend on that row
+  // alone, and nothing reads a padding row's hidden or partial output)
+  MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));
   if (fused) {
     MHMOE_TRY(launch_quant_scatter(x, sx_s, sx_h, S, H, dh, rows_map, offs_map, kf, R, w.pad_of_row, rows, w.a_data,
                                    w.a_sf, w.a_gscale, status, st));

@@ -137,10 +137,9 @@ cudaError_t launch_topk(const float* logits, const float* bias, int H, int S, in
                         cudaStream_t st);
 
 // combine.cu
-// sorted row -> padded row; with a_data, also zero-fills the A operand's padding rows
+// sorted row -> padded row
 cudaError_t launch_pad_rows(const int* cu_tiles, int HE, int64_t max_mtiles, const int* tile_row0,
-                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st, int dh = 0,
-                            uint8_t* a_data = nullptr, uint8_t* a_sf = nullptr, float* a_gscale = nullptr);
+                            const int* tile_rows, int32_t* pad_of_row, cudaStream_t st);
 cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, int dh, int S, int H,
                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
                            int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st);
