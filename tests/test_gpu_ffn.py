@@ -31,6 +31,8 @@ CASES = [
     (200, 2, 256, 512, 4, 3, 1, 0.0),
     (333, 1, 512, 256, 16, 4, 2, 2.0),     # Zipf-skewed: empty and crowded experts
     (40, 1, 256, 256, 8, 1, 3, 0.0),       # fewer rows than one tile
+    (96, 1, 3072, 512, 8, 4, 4, 0.0),      # config-1 head width: 3 blocks per lane in the quantiser
+    (64, 1, 4096, 256, 4, 2, 5, 1.0),      # 4 blocks per lane, K > 3072 in the gate/up GEMM
 ]
 
 

@@ -16,6 +16,7 @@ CASES = [
     (512, 1, 1024, 2048, 8, 2, "softmax", 1.0, False),
     (256, 2, 256, 256, 16, 3, "sigmoid", 4.9, True),       # production-style scoring
     (200, 1, 512, 512, 64, 8, "softmax", 1.0, True),
+    (128, 1, 3072, 1024, 16, 8, "softmax", 1.0, False),   # config-1 layer shape, fewer experts
 ]
 
 
