@@ -49,11 +49,12 @@ CFG2 = dict(name="config2", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=2, s
 CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, score_func="softmax")
 CFG4 = dict(name="config4", S=256, d=3072, H=1, E=128, K=8, de=1024, seed=4, score_func="softmax", layers=4)
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
-# libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, token quantise,
-# row grouping, gate/up GEMM, down GEMM, combine (atomic scatter: output zeroing instead).  EP (records arrive quantised): router,
+# libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, fused token
+# quantise + row grouping, gate/up GEMM, down GEMM, combine (atomic scatter: output zeroing
+# instead).  EP (records arrive quantised): router,
 # token quantise, destination mask, send sort x4, pack, unpack, receiver sort x4, tile tables,
 # pad map, row grouping, gate/up GEMM, down GEMM, per-record combine, source-side combine.
-KERNELS_PER_STEP = 12
+KERNELS_PER_STEP = 11
 KERNELS_PER_STEP_EP = 20
 CPU_SAMPLE_TOKENS = 512
 
