@@ -35,26 +35,31 @@ def _is_deterministic() -> bool:
     return os.environ.get("MHMOE_SCATTER", "combine") != "atomic"
 
 
-# Packed operands keyed by their source tensors' (address, version, shape, dtype, device).
-# An entry lives only as long as every source tensor object it was packed from: a weakref
-# callback evicts it when one dies, so a new tensor later allocated at the same address
-# (same version 0, same shape) can never pick up another tensor's packed weights.
-_pack_cache: dict[tuple, object] = {}
+# Packed operands, one entry per set of source tensors, keyed by their (address, shape,
+# dtype, device) and holding the versions they were packed at: an in-place update repacks
+# into the same entry (no stale copies pile up).  An entry lives only as long as every
+# source tensor object it was packed from: a weakref callback evicts it when one dies, so a
+# new tensor later allocated at the same address can never pick up another tensor's
+# packed weights.
+_pack_cache: dict[tuple, tuple] = {}
 
 
 def _key(t: torch.Tensor) -> tuple:
-    return (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device)
+    return (t.data_ptr(), tuple(t.shape), t.dtype, t.device)
 
 
 def _cached_pack(tag: str, srcs: tuple, pack):
     k = (tag,) + tuple(x for t in srcs for x in _key(t))
+    versions = tuple(t._version for t in srcs)
     hit = _pack_cache.get(k)
+    if hit is not None and hit[0] == versions:
+        return hit[1]
+    packed = pack(*srcs)
     if hit is None:
-        hit = pack(*srcs)
-        _pack_cache[k] = hit
         for t in srcs:
             weakref.finalize(t, _pack_cache.pop, k, None)
-    return hit
+    _pack_cache[k] = (versions, packed)
+    return packed
 
 
 def packed_weights(W_gate, W_up, W_down) -> tuple[NVFP4GateUp, NVFP4Down]:

@@ -16,14 +16,16 @@ def test_reuse_while_alive_and_evict_on_free():
         return object()
 
     a, b = torch.zeros(4, 8), torch.ones(4, 8)
+    n0 = len(fwd._pack_cache)
     first = fwd._cached_pack("test", (a, b), pack)
     assert fwd._cached_pack("test", (a, b), pack) is first and len(packs) == 1
-    b.add_(1)                                   # in-place update: new version, repacked
-    assert fwd._cached_pack("test", (a, b), pack) is not first and len(packs) == 2
-    n = len(fwd._pack_cache)
+    for _ in range(3):
+        b.add_(1)                               # in-place update: new version, repacked ...
+        assert fwd._cached_pack("test", (a, b), pack) is not first and len(packs) >= 2
+    assert len(fwd._pack_cache) == n0 + 1       # ... into the same entry
     del b, packs[:]
     gc.collect()
-    assert len(fwd._pack_cache) == n - 2        # both entries named the freed tensor
+    assert len(fwd._pack_cache) == n0           # the entry named the freed tensor
 
 
 def test_module_key_is_identity_based():
