@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
-      // merge: round 1 (1 -> 0, 3 -> 2), round 2 (2 -> 0); slot index [q][slot][j][lane]
+      // merge: first step 1 -> 0 and 3 -> 2, second step 2 -> 0; slot index [q][slot][j][lane]
       auto put = [&](int slot) {
 #pragma unroll
         for (int j = 0; j < KM; ++j) {

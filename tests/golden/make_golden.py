@@ -1,10 +1,10 @@
 """Generate golden fixtures by running the reference implementation itself.
 
-Run once, in a container that has the reference checkout (default
-``/root/reference``; override with ``MAGI2_REFERENCE``).  The fixtures are
-committed; nothing at test time reads the reference.
+Run once, in a container that has the reference checkout, with ``MAGI2_REFERENCE``
+naming its root directory.  The fixtures are committed; nothing at test time reads the
+reference.
 
-    python tests/golden/make_golden.py
+    MAGI2_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Produces:
 * ``route_cases.npz`` — inputs/outputs of ``compute_topk_probs_and_indices``
@@ -25,11 +25,15 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("MAGI2_REFERENCE", "/root/reference"))
+def _reference_root() -> Path:
+    root = os.environ.get("MAGI2_REFERENCE")
+    if not root:
+        raise SystemExit("set MAGI2_REFERENCE to the reference checkout's root directory")
+    return Path(root)
 
 
 def _import_reference():
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(_reference_root()))
     import torch  # noqa: F401
     from inference.flash_mh_moe import route  # type: ignore
     return route
