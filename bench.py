@@ -35,6 +35,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -69,29 +70,102 @@ def load_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons while the timed steps run.
+
+    An NVML polling thread (every 5 ms: the timed region lasts tens of milliseconds) records
+    (host time, SM clock, clocks-event reasons); the caller marks the timed region with
+    window(start, end) in host time (perf_counter, the timed launches issued after `start`
+    and synchronised before `end`) and summary() reports the samples inside it.  nvidia-smi
+    sampling (200 ms, the profiling recipe's clocks line) runs beside it as the fallback when
+    NVML is unavailable.  Only reads: no clock or other GPU setting is changed."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.005
+    REASONS = (("hw_slowdown", "HwSlowdown", 0x8), ("hw_thermal_slowdown", "HwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "SwThermalSlowdown", 0x20), ("sw_power_cap", "SwPowerCap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
         self.path = Path(tempfile.mkstemp(prefix="clk", suffix=".csv")[1])
+        self.nv: list[tuple[float, float, int]] = []
+        self.nv_max = None
+        self.win = None
+        self._nvml = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.smi_id = str(gpu_index)
+
+    def window(self, t_start: float, t_end: float) -> None:
+        self.win = (t_start, t_end)
+
+    def _gpu_uuid(self):
+        """"GPU-<uuid>" of CUDA device idx (NVML and nvidia-smi number GPUs in the driver's
+        order, not CUDA_VISIBLE_DEVICES's), or None."""
+        try:
+            import torch
+            if not torch.cuda.is_available():
+                return None
+            u = str(torch.cuda.get_device_properties(self.idx).uuid)
+            return u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            return None
+
+    def _start_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = None
+            uuid = self._gpu_uuid()
+            if uuid and hasattr(pynvml, "nvmlDeviceGetHandleByUUID"):
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+                    self.smi_id = uuid             # validated: nvidia-smi can use it too
+                except Exception:
+                    h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.nv_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = (getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None)
+                       or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons)
+        except Exception:
+            return
+        self._nvml = pynvml
+
+        def poll():
+            while not self._stop.is_set():
+                try:
+                    t = time.perf_counter()
+                    self.nv.append((t, float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), int(reasons(h))))
+                except Exception:
+                    return
+                self._stop.wait(self.PERIOD_S)
+
+        self._thread = threading.Thread(target=poll, daemon=True)
+        self._thread.start()
 
     def __enter__(self):
+        self._start_nvml()
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
-            time.sleep(0.3)
+                                          "-lms", "200", "-i", self.smi_id], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+        time.sleep(0.3)
         return self
 
     def __exit__(self, *a):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -101,7 +175,25 @@ class ClockSampler:
                 self.proc.kill()
             self.f.close()
 
+    def _summary_nvml(self):
+        inside = [x for x in self.nv if self.win and self.win[0] <= x[0] <= self.win[1]]
+        use = inside or self.nv
+        bits = 0
+        for x in use:
+            bits |= x[2]
+        reasons = []
+        for name, const, default in self.REASONS:
+            mask = getattr(self._nvml, "nvmlClocksEventReason" + const,
+                           getattr(self._nvml, "nvmlClocksThrottleReason" + const, default))
+            if bits & int(mask):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(x[1] for x in use), "sm_max_mhz": self.nv_max, "reasons": reasons,
+                "samples": len(use), "source": "nvml, " + ("inside the timed region" if inside else
+                                                            "around the timed region")}
+
     def summary(self) -> dict:
+        if self.nv:
+            return self._summary_nvml()
         rows = []
         try:
             for ln in self.path.read_text().splitlines():
@@ -117,7 +209,7 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, around the timed region"}
 
 
 def dist_setup():
@@ -236,11 +328,13 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
+        h0 = time.perf_counter()
         t0.record()
         for k in range(args.steps):
             step(m, x, evs[k])
         t1.record()
         torch.cuda.synchronize()
+        clk.window(h0, time.perf_counter())
     if world > 1:
         dist.barrier()
     _lib.check_device_status(dev)
@@ -519,11 +613,13 @@ def run_stack(args, cfg, dev):
     torch.cuda.synchronize()
     _lib.check_device_status(dev)
     with ClockSampler(0) as clk:
+        h0 = time.perf_counter()
         t0.record()
         for _ in range(args.steps):
             g(x0)
         t1.record()
         torch.cuda.synchronize()
+        clk.window(h0, time.perf_counter())
     ms = t0.elapsed_time(t1) / args.steps
     gu, dn = layers[0].packed_weights()
     wbytes = sum(t.numel() * t.element_size() for t in (gu.data, gu.sf, gu.gscale, dn.data, dn.sf, dn.gscale))
