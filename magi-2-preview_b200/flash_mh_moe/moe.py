@@ -18,6 +18,8 @@ expert ranges and tokens travel to their experts (flash_mh_moe.ep).
 """
 from __future__ import annotations
 
+import itertools
+import weakref
 from dataclasses import dataclass
 
 import torch
@@ -51,7 +53,10 @@ class CoreMultiHeadMoEConfig:
     recompute_once_in_bwd: bool = True
 
 
-_magi2_moe_registry: dict[int, "CoreMultiHeadMoE"] = {}
+# Modules by their op key.  Weak values: registering a module does not keep it (and its
+# weights) alive; keys come from a counter, so a key is never reused after a module dies.
+_magi2_moe_registry: "weakref.WeakValueDictionary[int, CoreMultiHeadMoE]" = weakref.WeakValueDictionary()
+_magi2_moe_keys = itertools.count()
 
 
 class CoreMultiHeadMoE(nn.Module):
@@ -59,7 +64,7 @@ class CoreMultiHeadMoE(nn.Module):
         super().__init__()
         if config.hidden_size % config.num_heads != 0:
             raise ValueError("hidden_size must be divisible by num_heads")
-        self._moe_key = len(_magi2_moe_registry)
+        self._moe_key = next(_magi2_moe_keys)
         _magi2_moe_registry[self._moe_key] = self
         self.config = config
         self.num_heads = config.num_heads
