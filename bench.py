@@ -49,6 +49,11 @@ CFG1 = dict(name="config1", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=1, s
 CFG2 = dict(name="config2", S=16384, d=3072, H=1, E=128, K=8, de=1024, seed=2, score_func="softmax", zipf=True)
 CFG3 = dict(name="config3", S=8192, d=3072, H=1, E=128, K=8, de=1024, seed=3, score_func="softmax")
 CFG4 = dict(name="config4", S=256, d=3072, H=1, E=128, K=8, de=1024, seed=4, score_func="softmax", layers=4)
+# MAGI-2's production head split (configs/magi2_preview.json:40-88): 12 heads of 256, 256
+# experts per head, top-6 sigmoid, route_scale 4.9, expert FFN dim 1280.
+CFGP = dict(name="prod_head_split", S=16384, d=3072, H=12, E=256, K=6, de=1280, seed=5, score_func="sigmoid",
+            route_scale=4.9)
+CONFIGS = {"1": CFG1, "2": CFG2, "4": CFG4, "prod": CFGP}
 METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling"
 # libmhmoe kernels per step.  1 GPU: fused router, sort x4, tile tables, pad map, fused token
 # quantise + row grouping, gate/up GEMM, down GEMM, combine (atomic scatter: output zeroing
@@ -57,7 +62,7 @@ METRIC = "MoE-layer tokens/s/GPU; NVFP4 tensor-pipe util %; 1/2/4/8 B200 scaling
 # pad map, row grouping, gate/up GEMM, down GEMM, per-record combine, source-side combine.
 KERNELS_PER_STEP = 11
 KERNELS_PER_STEP_EP = 20
-CPU_SAMPLE_TOKENS = 512
+CPU_SAMPLE_TOKENS = 4096
 
 
 def load_peaks() -> dict:
@@ -212,6 +217,11 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, around the timed region"}
 
 
+def torch_device(world):
+    import torch
+    return torch.device("cuda", torch.cuda.current_device())
+
+
 def dist_setup():
     import torch
     import torch.distributed as dist
@@ -232,7 +242,8 @@ def make_layer(cfg, device, rank, ep_group=None):
     from flash_mh_moe.moe import CoreMultiHeadMoE, CoreMultiHeadMoEConfig, init_moe_params_
     mc = CoreMultiHeadMoEConfig(hidden_size=cfg["d"], num_heads=cfg["H"], num_experts=cfg["E"], top_k=cfg["K"],
                                 expert_intermediate_size=cfg["de"], num_layers=1, params_dtype=torch.bfloat16,
-                                score_func=cfg["score_func"], route_norm=True, route_scale=1.0)
+                                score_func=cfg["score_func"], route_norm=True,
+                                route_scale=cfg.get("route_scale", 1.0))
     if ep_group is None:
         m = CoreMultiHeadMoE(mc).to(device)
         init_moe_params_(m, seed=cfg["seed"], device=device)
@@ -295,7 +306,7 @@ def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
     from flash_mh_moe import _lib
-    cfg = {1: CFG1, 2: CFG2, 4: CFG4}[args.config] if world == 1 else CFG3
+    cfg = CONFIGS[args.config] if world == 1 else CFG3
     if args.tokens:
         cfg = dict(cfg, S=args.tokens)
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -399,7 +410,7 @@ def run_ours(args, world, rank, local):
                                    "ms_per_step": round(msg, 4),
                                    "note": "module forward captured once (flash_mh_moe.graph.CapturedForward)"}
             del g
-        if args.config == 1 and not args.tokens and not args.no_extras:
+        if args.config == "1" and not args.tokens and not args.no_extras:
             S3 = CFG3["S"]
             ms3 = _time_explicit(args, m, x, S3, deterministic=det)
             out["weak_scaling_base"] = {
@@ -485,49 +496,103 @@ def _e2e(args, m, x_host, dev, world):
     return out[0], out[1]
 
 
+def _workload(cfg, world):
+    H = cfg["H"]
+    head = f"d={cfg['d']} (H=1)" if H == 1 else f"d={cfg['d']} as H={H} heads of {cfg['d'] // H}"
+    exp = f"E={cfg['E']}" + ("" if H == 1 else " per head")
+    rs = cfg.get("route_scale", 1.0)
+    route = f"top-{cfg['K']} {cfg['score_func']}" + (f" x{rs}" if rs != 1.0 else "")
+    if world > 1:
+        return (f"config3: {cfg['S']} tokens/GPU, {head}, {exp} sharded {cfg['E'] * H // world}/GPU, {route}, "
+                f"SwiGLU7 de={cfg['de']}")
+    return (f"{cfg['name']}: S={cfg['S']} tokens, {head}, {exp}, {route}, SwiGLU7 de={cfg['de']}"
+            + (", Zipf logit bias 2*ln((e+1)^-1.2)" if cfg.get("zipf") else ""))
+
+
+def fp4_library_ceiling(dev, M, N, K, iters=10):
+    """The measured FP4 ceiling: a library NVFP4 GEMM (cuBLASLt through torch._scaled_mm:
+    E2M1 operands, E4M3 scales per 16 along K) of the gate/up GEMM's dense-equivalent shape
+    M x N x K, median of `iters` launches after warm-up, in TFLOP/s; None when the library
+    call is unavailable."""
+    import torch
+    try:
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randint(0, 256, (M, K // 2), dtype=torch.uint8, device=dev, generator=g).view(torch.float4_e2m1fn_x2)
+        b = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g).view(torch.float4_e2m1fn_x2)
+        rup = lambda v, m: (v + m - 1) // m * m
+        sa = torch.full((rup(M, 128) * rup(K // 16, 4),), 1.0, device=dev).to(torch.float8_e4m3fn)
+        sb = torch.full((rup(N, 128) * rup(K // 16, 4),), 1.0, device=dev).to(torch.float8_e4m3fn)
+        for _ in range(3):
+            torch._scaled_mm(a, b.t(), sa, sb, out_dtype=torch.bfloat16)
+        ts = []
+        for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b.t(), sa, sb, out_dtype=torch.bfloat16)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        del a, b, sa, sb
+        torch.cuda.empty_cache()
+        return {"tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1), "ms": round(ms, 4), "shape_mnk": [M, N, K],
+                "what": "cuBLASLt NVFP4 dense GEMM (torch._scaled_mm, e2m1 x e4m3/16 -> bf16), median of "
+                        f"{iters} launches in this run"}
+    except Exception as e:  # pragma: no cover - depends on the installed torch / cuBLASLt
+        return {"tflops": None, "unavailable": repr(e)[:200]}
+
+
 def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
-    S, d, de, K = cfg["S"], cfg["d"], cfg["de"], cfg["K"]
-    R = S * K * cfg["H"]
+    S, d, de, K, H = cfg["S"], cfg["d"], cfg["de"], cfg["K"], cfg["H"]
+    dh = d // H
+    R = S * K * H
     if world > 1:
         from flash_mh_moe.ep import LAST_STATS
         R_gemm = int(LAST_STATS["rows_received"].item()) if "rows_received" in LAST_STATS else R  # expert-GEMM rows
     else:
         R_gemm = R
-    flop_gate_up = 2.0 * R_gemm * (d // cfg["H"]) * (2 * de)
-    flop_total = 6.0 * R * (d // cfg["H"]) * de
+    flop_gate_up = 2.0 * R_gemm * dh * (2 * de)
+    flop_total = 6.0 * R * dh * de
     peaks = load_peaks()
-    fp4_peak = 4.0 * peaks["bf16_tflops_sustained"]
+    fp4_peak = 4.0 * peaks["bf16_tflops"]
     achieved = flop_gate_up / (stages["gemm_gate_up_ms"] * 1e-3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "gemm_gate_up_config1_traffic.json"
-    if tf.exists():
+    if tf.exists() and cfg["name"] == "config1" and world == 1:
         traffic = json.loads(tf.read_text()).get("bytes_per_launch")
     layer_tflops = flop_total / (ms_step * 1e-3) / 1e12
     value = world * S / (ms_step * 1e-3)
+    lib = None
+    if not args.no_extras:
+        lib = fp4_library_ceiling(torch_device(world), R_gemm, 2 * de, dh)
+    roof = {"kernel": "ffn_gemm_nvfp4_kernel<EPI_SWIGLU> (gate/up GEMM)", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": round(fp4_peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / fp4_peak, 4), "traffic": traffic,
+            "peak_note": f"4 x {peaks['source']} bf16 burst {peaks['bf16_tflops']} TFLOP/s (dense FP4 = 4x bf16 "
+                         f"on B200; the kernel is timed inside a ~1 ms step); datasheet dense FP4 9000 TFLOP/s -> "
+                         f"frac {achieved / 9000.0:.4f}",
+            "algorithmic_flop_per_launch": flop_gate_up,
+            "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch at config 1 "
+                            "(profiles/gemm_gate_up_config1_traffic.json)" if traffic else None}
+    if lib is not None:
+        roof["library_fp4_ceiling"] = dict(lib, frac=round(achieved / lib["tflops"], 4) if lib.get("tflops") else None)
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "nvfp4 (e2m1 x ue4m3/16, fp32 accumulate; bf16 in/out)",
-        "data": "synthetic (seeded, config-1 distributions)",
-        "config": {"workload": (f"{cfg['name']}: S={S} tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024"
-                                + (", Zipf logit bias 2*ln((e+1)^-1.2)" if cfg.get("zipf") else "")
-                                if world == 1 else
-                                f"config3: {S} tokens/GPU, d=3072 (H=1), E=128 sharded {cfg['E'] // world}/GPU, "
-                                "top-8 softmax, SwiGLU7 de=1024"),
+        "data": f"synthetic (seeded, {cfg['name']} distributions)",
+        "config": {"workload": _workload(cfg, world),
                    "tokens_per_gpu": S, "global_batch": world * S,
                    "parallelism": f"ep{world} (token->expert all-to-all, NCCL)" if world > 1 else "1 GPU",
-                   "l2": "inputs larger than L2 (0.68 GB NVFP4 weights + 0.1 GB x per step)"},
+                   "l2": "inputs larger than L2 (NVFP4 weights of every expert + x streamed every step)"},
         "tokens_per_s_per_gpu": round(value / world, 1),
         "layer_tflops": round(layer_tflops, 1),
-        "nvfp4_util_pct": {"vs_4x_measured_bf16_sustained": round(100 * layer_tflops / fp4_peak, 2),
-                           "vs_datasheet_9pf": round(100 * layer_tflops / 9000.0, 2)},
+        "nvfp4_util_pct": {"vs_4x_measured_bf16_burst": round(100 * layer_tflops / fp4_peak, 2),
+                           "vs_datasheet_9pf": round(100 * layer_tflops / 9000.0, 2),
+                           "vs_library_fp4_ceiling": (round(100 * layer_tflops / lib["tflops"], 2)
+                                                      if lib and lib.get("tflops") else None)},
         "stages_ms": {k: round(v, 4) for k, v in stages.items()},
-        "roofline": {"kernel": "ffn_gemm_nvfp4_kernel<EPI_SWIGLU> (gate/up GEMM)", "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": round(fp4_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp4_peak, 4), "traffic": traffic,
-                     "peak_note": f"4 x {peaks['source']} bf16 sustained (FP4 dense = 4x bf16); "
-                                  f"datasheet dense FP4 9000 TFLOP/s -> frac {achieved / 9000.0:.4f}",
-                     "algorithmic_flop_per_launch": flop_gate_up},
+        "roofline": roof,
         "e2e": None if e2e_ms[0] != e2e_ms[0] else {
             "value": round(world * S / (e2e_ms[0] * 1e-3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": S * d * 2, "d2h_bytes_per_step": S * d * 2, "ms_per_step": round(e2e_ms[0], 4),
@@ -571,8 +636,8 @@ def _report(args, cfg, world, ms_step, stages, e2e_ms, clk, m, x_host):
                                      "plus the wait for every source (a2a_records_ms), and remote bytes of the "
                                      "fused combine-and-return kernel over its time (local_combine_ms, which "
                                      "also reads the partial rows); peak = measured peer copy"}
-    if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == 1:
-        out["cpu_baseline"] = cpu_baseline(m, x_host, reps=2)
+    if world == 1 and not args.no_cpu_baseline and not args.release_master and args.config == "1":
+        out["cpu_baseline"] = cpu_baseline(m, x_host, cfg, reps=2)
     return out
 
 
@@ -644,52 +709,106 @@ def run_stack(args, cfg, dev):
             "gpu_launches": KERNELS_PER_STEP * cfg["layers"] * args.steps, "clocks": clk.summary()}
 
 
-# ───────────────────────────── CPU reference path (oracle port) ─────────────────────────────
+# ───────────────────────────── CPU reference path ─────────────────────────────
+# The reference's own layer path on the host cores: its route.py top-k and global sort and
+# its _scatter_back run unchanged from the staged copy under oracle/_ref (oracle/stage_ref.py),
+# with the Triton expert kernel restated in torch (oracle/ffn_torch_ref.py; the reference
+# has no CPU version of it).  Without the staged copy the oracle's restatement of route.py
+# stands in.  torch uses every host thread.
 
-def _host_weights(m):
-    import numpy as np
+def _cpu_threads() -> int:
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def _staged_ref():
+    try:
+        from oracle.stage_ref import import_ref
+        return import_ref()
+    except ImportError:
+        return None
+
+
+def _host_layer(m, x_host, n_tokens):
     import torch
     with torch.no_grad():
-        Wg = m.W_gate.detach().float().cpu().numpy()
-        Wu = m.W_up.detach().float().cpu().numpy()
-        Wd = m.W_down.detach().float().cpu().numpy()
-        gate = m.gate.detach().float().cpu().numpy()
-    return gate, Wg, Wu, Wd
+        w = tuple(t.detach().to("cpu", torch.bfloat16) for t in (m.W_gate, m.W_up, m.W_down))
+        gate = m.gate.detach().float().cpu()
+        bias = m.router.expert_bias.detach().float().cpu()
+    x = x_host[:n_tokens].view(n_tokens, m.num_heads, m.d_head).contiguous()
+    return x, gate, w, bias
 
 
-def cpu_layer_sample(gate, Wg, Wu, Wd, x_np, cfg):
-    """Reference CPU path on x_np [n, d]: fp32 einsum router, route.py top-k + sort, bf16 FFN."""
-    from oracle import ffn_ref, route_ref
-    n = x_np.shape[0]
-    H, E = cfg["H"], cfg["E"]
-    xh = x_np.reshape(n, H, -1)
-    logits = route_ref.router_logits(xh, gate, E)
-    p, i = route_ref.compute_topk_probs_and_indices(logits, cfg["K"], cfg["score_func"])
-    g, ps, o = route_ref.flash_mh_moe_global_sort(p, i, E)
-    return ffn_ref.mh_moe_fwd_ref(xh, g, ps, o, Wg, Wu, Wd, dtype="bf16", round_weights=False)
+def cpu_layer(m, host, cfg, ref):
+    from oracle import ffn_torch_ref
+    x, gate, (Wg, Wu, Wd), bias = host
+    return ffn_torch_ref.moe_layer_cpu(x, gate, Wg, Wu, Wd, cfg["E"], cfg["K"], cfg["score_func"],
+                                       cfg.get("route_scale", 1.0), bias, ref=ref)
 
 
-def _cores():
-    try:
-        from threadpoolctl import threadpool_info
-        n = max((d.get("num_threads", 0) for d in threadpool_info()), default=0)
-        return int(n) or os.cpu_count()
-    except Exception:
-        return os.cpu_count()
+def _cpu_sample_note(cfg, n, ref, extra=""):
+    return (f"first {n} tokens of the {cfg['name']} batch through the whole layer (router einsum, top-k, sort, all "
+            f"{cfg['E'] * cfg['H']} experts' bf16 FFN, scatter)" + extra + "; "
+            + ("reference route.py + _scatter_back (staged oracle/_ref) with the expert kernel restated in torch"
+               if ref is not None else "oracle restatement of route.py with the expert kernel restated in torch"))
 
 
-def cpu_baseline(m, x_host, reps=2, host=None):
-    host = host or _host_weights(m)
-    x_np = x_host[:CPU_SAMPLE_TOKENS].float().numpy()
+def cpu_baseline(m, x_host, cfg, reps=2):
+    cores = _cpu_threads()
+    ref = _staged_ref()
+    n = min(CPU_SAMPLE_TOKENS, cfg["S"])
+    host = _host_layer(m, x_host, n)
     times = []
     for _ in range(reps + 1):
         t = time.perf_counter()
-        cpu_layer_sample(*host, x_np, CFG1)
+        cpu_layer(m, host, cfg, ref)
         times.append(time.perf_counter() - t)
-    best = min(times[1:]) if len(times) > 1 else times[0]
-    return {"value": round(CPU_SAMPLE_TOKENS / best, 1), "unit": "tokens/s", "cores": _cores(), "kind": "port",
-            "sample": f"first {CPU_SAMPLE_TOKENS} tokens of the config-1 batch through the full layer "
-                      f"(all 128 experts' bf16 weights), best of {reps} after 1 warm-up; numpy/BLAS threads"}
+    best = min(times[1:])
+    return {"value": round(n / best, 1), "unit": "tokens/s", "cores": cores, "kind": "reference" if ref else "port",
+            "sample": _cpu_sample_note(cfg, n, ref, f", best of {reps} after 1 warm-up")}
+
+
+def _triton_reference_gpu(ref, dev):
+    """The reference's own Triton expert kernel (mh_moe_fwd_func) on this GPU, at the shapes
+    it is written for: MAGI-2's production head split and BASELINE config 0.  Triton
+    rejects a kernel whose tensor-memory need exceeds the SM's 512 columns before launching
+    it; that refusal is reported as is."""
+    import torch
+    from ref_flash_mh_moe.triton.mh_moe_fwd import mh_moe_fwd_func
+    out = {}
+    for name, (S, H, dh, E, K, de, score, scale) in {
+            "prod_head_split": (16384, 12, 256, 256, 6, 1280, "sigmoid", 4.9),
+            "config0": (512, 1, 1024, 8, 2, 2048, "softmax", 1.0)}.items():
+        g = torch.Generator(device=dev).manual_seed(0)
+        try:
+            x = torch.randn(S, H, dh, device=dev, generator=g).to(torch.bfloat16)
+            W = [(torch.randn(H * E, a, b, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+                 for a, b in ((dh, de), (dh, de), (de, dh))]
+            gate = (torch.randn(H, E, dh, device=dev, generator=g) * 0.02).float()
+
+            def layer():
+                logits = torch.einsum("shd,hed->hse", x.float(), gate)
+                p, i = ref.compute_topk_probs_and_indices(logits, K, score_func=score)
+                gi, ps, of = ref.flash_mh_moe_global_sort(p * scale, i, E)
+                return mh_moe_fwd_func(x, gi, ps, of, *W, deterministic=False)
+            layer()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                layer()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 5
+            out[name] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(S / (ms * 1e-3), 1)}
+        except Exception as e:
+            out[name] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+        finally:
+            x = W = gate = None
+            torch.cuda.empty_cache()
+    return out
 
 
 def run_reference(args, world, rank):
@@ -697,27 +816,33 @@ def run_reference(args, world, rank):
     if rank != 0:
         return None
     cfg = CFG1
-    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
-    m, x_host = make_layer(cfg, dev, 0) if dev.type == "cuda" else (None, None)
-    host = _host_weights(m)
-    x_np = x_host[:CPU_SAMPLE_TOKENS].float().numpy()
+    dev = torch.device("cuda", 0)
+    cores = _cpu_threads()
+    ref = _staged_ref()
+    m, x_host = make_layer(cfg, dev, 0)
+    n = CPU_SAMPLE_TOKENS
+    host = _host_layer(m, x_host, n)
+    del m
+    torch.cuda.empty_cache()
     for _ in range(args.warmup):
-        cpu_layer_sample(*host, x_np, cfg)
+        cpu_layer(None, host, cfg, ref)
     t = time.perf_counter()
     for _ in range(args.steps):
-        cpu_layer_sample(*host, x_np, cfg)
+        cpu_layer(None, host, cfg, ref)
     dt = (time.perf_counter() - t) / args.steps
-    v = CPU_SAMPLE_TOKENS / dt
-    return {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
-            "data": "synthetic (seeded, config-1 distributions)",
-            "config": {"workload": "config1: S=16384 tokens, d=3072 (H=1), E=128, top-8 softmax, SwiGLU7 de=1024",
-                       "sample_tokens_per_step": CPU_SAMPLE_TOKENS, "parallelism": "host CPU"},
-            "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": _cores(), "kind": "port",
-                             "sample": f"{CPU_SAMPLE_TOKENS} tokens of the config-1 batch per step"},
-            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "gpu_launches": 0}
+    v = n / dt
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "tokens/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
+           "data": "synthetic (seeded, config1 distributions)",
+           "config": {"workload": _workload(cfg, 1), "sample_tokens_per_step": n, "parallelism": "host CPU"},
+           "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": cores,
+                            "kind": "reference" if ref else "port", "sample": _cpu_sample_note(cfg, n, ref)},
+           "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "gpu_launches": 0}
+    if ref is not None and not args.no_extras:
+        out["triton_reference_gpu"] = _triton_reference_gpu(ref, dev)
+    return out
 
 
 def main():
@@ -730,8 +855,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the other-scatter and 8192-token timings (profiling runs)")
-    ap.add_argument("--config", type=int, choices=[1, 2, 4], default=1,
-                    help="BASELINE config at N=1 (1: headline; 2: Zipf-skewed routing; 4: 4-layer small batch)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="1",
+                    help="BASELINE config at N=1 (1: headline; 2: Zipf-skewed routing; 4: 4-layer small batch; "
+                         "prod: MAGI-2's production head split)")
     ap.add_argument("--release-master", action="store_true",
                     help="free the bf16 expert weights after NVFP4 packing (profiler captures)")
     ap.add_argument("--tokens", type=int, default=None,

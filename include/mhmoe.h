@@ -5,9 +5,11 @@
  * (router top-k, global sort, fused expert FFN) plus the expert-parallel
  * dispatch/combine.  Every entry point takes raw device pointers, shapes and a
  * cudaStream_t (passed as void*), enqueues work on that stream and returns an
- * mhmoe_status.  Nothing here allocates device memory: callers own every
- * buffer, including the scratch buffers whose sizes the *_bytes queries give.
- * No entry point synchronises the stream.
+ * mhmoe_status.  The compute entry points allocate no device memory: callers own
+ * every buffer, including the scratch buffers whose sizes the *_bytes queries give.
+ * The one exception is mhmoe_ep_sym_alloc, the set-up call that allocates (and
+ * exports for CUDA IPC) an expert-parallel exchange buffer; mhmoe_ep_sym_free
+ * releases it.  No compute entry point synchronises the stream.
  *
  * Kernels that wait on on-chip barriers give up after `timeout_ns` (0 selects
  * the default of 2 s) and record MHMOE_ERR_TIMEOUT in the optional device word
@@ -121,8 +123,10 @@ MHMOE_API int mhmoe_global_sort(const float* topk_probs, const int64_t* topk_idx
  * ~1.05 MB array inside the library, held by every GPU that loads it; limits:
  * H*S*K <= 262144 routed rows and H*E <= 1024 experts, else MHMOE_ERR_CAPACITY with
  * nothing launched.  The first call on a device (with it current) resolves the
- * array's device address; make that call before any stream capture.  All calls share
- * the array: calls that overlap on the GPU race, so order them. */
+ * array's device address; make that call before any stream capture.  The address is
+ * cached per device for the life of the process: do not use this entry point across a
+ * device reset (cudaDeviceReset) of that device.  All calls share the array: calls that
+ * overlap on the GPU race, so order them. */
 MHMOE_API int mhmoe_global_sort_noalloc(const float* topk_probs, const int64_t* topk_idx, int H, int S, int K, int E,
                                         int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,
                                         int32_t* row_of_flat, int* dev_status, void* stream);
@@ -146,7 +150,7 @@ MHMOE_API int mhmoe_pack_weights_nvfp4(int kind, const void* w0, const void* w1,
                              uint8_t* data, uint8_t* sf, float* gscale, float* amax_scratch, void* stream);
 
 /* Fused expert FFN on NVFP4 operands.  Replaces flash_mh_moe_fwd / mh_moe_fwd_func
- * (inference/flash_mh_moe/fwd.py:16-40, triton/mh_moe_fwd.py:271-373): gather ->
+ * (inference/flash_mh_moe/fwd.py:16-40, triton/mh_moe_fwd.py:231-331): gather ->
  * x quantise (per row) -> grouped GEMM gate/up + SwiGLU7 + hidden quantise ->
  * grouped GEMM down x prob -> deterministic combine into y [S,H,dh] bf16.
  * R = number of routed rows, n_experts = H*E (flattened).  dh % 256 == 0,
@@ -166,7 +170,7 @@ MHMOE_API int mhmoe_ffn_nvfp4(const void* x, int64_t x_stride_s, int64_t x_strid
 
 /* mhmoe_ffn_nvfp4 with the reference's default (non-deterministic) scatter: the down
  * GEMM adds each routed row's bf16(y_acc * prob) into y with bf16 atomics
- * (_mh_moe_fwd_kernel with deterministic=False, triton/mh_moe_fwd.py:213-221, selected
+ * (_mh_moe_fwd_kernel with deterministic=False, triton/mh_moe_fwd.py:172-181, selected
  * when MAGI2_DETERMINISTIC is not "1", fwd.py:12-13).  y is zeroed first; no partial
  * buffer and no combine pass.  Results may differ run to run in the last bf16 bits. */
 MHMOE_API int mhmoe_ffn_nvfp4_atomic(const void* x, int64_t x_stride_s, int64_t x_stride_h, int S, int H, int dh,
@@ -204,7 +208,7 @@ MHMOE_API int mhmoe_quant_tokens(const void* x, int64_t x_stride_s, int64_t x_st
 /* Deterministic combine: y[s,h,:] = bf16(sum, in ascending row id, of P[map(r), :] over
  * the rows r of key h*S + s), rows from tok_rows/tok_offsets (or k_fixed rows per key);
  * map = pad_of_row when given, else identity.  Replaces the scatter of the reference
- * FFN (triton/mh_moe_fwd.py:213-221, :229-255) and, in expert parallelism, the head
+ * FFN (triton/mh_moe_fwd.py:172-181, :189-215) and, in expert parallelism, the head
  * un-dispatch (magi2_preview.py:3303-3327). */
 MHMOE_API int mhmoe_combine(const void* P, int64_t P_rows, const int32_t* pad_of_row, int dh, int S, int H,
                             const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R, void* y,

@@ -203,7 +203,7 @@ static int ffn_entry(const void* x, int64_t x_stride_s, int64_t x_stride_h, int 
   MHMOE_CHECK_ARCH();
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (S == 0) return MHMOE_OK;
-  if (R == 0) {   // no routed rows: y = 0 (reference: mh_moe_fwd.py:297-298)
+  if (R == 0) {   // no routed rows: y = 0 (reference: mh_moe_fwd.py:257-258)
     cudaError_t e;
     if (y_stride_h == dh && y_stride_s == (int64_t)H * dh) {
       e = cudaMemsetAsync(y, 0, sizeof(__nv_bfloat16) * (size_t)S * H * dh, st);

@@ -2,8 +2,8 @@
 // routed rows r, in ascending r, of P[r, :] ) with fp32 accumulation.
 //
 // Replaces the scatter of the reference FFN: the bf16 atomic_add of
-// _mh_moe_fwd_kernel (inference/flash_mh_moe/triton/mh_moe_fwd.py:213-221) and the
-// deterministic _scatter_back (:229-255).  P already holds bf16(y_acc * prob) per
+// _mh_moe_fwd_kernel (inference/flash_mh_moe/triton/mh_moe_fwd.py:172-181) and the
+// deterministic _scatter_back (:189-215).  P already holds bf16(y_acc * prob) per
 // sorted row, exactly the values the reference scatters; the sum is taken in fp32
 // in a fixed order, so the result is run-to-run identical.
 #include <cstdlib>

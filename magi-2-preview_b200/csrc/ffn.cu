@@ -55,10 +55,17 @@ cudaError_t encode_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner
 }
 
 int num_sms() {
-  int dev = 0, n = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  static int n_sms[MHMOE_MAX_DEVICES] = {};
+  static PerDeviceOnce once;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MHMOE_MAX_DEVICES) return 148;
+  once.run([](int d) {
+    int n = 0;
+    const cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    n_sms[d] = (e == cudaSuccess && n > 0) ? n : 148;
+    return e;
+  });
+  return n_sms[dev];
 }
 
 // SF atom array of `bytes` bytes as [bytes/256, 256] u8 rows, box 256 x 8 (one 2 KB m/n-tile stage).
@@ -78,23 +85,26 @@ template <int EPI>
 static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                                     const CUtensorMap& tsfa, const CUtensorMap& tsfb, const FfnGemmParams& p,
                                     int64_t max_work, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  static int max_clusters = 0;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(ffn_gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    gemmp_smem_bytes(EPI));
-    if (attr_err != cudaSuccess) return;
+  // per device: the shared-memory attribute and the cluster occupancy of its context
+  static PerDeviceOnce once;
+  static int max_clusters[MHMOE_MAX_DEVICES] = {};
+  const cudaError_t attr_err = once.run([](int dev) {
+    cudaError_t e = cudaFuncSetAttribute(ffn_gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemmp_smem_bytes(EPI));
+    if (e != cudaSuccess) return e;
     // the kernel's cluster shape (2, 1, 1) is compiled in, so the query config names none
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (num_sms() / 2));
     cfg.blockDim = dim3(GEMMP_THREADS);
     cfg.dynamicSmemBytes = gemmp_smem_bytes(EPI);
-    attr_err = cudaOccupancyMaxActiveClusters(&max_clusters, ffn_gemm_pair_kernel<EPI>, &cfg);
-    if (attr_err == cudaSuccess && max_clusters <= 0) attr_err = cudaErrorInvalidConfiguration;
+    e = cudaOccupancyMaxActiveClusters(&max_clusters[dev], ffn_gemm_pair_kernel<EPI>, &cfg);
+    if (e == cudaSuccess && max_clusters[dev] <= 0) e = cudaErrorInvalidConfiguration;
+    return e;
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(max_clusters, max_work));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int clusters = (int)std::max<int64_t>(1, std::min<int64_t>(max_clusters[dev], max_work));
   ffn_gemm_pair_kernel<EPI><<<2 * clusters, GEMMP_THREADS, gemmp_smem_bytes(EPI), st>>>(ta, tb, tc, tsfa, tsfb, p);
   return cudaGetLastError();
 }
@@ -102,11 +112,10 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
 template <int EPI>
 static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                                const FfnGemmParams& p, int64_t max_work, cudaStream_t st) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(ffn_gemm_nvfp4_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    gemm_smem_bytes(EPI));
+  static PerDeviceOnce once;
+  const cudaError_t attr_err = once.run([](int) {
+    return cudaFuncSetAttribute(ffn_gemm_nvfp4_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                gemm_smem_bytes(EPI));
   });
   if (attr_err != cudaSuccess) return attr_err;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), max_work));

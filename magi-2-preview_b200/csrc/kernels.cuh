@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 #include <string>
 
 #include "mhmoe_common.cuh"
@@ -38,6 +39,31 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 inline int64_t mtiles_upper_bound(int64_t R, int64_t n_experts, int align = 1) {
   return (R + 127) / 128 + (int64_t)align * n_experts;
 }
+
+// Set-up that belongs to one device's context (kernel attributes such as the dynamic
+// shared-memory limit, occupancy queries): run(f) calls f(device) the first time it runs
+// with that device current and returns the recorded result on every later call there.
+// A process that drives several GPUs (one host thread per device, or one thread switching
+// devices) gets the set-up on each of them.
+constexpr int MHMOE_MAX_DEVICES = 64;
+struct PerDeviceOnce {
+  std::mutex mu;
+  bool done[MHMOE_MAX_DEVICES] = {};
+  cudaError_t err[MHMOE_MAX_DEVICES] = {};
+  template <class F>
+  cudaError_t run(F&& f) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= MHMOE_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+      err[dev] = f(dev);
+      done[dev] = true;
+    }
+    return err[dev];
+  }
+};
 
 // ───────── expert-parallel peer buffers (ep_p2p.cu, combine.cu) ─────────
 // Every rank allocates one buffer with this layout and maps every peer's (CUDA IPC):

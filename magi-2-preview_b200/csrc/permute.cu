@@ -2,7 +2,7 @@
 // offsets, 128-row tile tables, and the inverse (token -> rows) map.
 //
 // Replaces flash_mh_moe_global_sort (inference/flash_mh_moe/route.py:209-253) and the
-// tile-count prep of mh_moe_fwd_func (inference/flash_mh_moe/triton/mh_moe_fwd.py:315-322).
+// tile-count prep of mh_moe_fwd_func (inference/flash_mh_moe/triton/mh_moe_fwd.py:275-282).
 //
 // Stable sort = argsort(stable=True) over the flat (h, s, k) order:
 //   1. chunk histograms   hist[c][g]  (one CTA per chunk, shared-memory counters)
@@ -439,8 +439,10 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
   int* tile_row0 = tile_expert + mt;
   int* tile_rows = tile_row0 + mt;
   if (R <= SORT_SMALL_MAX && HE <= SORT_SMALL_MAX_KEYS) {
-    static cudaError_t attr = cudaFuncSetAttribute(sort_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   SORT_SMALL_SMEM);
+    static PerDeviceOnce once;
+    const cudaError_t attr = once.run([](int) {
+      return cudaFuncSetAttribute(sort_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SORT_SMALL_SMEM);
+    });
     if (attr != cudaSuccess) return attr;
     MHMOE_LAUNCH_PDL(sort_small_kernel, 1, 1024, SORT_SMALL_SMEM, st, idx, probs, (int)R, S, K, E, HE, expert_offsets,
                      gather_ids, probs_sorted, row_of_flat, status);

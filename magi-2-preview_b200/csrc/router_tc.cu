@@ -410,12 +410,12 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   const int smem = p.stages * stage_bytes + fixed;
   // top-K lists of 8 entries cover K <= 8; 16 entries otherwise (K <= 16)
   auto kernel = K <= 8 ? router_tc_kernel<8> : router_tc_kernel<16>;
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(router_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(router_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  static PerDeviceOnce once;
+  const cudaError_t attr = once.run([](int) {
+    cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(router_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    return e;
   });
   if (attr != cudaSuccess) {
     *cerr = attr;

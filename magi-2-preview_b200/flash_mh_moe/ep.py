@@ -251,11 +251,17 @@ class PeerExchange:
         self.group, self.device, self.cap, self.dh, self.K = group, device, int(cap), int(dh), int(K)
         self.n = dist.get_world_size(group)
         self.me = dist.get_rank(group)
-        ident = (socket.gethostname(), str(torch.cuda.get_device_properties(device).uuid))
+        ident = (socket.gethostname(), str(torch.cuda.get_device_properties(device).uuid), self.cap)
         idents = [None] * self.n
         dist.all_gather_object(idents, ident, group=group)
-        if len({h for h, _ in idents}) != 1 or len({u for _, u in idents}) != self.n:
+        if len({i[0] for i in idents}) != 1 or len({i[1] for i in idents}) != self.n:
             raise RuntimeError("peer-memory EP needs every rank on its own GPU of one node")
+        if len({i[2] for i in idents}) != 1:
+            # every rank must pass the same number of (head, token) rows, as the reference's
+            # equal-split all-to-all (magi2_preview.py:3277-3299) requires; checked here, at
+            # the collective, so that all ranks raise together
+            raise ValueError(f"expert-parallel ranks passed different token counts {[i[2] for i in idents]}; "
+                             "every rank of the EP group must pass the same S")
         size = int(L.mhmoe_ep_sym_bytes(self.n, self.cap, dh, K))
         ptr = C.c_void_p()
         handle = (C.c_ubyte * 64)()
@@ -284,8 +290,11 @@ class PeerExchange:
 
     @classmethod
     def get(cls, group, device: torch.device, cap: int, dh: int, K: int, slot: int = 0) -> "PeerExchange":
-        """The group's exchange on this device (one per pipeline slot), re-created
-        (collectively: every rank passes the same ``cap``) when a larger capacity is needed."""
+        """The group's exchange on this device (one per pipeline slot), re-created when a
+        larger capacity is needed.  Creation is collective and checks that every rank asks
+        for the same ``cap`` (ranks passing different token counts raise together there);
+        a later call passes without any collective when its ``cap`` fits, so every rank of
+        the group must keep passing the same token count per call."""
         key = (id(group), device.index, int(dh), int(K), int(slot))
         px = cls._cache.get(key)
         if px is None or px.cap < cap:

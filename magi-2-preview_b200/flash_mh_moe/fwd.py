@@ -1,7 +1,7 @@
 """Expert FFN forward — same call signature as the reference's ``inference/flash_mh_moe/fwd.py``.
 
 ``flash_mh_moe_fwd(x, gather_ids, probs, expert_offsets, W_gate, W_up, W_down)``
-(reference ``fwd.py:16-40`` -> ``triton/mh_moe_fwd.py:271-373``): gather ->
+(reference ``fwd.py:16-40`` -> ``triton/mh_moe_fwd.py:231-331``): gather ->
 gate/up GEMM -> SwiGLU7 -> down GEMM -> weighted scatter, here as the NVFP4 B200 path:
 
     per-row NVFP4 quantise of the gathered x  ->  tcgen05 block-scaled grouped GEMM

@@ -59,6 +59,21 @@ _magi2_moe_registry: "weakref.WeakValueDictionary[int, CoreMultiHeadMoE]" = weak
 _magi2_moe_keys = itertools.count()
 
 
+def _psm_ep() -> tuple[int, int, object]:
+    """(ep_size, ep_rank, ep_group) from MAGI-2's process-group manager, read the way the
+    reference module reads it (``psm.get_world_size("ep")`` at construction,
+    ``psm.get_parallel_group("ep")`` at forward: magi2_preview.py:2509, 2632-2637;
+    psm.py:94-128), when ``inference.infra.distributed`` is importable; otherwise one rank."""
+    try:
+        from inference.infra.distributed import psm
+    except ImportError:
+        return 1, 0, None
+    size = int(psm.get_world_size("ep"))
+    if size <= 1:
+        return 1, 0, None
+    return size, int(psm.get_local_rank("ep")), psm.get_parallel_group("ep")
+
+
 class CoreMultiHeadMoE(nn.Module):
     def __init__(self, config: CoreMultiHeadMoEConfig, ep_group=None) -> None:
         super().__init__()
@@ -73,9 +88,13 @@ class CoreMultiHeadMoE(nn.Module):
         self.d_head = config.hidden_size // config.num_heads
         self.d_expert = config.expert_intermediate_size
         self.flatten_num_experts = self.num_heads * self.num_experts
+        if ep_group is not None:
+            self.ep_size = torch.distributed.get_world_size(ep_group)
+            self.ep_rank = torch.distributed.get_rank(ep_group)
+        else:
+            # as the reference: the expert-parallel group comes from the process-group manager
+            self.ep_size, self.ep_rank, ep_group = _psm_ep()
         self.ep_group = ep_group
-        self.ep_size = torch.distributed.get_world_size(ep_group) if ep_group is not None else 1
-        self.ep_rank = torch.distributed.get_rank(ep_group) if ep_group is not None else 0
         if self.flatten_num_experts % self.ep_size != 0:
             raise ValueError(f"H*E ({self.flatten_num_experts}) must be divisible by ep_size ({self.ep_size})")
         # token -> expert EP: this rank owns flattened experts [expert_lo, expert_lo + local)
@@ -112,10 +131,18 @@ class CoreMultiHeadMoE(nn.Module):
             self._packed_key = key
         return self._packed
 
+    _MASTERS = ("W_gate", "W_up", "W_down")
+
+    def _master_shapes(self) -> dict[str, tuple[int, int, int]]:
+        nl, dh, de = self.local_flatten_num_experts, self.d_head, self.d_expert
+        return {"W_gate": (nl, dh, de), "W_up": (nl, dh, de), "W_down": (nl, de, dh)}
+
     def release_master_weights(self) -> None:
         """Pack (if needed), then free the params_dtype expert weights: inference only needs
         the NVFP4 operands (0.56 B/weight instead of 2).  The parameters stay registered
-        with zero elements; load a state dict again to restore them."""
+        with zero elements until a state dict holding all three of them is loaded: the load
+        gives them back their full shapes, copies the new values in, and the next forward
+        packs those."""
         self.packed_weights()
         with torch.no_grad():
             for p in (self.W_gate, self.W_up, self.W_down):
@@ -127,9 +154,27 @@ class CoreMultiHeadMoE(nn.Module):
         self._packed = (gu, dn)
         self._packed_key = self._weights_key()
 
-    def _load_from_state_dict(self, *args, **kwargs):
-        super()._load_from_state_dict(*args, **kwargs)
-        self._masters_released = False       # new masters: pack again at first use
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        restore = self._masters_released and all(prefix + n in state_dict for n in self._MASTERS)
+        if restore:
+            # released masters have zero elements: give them their shapes back so the load
+            # copies into them (a released module whose state dict lacks one of the three
+            # keeps serving its packed weights)
+            for n, shape in self._master_shapes().items():
+                p = getattr(self, n)
+                p.data = torch.empty(shape, dtype=p.dtype, device=p.device)
+        n_err = len(error_msgs)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+        if len(error_msgs) != n_err:
+            if restore:       # this module's load failed: back to the released state
+                for n in self._MASTERS:
+                    p = getattr(self, n)
+                    p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+            return
+        if restore or not self._masters_released:
+            self._masters_released = False    # new masters: pack again at first use
 
     def router_planes(self) -> tuple[torch.Tensor, int]:
         key = ((self.gate, self.gate.data_ptr(), self.gate._version),)
@@ -160,6 +205,8 @@ class CoreMultiHeadMoE(nn.Module):
     def _forward_impl(self, x: torch.Tensor) -> torch.Tensor:
         x_heads = x.view(-1, self.num_heads, self.d_head)
         if self.ep_size > 1:
+            if self.ep_group is None:
+                raise RuntimeError(f"MAGI-2 EP group is not initialized but ep_size={self.ep_size}")
             from .ep import ep_moe_forward
             out = ep_moe_forward(self, x_heads)
         else:

@@ -22,13 +22,13 @@ import numpy as np
 
 from . import nvfp4_ref as nv
 
-SWIGLU7_ALPHA = np.float32(1.702)   # mh_moe_fwd.py:59-61
+SWIGLU7_ALPHA = np.float32(1.702)   # mh_moe_fwd.py:18-20
 SWIGLU7_LIMIT = np.float32(7.0)
 SWIGLU7_BIAS = np.float32(1.0)
 
 
 def swiglu7(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
-    """mh_moe_fwd.py:64-70 in fp32."""
+    """mh_moe_fwd.py:24-30 in fp32."""
     g = np.minimum(np.asarray(gate, np.float32), SWIGLU7_LIMIT)
     u = np.clip(np.asarray(up, np.float32), -SWIGLU7_LIMIT, SWIGLU7_LIMIT)
     sig = (np.float32(1.0) / (np.float32(1.0) + np.exp(-(SWIGLU7_ALPHA * g)).astype(np.float32))).astype(np.float32)
@@ -36,7 +36,7 @@ def swiglu7(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
 
 
 def _row_meta(gather_ids, expert_offsets, num_heads):
-    """Per sorted row: global expert id and head id (mh_moe_fwd.py:133-137, :243-245)."""
+    """Per sorted row: global expert id and head id (mh_moe_fwd.py:93-97)."""
     offs = np.asarray(expert_offsets, np.int64)
     nflat = offs.size - 1
     counts = np.diff(offs)

@@ -12,7 +12,7 @@ Produces:
   (``route.py:209``) on seeded logits: softmax/sigmoid, expert_bias, virtual
   groups, route_norm off, a Zipf-skewed bias, the production head shape.
 * ``ffn_fp32.npz`` — the reference Triton kernel ``_mh_moe_fwd_kernel``
-  (``inference/flash_mh_moe/triton/mh_moe_fwd.py:90``) run under
+  (``inference/flash_mh_moe/triton/mh_moe_fwd.py:50-181``) run under
   ``TRITON_INTERPRET=1`` on fp32 tensors (the interpreter does not support bf16),
   atomic and deterministic variants.
 """
@@ -89,7 +89,7 @@ def make_route(route):
 def make_ffn(route):
     os.environ["TRITON_INTERPRET"] = "1"
     import torch
-    torch.cuda.get_device_capability = lambda *a, **k: (10, 0)    # mh_moe_fwd.py:265 on a CPU box
+    torch.cuda.get_device_capability = lambda *a, **k: (10, 0)    # mh_moe_fwd.py:225 on a CPU box
     from inference.flash_mh_moe.triton import mh_moe_fwd as mk  # type: ignore
     out = {}
     cases = [("small", 32, 2, 64, 4, 2, 64, 21), ("ragged", 40, 1, 128, 8, 3, 96, 22)]

@@ -226,3 +226,54 @@ def _roundtrip_worker(rank, world, port, q):
         q.put((rank, bool(torch.equal(x, y))))
     finally:
         dist.destroy_process_group()
+
+
+def _leave_worker(rank, world, port, q):
+    """Both ranks run one EP step; rank 1 then leaves (exits without a further collective,
+    as a crashed or departed rank does).  Rank 0's next EP step must fail with an error
+    within the process group's timeout instead of waiting for ever."""
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    sys.path[:0] = [str(root), str(root / "magi-2-preview_b200")]
+    from flash_mh_moe.ep import ep_moe_layer
+    gu, dn = _weights()
+    E_loc = H * E // world
+    gu_l, dn_l = ffn_ref.slice_packs(gu, dn, rank * E_loc, (rank + 1) * E_loc)
+    x, probs, idx = _problem(rank)
+    ep_moe_layer(x, probs, idx, E, gu_l, dn_l, dist.group.WORLD, backend=RefBackend())
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+    else:
+        t = time.time()
+        try:
+            ep_moe_layer(x, probs, idx, E, gu_l, dn_l, dist.group.WORLD, backend=RefBackend())
+            q.put((rank, "no error", time.time() - t))
+        except Exception as e:   # the collective reports the missing peer
+            q.put((rank, "error: " + type(e).__name__, time.time() - t))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_ep_peer_leaves_between_steps_raises():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leave_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict((r, (what, dt)) for r, what, dt in (q.get(timeout=240) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    what, dt = res[0]
+    assert what.startswith("error"), f"rank 0's step after rank 1 left: {what}"
+    assert dt < 60, f"rank 0 took {dt:.1f} s to notice the missing rank"

@@ -81,7 +81,7 @@ def test_ffn_deterministic_and_empty(scatter, monkeypatch):
         assert torch.equal(y1, y2)
     else:   # atomic order may differ run to run: bf16 rounding only
         assert rel_l2(to_np(y1), to_np(y2)) < 1e-2
-    # no routed rows -> zeros (reference mh_moe_fwd.py:297-298)
+    # no routed rows -> zeros (reference mh_moe_fwd.py:257-258)
     z = flash_mh_moe_fwd(args[0], torch.empty(0, dtype=torch.int32, device="cuda"),
                          torch.empty(0, device="cuda"), torch.zeros(E + 1, dtype=torch.int64, device="cuda"),
                          *args[4:])

@@ -146,3 +146,36 @@ def test_pack_roundtrip_close():
     d2 = nv.dequant_down(nv.pack_down(wd))
     for a, b in ((g2, wg), (u2, wu), (d2, wd)):
         assert ffn_ref.rel_l2(a, b) < 0.12
+
+
+# ───────────────────────── torch CPU path of the timed baseline ─────────────────────────
+
+@pytest.mark.parametrize("H,dh,de,E,K,score,scale", [(1, 256, 512, 8, 2, "softmax", 1.0),
+                                                     (3, 128, 256, 6, 3, "sigmoid", 4.9)])
+def test_torch_cpu_layer_matches_oracle(H, dh, de, E, K, score, scale):
+    """The CPU baseline's torch layer (oracle.ffn_torch_ref) equals the numpy restatement
+    pinned against the reference kernel: routing and sort exactly, output within bf16
+    rounding of the accumulation order.  With the reference package staged under
+    oracle/_ref its own route.py and _scatter_back run, and must give the same result."""
+    import torch
+
+    from oracle import ffn_torch_ref, stage_ref
+    from gpu_util import seeded_moe
+    S = 96
+    x, gate, Wg, Wu, Wd = seeded_moe(S, H, dh, de, E, K, seed=5)
+    xh = x.reshape(S, H, dh)
+    lg = route_ref.router_logits(xh, gate, E)
+    p, i = route_ref.compute_topk_probs_and_indices(lg, K, score)
+    p = (p * np.float32(scale)).astype(np.float32)
+    g, ps, o = route_ref.flash_mh_moe_global_sort(p, i, E)
+    want = ffn_ref.mh_moe_fwd_ref(xh, g, ps, o, Wg, Wu, Wd, dtype="bf16")
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16)
+    args = (t(xh), torch.from_numpy(gate), t(Wg), t(Wu), t(Wd), E, K, score, scale)
+    got = ffn_torch_ref.moe_layer_cpu(*args).float().numpy()
+    assert ffn_ref.rel_l2(got, want) < 5e-3
+    try:
+        ref = stage_ref.import_ref()
+    except ImportError:
+        return
+    got_ref = ffn_torch_ref.moe_layer_cpu(*args, ref=ref).float().numpy()
+    np.testing.assert_array_equal(got_ref, got)

@@ -44,8 +44,9 @@ def test_noalloc_sort_matches_allocating_sort_twice():
     from flash_mh_moe import _lib
     from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse
     L = _lib.lib()
-    # two calls in a row: config-1-sized routing, then a smaller multi-head problem
-    for (H, S, K, E), seed in (((1, 16384, 8, 128), 11), ((3, 1000, 5, 40), 12)):
+    # calls in a row: config-1-sized routing (chunked sort), a smaller multi-head problem,
+    # then one small enough for the single-CTA sort (H*S*K <= 8192 rows, H*E <= 256)
+    for (H, S, K, E), seed in (((1, 16384, 8, 128), 11), ((3, 1000, 5, 40), 12), ((2, 500, 4, 64), 13)):
         probs, idx = _inputs(H, S, K, E, seed)
         got = _noalloc(L, probs, idx, E)
         want = flash_mh_moe_global_sort_with_inverse(probs, idx, E)
@@ -53,6 +54,20 @@ def test_noalloc_sort_matches_allocating_sort_twice():
         _lib.check_device_status(idx.device)
         for a, b in zip(got, want):
             assert torch.equal(a, b)
+
+
+def test_noalloc_sort_empty_batch_zeroes_offsets():
+    from flash_mh_moe import _lib
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    H, K, E = 2, 4, 64
+    dummy = torch.zeros(8, dtype=torch.int64, device=dev)         # R == 0: nothing to write but offsets
+    o = torch.full((H * E + 1,), -7, dtype=torch.int64, device=dev)
+    rc = L.mhmoe_global_sort_noalloc(dummy.data_ptr(), dummy.data_ptr(), H, 0, K, E, dummy.data_ptr(),
+                                     dummy.data_ptr(), o.data_ptr(), None, None, _lib.stream_ptr(dev))
+    _lib.check(rc, "mhmoe_global_sort_noalloc")
+    torch.cuda.synchronize()
+    assert torch.equal(o, torch.zeros_like(o))
 
 
 def test_noalloc_sort_rejects_oversize():
