@@ -306,6 +306,19 @@ MHMOE_API int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank,
                                   void* const* peer_bases, int* dev_status, uint64_t timeout_ns,
                                   void* const* stage_events, void* stream);
 
+/* ───────────────────────── MoE layer around the routed core ───────────────────────── */
+
+/* Multi-modality RMSNorm, the MoE layer's pre-norm.  Replaces MultiModalityRMSNorm.forward
+ * (inference/model/magi2_preview.py:497-623, used as MultiHeadMoELayer.pre_norm at :2734):
+ * y[t,:] = bf16(x[t,:] * rsqrt(mean(x[t,:]^2) + eps) * (weight[m(t),:] + weight_bias)) in
+ * fp32, with rows grouped by modality: rows [cu_group_rows[m], cu_group_rows[m+1]) use
+ * weight row m (fp32 [n_groups, dim]).  cu_group_rows: device int32 [n_groups+1] (may be
+ * NULL when n_groups == 1).  x, y bf16 rows with the given strides (elements); dim % 8 == 0,
+ * dim <= 8192, 16-B aligned pointers and strides. */
+MHMOE_API int mhmoe_rmsnorm(const void* x, int64_t x_stride, const float* weight, const int32_t* cu_group_rows,
+                            int n_groups, int64_t rows, int dim, float eps, float weight_bias, void* y,
+                            int64_t y_stride, void* stream);
+
 /* ───────────────────────── failure detection ───────────────────────── */
 
 /* Self test of the bounded device waits (no counterpart in the reference).  Every

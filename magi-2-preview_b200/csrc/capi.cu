@@ -383,6 +383,21 @@ int mhmoe_wait_selftest(const int* flag, int expected, int mode, uint64_t timeou
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "wait_selftest");
 }
 
+/* ───────── MoE layer around the routed core ───────── */
+
+int mhmoe_rmsnorm(const void* x, int64_t x_stride, const float* weight, const int32_t* cu_group_rows, int n_groups,
+                  int64_t rows, int dim, float eps, float weight_bias, void* y, int64_t y_stride, void* stream) {
+  MHMOE_REQUIRE(x && y && weight && rows >= 0 && dim > 0 && dim % 8 == 0 && dim <= 8192);
+  MHMOE_REQUIRE(n_groups >= 1 && (n_groups == 1 || cu_group_rows));
+  MHMOE_REQUIRE(x_stride >= dim && y_stride >= dim && x_stride % 8 == 0 && y_stride % 8 == 0);
+  MHMOE_REQUIRE(aligned16(x) && aligned16(y) && aligned16(weight));
+  MHMOE_CHECK_ARCH();
+  const cudaError_t e = launch_rmsnorm_modality(
+      static_cast<const __nv_bfloat16*>(x), x_stride, weight, n_groups > 1 ? cu_group_rows : nullptr, n_groups, rows,
+      dim, eps, weight_bias, static_cast<__nv_bfloat16*>(y), y_stride, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "rmsnorm");
+}
+
 /* ───────── expert-parallel exchange over peer memory ───────── */
 
 size_t mhmoe_ep_sym_bytes(int n_ranks, int64_t cap, int dh, int K) {

@@ -224,6 +224,11 @@ cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataTy
                            uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
                            uint32_t box_rows, bool swizzle128 = true);
 
+// norm.cu
+cudaError_t launch_rmsnorm_modality(const __nv_bfloat16* x, int64_t sx, const float* w, const int32_t* cu_groups,
+                                    int n_groups, int64_t rows, int dim, float eps, float weight_bias,
+                                    __nv_bfloat16* y, int64_t sy, cudaStream_t st);
+
 // wait_selftest.cu
 cudaError_t launch_wait_selftest(const int* flag, int expected, int mode, uint64_t timeout_ns, int* status,
                                  int64_t* elapsed_ns, cudaStream_t st);

@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_quantize_rows_nvfp4": (i32, [vp, i64, i64, i32, vp, vp, vp, vp]),
     "mhmoe_gemm_nvfp4_raw": (i32, [vp, vp, i32, vp, vp, vp, i32, i32, i32, vp, vp, u64, vp]),
     "mhmoe_wait_selftest": (i32, [vp, i32, i32, u64, vp, vp, vp]),
+    "mhmoe_rmsnorm": (i32, [vp, i64, vp, vp, i32, i64, i32, f32, f32, vp, i64, vp]),
     "mhmoe_ffn_nvfp4_atomic": (i32, [vp, i64, i64, i32, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                      vp, vp, i64, i64, vp, u64, vp, vp]),
     "mhmoe_ep_sym_bytes": (sz, [i32, i64, i32, i32]),

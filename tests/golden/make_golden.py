@@ -15,6 +15,9 @@ Produces:
   (``inference/flash_mh_moe/triton/mh_moe_fwd.py:50-181``) run under
   ``TRITON_INTERPRET=1`` on fp32 tensors (the interpreter does not support bf16),
   atomic and deterministic variants.
+* ``layer_cases.npz`` — the MoE layer's pre-norm and shared experts from the reference
+  module ``inference/model/magi2_preview.py`` (``MultiModalityRMSNorm`` torch path,
+  ``MultiHeadMoELayer._shared_expert_forward``) in bf16 on the CPU, with seeded weights.
 """
 from __future__ import annotations
 
@@ -120,7 +123,92 @@ def make_ffn(route):
     print("ffn_fp32.npz:", len(cases), "cases")
 
 
+def _import_reference_model():
+    """inference/model/magi2_preview.py on a CPU box: three GPU-only imports it names at
+    module level are stubbed (FA3, MagiAttention's FA3-with-sink, MagiCompiler's
+    decorators as identities) and torch.compile runs eagerly; nothing on the MoE layer's
+    path uses them."""
+    import types
+    os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+    sys.path.insert(0, str(_reference_root()))
+    def _stub(name, value):
+        m = types.ModuleType(name)
+
+        def attr(a):
+            if a.startswith("__"):
+                raise AttributeError(a)
+            return value
+        m.__getattr__ = attr
+        sys.modules.setdefault(name, m)
+    _stub("flash_attn_interface", types.SimpleNamespace())
+    _stub("magi_attn_extensions", None)
+    _stub("magi_attn_extensions.fa3_interface_with_sink", lambda *a, **k: None)
+    mc = types.ModuleType("magi_compiler")
+
+    def _identity_decorator(*a, **k):
+        if len(a) == 1 and callable(a[0]) and not k:
+            return a[0]
+        return lambda f: f
+    mc.magi_compile = mc.magi_register_custom_op = _identity_decorator
+    sys.modules.setdefault("magi_compiler", mc)
+    from inference.model import magi2_preview  # type: ignore
+    return magi2_preview
+
+
+LAYER_CASES = [
+    # name, modality group sizes, hidden, shared, modality-specific, seed
+    ("three_modalities", (40, 24, 32), 256, 128, 128, 31),
+    ("empty_modality_unequal", (16, 0, 48), 256, 64, 128, 32),
+]
+
+
+def make_layer(mp):
+    """MultiModalityRMSNorm (magi2_preview.py:497-623, torch path) and
+    MultiHeadMoELayer._shared_expert_forward (:2775-2795) in bf16, from the reference
+    module itself; split/merge are plain F.linear and the routed core is pinned above."""
+    import torch
+    out = {}
+    for name, groups, d, Is, Im, seed in LAYER_CASES:
+        g = torch.Generator().manual_seed(seed)
+        moe = mp.MoEConfig(num_experts=4, top_k=2, num_heads=1, expert_intermediate_size=64,
+                           shared_expert_intermediate_size=Is, modality_specific_expert_intermediate_size=Im) \
+            if hasattr(mp, "MoEConfig") else None
+        if moe is None:
+            from inference.common.magi2_config import MoEConfig  # type: ignore
+            moe = MoEConfig(num_experts=4, top_k=2, num_heads=1, expert_intermediate_size=64,
+                            shared_expert_intermediate_size=Is, modality_specific_expert_intermediate_size=Im)
+        cfg = mp.MultiHeadMoELayerConfig(hidden_size=d, num_modality=len(groups), num_layers=1,
+                                         activation_type=mp.MLPActivationType.SWIGLU7, params_dtype=torch.bfloat16,
+                                         shared_expert_intermediate_sizes=Is,
+                                         modality_specific_expert_intermediate_sizes=Im,
+                                         shared_expert_params_dtype=torch.bfloat16,
+                                         split_merge_intermediate_size=None, moe_config=moe)
+        layer = mp.MultiHeadMoELayer(cfg)
+        p = f"{name}/"
+        with torch.no_grad():
+            for pname, prm in layer.named_parameters():
+                if pname.startswith("moe_mlp."):
+                    continue
+                std = 0.1 if pname == "pre_norm.weight" else 0.05
+                prm.copy_((torch.randn(prm.shape, generator=g) * std).to(prm.dtype))
+                out[p + pname] = prm.float().numpy()
+        mapping = torch.cat([torch.full((n,), m, dtype=torch.int64) for m, n in enumerate(groups)])
+        disp = mp.ModalityDispatcher(mapping, len(groups))
+        x = torch.randn(sum(groups), d, generator=g).to(torch.bfloat16)
+        with torch.no_grad():
+            layer.pre_norm.backend = "torch"
+            norm = layer.pre_norm(x, modality_dispatcher=disp)
+            shared = layer._shared_expert_forward(norm, disp)
+        out[p + "groups"] = np.array(groups, np.int64)
+        out[p + "x"] = x.float().numpy()
+        out[p + "norm"] = norm.float().numpy()
+        out[p + "shared"] = shared.float().numpy()
+    np.savez_compressed(HERE / "layer_cases.npz", **out)
+    print("layer_cases.npz:", len(LAYER_CASES), "cases")
+
+
 if __name__ == "__main__":
     r = _import_reference()
     make_route(r)
     make_ffn(r)
+    make_layer(_import_reference_model())

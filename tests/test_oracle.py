@@ -179,3 +179,27 @@ def test_torch_cpu_layer_matches_oracle(H, dh, de, E, K, score, scale):
         return
     got_ref = ffn_torch_ref.moe_layer_cpu(*args, ref=ref).float().numpy()
     np.testing.assert_array_equal(got_ref, got)
+
+
+# ───────────────────────── MoE layer around the core vs the reference module ─────────────────────────
+
+_L = np.load(GOLD / "layer_cases.npz")
+_LNAMES = sorted({k.split("/")[0] for k in _L.files})
+
+
+@pytest.mark.parametrize("name", _LNAMES)
+def test_layer_oracle_matches_reference(name):
+    """oracle.layer_ref's pre-norm and shared experts against the reference module's own
+    MultiModalityRMSNorm and MultiHeadMoELayer._shared_expert_forward (bf16, CPU)."""
+    from oracle import layer_ref
+    d = lambda k: _L[f"{name}/{k}"]
+    groups = [int(v) for v in d("groups")]
+    norm = layer_ref.rmsnorm_ref(d("x"), d("pre_norm.weight"), groups)
+    # one bf16 ulp at most (the mean's summation order differs)
+    ulp = np.abs(norm - d("norm")) / np.maximum(np.abs(d("norm")), 1e-30)
+    assert float(ulp.max()) <= 2.0 ** -7
+    shared = layer_ref.shared_experts_ref(d("norm"), groups, d("shared_expert_fc1.weight"),
+                                          d("shared_expert_fc2.weight"),
+                                          d("modality_specific_shared_expert_fc1.weight"),
+                                          d("modality_specific_shared_expert_fc2.weight"))
+    assert ffn_ref.rel_l2(shared, d("shared")) < 2e-3
