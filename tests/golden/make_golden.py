@@ -18,6 +18,8 @@ Produces:
 * ``layer_cases.npz`` — the MoE layer's pre-norm and shared experts from the reference
   module ``inference/model/magi2_preview.py`` (``MultiModalityRMSNorm`` torch path,
   ``MultiHeadMoELayer._shared_expert_forward``) in bf16 on the CPU, with seeded weights.
+* ``ckpt_slices.npz`` — the rows the reference checkpoint reader's expert-parallel rule
+  (``inference/infra/checkpoint/magi2_checkpointing.py:81-105``) gives each rank.
 """
 from __future__ import annotations
 
@@ -207,8 +209,48 @@ def make_layer(mp):
     print("layer_cases.npz:", len(LAYER_CASES), "cases")
 
 
+CKPT_CASES = [
+    # real rows, target rows, ep size
+    (12, 12, 4),        # replicated router tensor: read whole
+    (12, 3, 4),         # even split
+    (12, 4, 4),         # heads padded up to the EP size: the last rank is all zeros
+    (10, 4, 3),         # the last rank partly past the real rows
+]
+
+
+def make_ckpt():
+    """The reference's EP row reader (_read_ep_slice, magi2_checkpointing.py:81-105) on a
+    safetensors file of numbered rows, for every rank of each case."""
+    import tempfile
+
+    import torch
+    from safetensors.torch import save_file
+    sys.path.insert(0, str(_reference_root()))
+    from safetensors import safe_open
+    from inference.infra.checkpoint import magi2_checkpointing as ck  # type: ignore
+    out = {}
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "t.safetensors")
+        tensors = {f"layer.moe_mlp.W_gate{i}": (torch.arange(real * 6, dtype=torch.float32).view(real, 2, 3) + 1)
+                   .to(torch.bfloat16) for i, (real, _, _) in enumerate(CKPT_CASES)}
+        save_file(tensors, path)
+        for i, (real, shard, ep) in enumerate(CKPT_CASES):
+            for rank in range(ep):
+                ck.psm.get_world_size = lambda dim="", _e=ep: _e
+                ck.psm.get_local_rank = lambda dim, _r=rank: _r
+                ck._is_ep_sharded_key = lambda key: True
+                key = f"layer.moe_mlp.W_gate{i}"
+                with safe_open(path, framework="pt") as h:
+                    got = ck._read_ep_slice(h, key, torch.empty(shard, 2, 3, dtype=torch.bfloat16))
+                out[f"case{i}/rank{rank}"] = got.float().numpy()
+            out[f"case{i}/meta"] = np.array([real, shard, ep], np.int64)
+    np.savez_compressed(HERE / "ckpt_slices.npz", **out)
+    print("ckpt_slices.npz:", len(CKPT_CASES), "cases")
+
+
 if __name__ == "__main__":
     r = _import_reference()
     make_route(r)
     make_ffn(r)
     make_layer(_import_reference_model())
+    make_ckpt()
