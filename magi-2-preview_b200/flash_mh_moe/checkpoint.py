@@ -117,7 +117,7 @@ def load_moe_module(module, checkpoint_dir: str | None = None, prefix: str = "",
     reading, ``chunk_experts`` experts at a time; with ``release_masters`` the bf16 expert
     parameters are left empty (``CoreMultiHeadMoE.release_master_weights`` state), else they
     are filled too.  Returns the (start, stop, pad) row ranges read per key."""
-    from .nvfp4 import NVFP4Down, NVFP4GateUp, pack_down, pack_gate_up
+    from .nvfp4 import NVFP4Down, NVFP4GateUp, pack_down, pack_gate_up, padded
     wm = weight_map if weight_map is not None else read_weight_map(checkpoint_dir)
     files = _Files(wm)
     ranges: dict[str, tuple[int, int, int]] = {}
@@ -164,13 +164,14 @@ def load_moe_module(module, checkpoint_dir: str | None = None, prefix: str = "",
             module._masters_released = False
             return ranges
 
-        dh, de = module.d_head, module.d_expert
+        dh0, de0 = module.d_head, module.d_expert
+        dh, de = padded(dh0), padded(de0)          # the packed (tile-multiple) sizes
         gu = NVFP4GateUp(torch.empty(nl, 2 * de, dh // 2, dtype=torch.uint8, device=dev),
                          torch.empty(nl, 2 * de * dh // 16, dtype=torch.uint8, device=dev),
-                         torch.empty(2, nl, dtype=torch.float32, device=dev), nl, dh, de)
+                         torch.empty(2, nl, dtype=torch.float32, device=dev), nl, dh, de, dh0, de0)
         dn = NVFP4Down(torch.empty(nl, dh, de // 2, dtype=torch.uint8, device=dev),
                        torch.empty(nl, dh * de // 16, dtype=torch.uint8, device=dev),
-                       torch.empty(nl, dtype=torch.float32, device=dev), nl, dh, de)
+                       torch.empty(nl, dtype=torch.float32, device=dev), nl, dh, de, dh0, de0)
         keep = not release_masters
         if keep:
             for n, p in (("W_gate", module.W_gate), ("W_up", module.W_up), ("W_down", module.W_down)):

@@ -459,6 +459,9 @@ def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None, comm_events
     """``CoreMultiHeadMoE`` forward with ``ep_size > 1`` (route locally, EP FFN)."""
     probs, idx = module._route(x_heads)
     gu, dn = module.packed_weights()
+    if gu.d_head != x_heads.shape[-1]:
+        raise NotImplementedError(f"expert parallelism takes d_head multiples of 256 (got {x_heads.shape[-1]}): "
+                                  "its records carry the unpadded NVFP4 rows")
     if ep_transport(module) == "peer":
         return ep_moe_layer_peer_pipelined(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
                                            chunks=ep_chunks(), stage_events=stage_events, comm_events=comm_events)

@@ -86,16 +86,24 @@ def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tens
     before the tile tables, gate/up GEMM, down GEMM, combine, and at the end.
     """
     _lib.require_cuda(x_heads, expert_offsets)
-    S, H, dh = x_heads.shape
+    S, H, dh0 = x_heads.shape
     n = expert_offsets.numel() - 1
     if gu.num_experts != n or dn.num_experts != n:
         raise ValueError(f"weights hold {gu.num_experts}/{dn.num_experts} experts, expert_offsets {n}")
-    if gu.d_head != dh or dn.d_head != dh or gu.d_expert != dn.d_expert:
+    if gu.shape[1] != dh0 or dn.shape[2] != dh0 or gu.d_head != dn.d_head or gu.d_expert != dn.d_expert:
         raise ValueError("weight shapes do not match x")
-    de = gu.d_expert
-    assert dh % 256 == 0, f"d_head={dh} must be divisible by 256"
-    assert de % 256 == 0, f"d_expert={de} must be divisible by 256"
+    dh, de = gu.d_head, gu.d_expert
+    assert dh % 256 == 0 and de % 256 == 0, "packed dimensions are multiples of 256"
     x = x_heads if x_heads.dtype == torch.bfloat16 else x_heads.to(torch.bfloat16)
+    if dh != dh0:
+        # a head size the tiles do not take: zero-pad the rows (exact; see nvfp4.py), crop y
+        y_pad = ffn_nvfp4(torch.nn.functional.pad(x, (0, dh - dh0)), gather_ids, probs, expert_offsets, gu, dn,
+                          tok_rows, tok_offsets, k_fixed, None, stage_events, deterministic)
+        y = y_pad[..., :dh0]
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y.contiguous()
     if x.stride(2) != 1 or x.stride(0) % 8 or x.stride(1) % 8 or x.data_ptr() % 16:
         x = x.contiguous()
     dev = x.device

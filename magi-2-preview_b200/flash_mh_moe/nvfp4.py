@@ -15,6 +15,14 @@ form of those same parameters, built on the GPU by ``mhmoe_pack_weights_nvfp4``.
   matching up rows, so each 32-column accumulator chunk of the gate/up GEMM holds
   one 16-wide SwiGLU block.  gscale [2, H*E] (gate, up).
 * ``NVFP4Down``: W_down ([H*E, de, dh]) as the K-major operand [H*E, dh, de/2].
+
+Shapes the reference accepts but the tensor-core tiles do not (its kernel asserts only
+``d_head % 64 == 0`` and ``d_expert % 32 == 0``, ``triton/mh_moe_fwd.py:264-265``) are packed
+zero-padded to multiples of 256: ``d_head`` / ``d_expert`` hold the padded sizes and
+``src_d_head`` / ``src_d_expert`` the caller's.  The padding is exact: zero weight rows and
+columns contribute nothing to the accumulators, zero gate and up columns give a zero
+SwiGLU7 output, and zero blocks leave the per-row and per-block scales of the real data
+unchanged.
 """
 from __future__ import annotations
 
@@ -31,12 +39,14 @@ class NVFP4GateUp:
     sf: torch.Tensor         # uint8 [n, 2*de*dh/16]  (SF atoms per expert)
     gscale: torch.Tensor     # fp32 [2, n]
     num_experts: int         # flattened H*E
-    d_head: int
-    d_expert: int
+    d_head: int              # packed (multiple of 256)
+    d_expert: int            # packed (multiple of 256)
+    src_d_head: int | None = None
+    src_d_expert: int | None = None
 
     @property
     def shape(self):  # reference W_gate shape
-        return (self.num_experts, self.d_head, self.d_expert)
+        return (self.num_experts, self.src_d_head or self.d_head, self.src_d_expert or self.d_expert)
 
 
 @dataclass
@@ -47,14 +57,33 @@ class NVFP4Down:
     num_experts: int
     d_head: int
     d_expert: int
+    src_d_head: int | None = None
+    src_d_expert: int | None = None
 
     @property
     def shape(self):  # reference W_down shape
-        return (self.num_experts, self.d_expert, self.d_head)
+        return (self.num_experts, self.src_d_expert or self.d_expert, self.src_d_head or self.d_head)
 
 
 def _bf16c(w: torch.Tensor) -> torch.Tensor:
     return w.detach().to(torch.bfloat16).contiguous()
+
+
+def padded(n: int) -> int:
+    """The tile multiple (256) a head or expert dimension is packed at."""
+    return (n + 255) // 256 * 256
+
+
+def check_dims(dh: int, de: int) -> None:
+    """The reference's shape contract (triton/mh_moe_fwd.py:264-265)."""
+    assert dh % 64 == 0, f"d_head={dh} must be divisible by 64"
+    assert de % 32 == 0, f"d_expert={de} must be divisible by 32"
+
+
+def _pad_to(w: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    if w.shape[1] == rows and w.shape[2] == cols:
+        return w
+    return torch.nn.functional.pad(w, (0, cols - w.shape[2], 0, rows - w.shape[1]))
 
 
 def pack_gate_up(W_gate: torch.Tensor, W_up: torch.Tensor) -> NVFP4GateUp:
@@ -62,8 +91,10 @@ def pack_gate_up(W_gate: torch.Tensor, W_up: torch.Tensor) -> NVFP4GateUp:
     _lib.require_cuda(W_gate, W_up)
     if W_gate.shape != W_up.shape or W_gate.dim() != 3:
         raise ValueError(f"W_gate/W_up must both be [n, dh, de], got {tuple(W_gate.shape)}, {tuple(W_up.shape)}")
-    n, dh, de = W_gate.shape
-    wg, wu = _bf16c(W_gate), _bf16c(W_up)
+    n, dh0, de0 = W_gate.shape
+    check_dims(dh0, de0)
+    dh, de = padded(dh0), padded(de0)
+    wg, wu = _pad_to(_bf16c(W_gate), dh, de), _pad_to(_bf16c(W_up), dh, de)
     dev = wg.device
     data = torch.empty(n, 2 * de, dh // 2, dtype=torch.uint8, device=dev)
     sf = torch.empty(n, 2 * de * dh // 16, dtype=torch.uint8, device=dev)
@@ -73,7 +104,7 @@ def pack_gate_up(W_gate: torch.Tensor, W_up: torch.Tensor) -> NVFP4GateUp:
         _lib.check(_lib.lib().mhmoe_pack_weights_nvfp4(0, wg.data_ptr(), wu.data_ptr(), n, dh, de, data.data_ptr(),
                                                         sf.data_ptr(), gscale.data_ptr(), amax.data_ptr(),
                                                         _lib.stream_ptr(dev)), "pack_gate_up")
-    return NVFP4GateUp(data, sf, gscale, n, dh, de)
+    return NVFP4GateUp(data, sf, gscale, n, dh, de, dh0, de0)
 
 
 def pack_down(W_down: torch.Tensor) -> NVFP4Down:
@@ -81,8 +112,10 @@ def pack_down(W_down: torch.Tensor) -> NVFP4Down:
     _lib.require_cuda(W_down)
     if W_down.dim() != 3:
         raise ValueError(f"W_down must be [n, de, dh], got {tuple(W_down.shape)}")
-    n, de, dh = W_down.shape
-    wd = _bf16c(W_down)
+    n, de0, dh0 = W_down.shape
+    check_dims(dh0, de0)
+    dh, de = padded(dh0), padded(de0)
+    wd = _pad_to(_bf16c(W_down), de, dh)
     dev = wd.device
     data = torch.empty(n, dh, de // 2, dtype=torch.uint8, device=dev)
     sf = torch.empty(n, dh * de // 16, dtype=torch.uint8, device=dev)
@@ -92,7 +125,7 @@ def pack_down(W_down: torch.Tensor) -> NVFP4Down:
         _lib.check(_lib.lib().mhmoe_pack_weights_nvfp4(1, wd.data_ptr(), None, n, dh, de, data.data_ptr(),
                                                         sf.data_ptr(), gscale.data_ptr(), amax.data_ptr(),
                                                         _lib.stream_ptr(dev)), "pack_down")
-    return NVFP4Down(data, sf, gscale, n, dh, de)
+    return NVFP4Down(data, sf, gscale, n, dh, de, dh0, de0)
 
 
 def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
