@@ -82,7 +82,9 @@ MHMOE_API int mhmoe_router_prepare(const float* gate, int n_experts, int dh, int
  * contiguous (x_stride_h == dh).  E <= 256, K <= 16, dh % 64 == 0.
  * logit_bias (optional, fp32 [H*E]) is added to the logits before scoring (a gate bias
  * term; the reference has none, pass NULL).  logits (optional) receives the fp32 [H, S, E]
- * logits the scores were computed from. */
+ * logits the scores were computed from.  Batches of a few 128-token tiles (H*ceil(S/128)
+ * at most a quarter of the SMs, dh % 128 == 0) run a cluster kernel that splits the
+ * reduction over 8 CTAs instead (same contract, exact products summed in fp32). */
 MHMOE_API int mhmoe_route(const void* x, int64_t x_stride_s, int64_t x_stride_h, const void* planes, int nsplit,
                           int S, int H, int dh, int E, int K, int score_func, const float* logit_bias,
                           const float* expert_bias, int route_norm, float norm_eps, float route_scale, float* probs,

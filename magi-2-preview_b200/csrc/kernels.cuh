@@ -224,6 +224,14 @@ cudaError_t encode_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataTy
                            uint64_t inner, uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner,
                            uint32_t box_rows, bool swizzle128 = true);
 
+// route_small.cu: the router for batches of a few 128-token tiles (cluster split of the
+// reduction dimension, CUDA cores); same contract as router_tc
+bool router_small_supported(int S, int H, int dh, int E, int K);
+cudaError_t launch_router_small(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* planes, int nsplit,
+                                int S, int H, int dh, int E, int K, int score_func, const float* logit_bias,
+                                const float* bias, int route_norm, float norm_eps, float route_scale, float* probs,
+                                int64_t* idx, float* logits, cudaStream_t st);
+
 // norm.cu
 cudaError_t launch_rmsnorm_modality(const __nv_bfloat16* x, int64_t sx, const float* w, const int32_t* cu_groups,
                                     int n_groups, int64_t rows, int dim, float eps, float weight_bias,

@@ -1,0 +1,257 @@
+// Router for small batches: the fused router's contract (fp32-accurate logits, scoring,
+// +expert_bias for selection, top-k sorted descending with ties to the lower expert, L1
+// normalisation, route_scale; CoreMultiHeadMoE._route, inference/model/magi2_preview.py:
+// 2588-2601 and inference/flash_mh_moe/route.py:28-148) for batches too small to occupy
+// the GPU with one 128-token tensor-core tile per SM.
+//
+// At 256 tokens the tensor-core router runs two CTAs, each streaming 128 x dh of x and
+// the whole gate through one SM (~50 us).  Here a cluster of 8 CTAs splits the reduction
+// dimension of a 32-token tile: CTA r accumulates x[:, r*dh/8 : (r+1)*dh/8] against the
+// same slice of the gate planes, on the CUDA cores, as exact products (bf16 x bf16 plane
+// values) added in fp32 — the arithmetic of the tensor-core router.  The leader CTA sums
+// the eight partial tiles through distributed shared memory in rank order (run-to-run
+// identical), then scores and selects, one warp per token.  No scratch memory.
+#include "kernels.cuh"
+
+namespace mhmoe {
+
+constexpr int RS_TOK = 32;            // tokens per cluster tile
+constexpr int RS_SPLIT = 8;           // CTAs per cluster (reduction-dimension split)
+constexpr int RS_KC = 16;             // reduction elements per shared-memory chunk
+constexpr int RS_THREADS = 256;
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Warp-wide argmax: larger value wins, ties to the smaller index.
+__device__ __forceinline__ void rs_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+// EP = experts per lane (E <= 32 * EP).
+template <int EP>
+__global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1)
+    router_small_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, const __nv_bfloat16* __restrict__ planes,
+                        int nsplit, int S, int H, int dh, int E, int K, int score_func,
+                        const float* __restrict__ logit_bias, const float* __restrict__ bias, int route_norm,
+                        float norm_eps, float route_scale, float* __restrict__ probs, int64_t* __restrict__ idx,
+                        float* __restrict__ logits) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float rs_smem[];
+  constexpr int EPAD = 32 * EP;
+  float* red = rs_smem;                                   // [RS_TOK][EPAD] partial (leader: final) logits
+  float* xs = red + RS_TOK * EPAD;                        // [RS_TOK][RS_KC + 1]
+  float* gs = xs + RS_TOK * (RS_KC + 1);                  // [nsplit * EPAD][RS_KC + 1]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int tiles_per_head = (S + RS_TOK - 1) / RS_TOK;
+  const int tile = blockIdx.x / RS_SPLIT;
+  const int h = tile / tiles_per_head;
+  const int s0 = (tile % tiles_per_head) * RS_TOK;
+  const int kspan = dh / RS_SPLIT;
+  const int k_begin = (int)rank * kspan;
+  const int64_t prow = (int64_t)nsplit * dh;              // plane row pitch (elements)
+
+  float acc[4][EP];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < EP; ++j) acc[i][j] = 0.f;
+
+  for (int k0 = k_begin; k0 < k_begin + kspan; k0 += RS_KC) {
+    // x chunk: 32 tokens x 16 elements, one bf16 pair per thread
+    {
+      const int t = tid >> 3, c = (tid & 7) * 2;
+      const int s = s0 + t;
+      float2 v = make_float2(0.f, 0.f);
+      if (s < S) {
+        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(x + (int64_t)s * sx_s + (int64_t)h * dh +
+                                                                          k0 + c);
+        v = __bfloat1622float2(b);
+      }
+      xs[t * (RS_KC + 1) + c] = v.x;
+      xs[t * (RS_KC + 1) + c + 1] = v.y;
+    }
+    // gate planes chunk: nsplit x E rows of 16 elements (two 16-B loads per row)
+    const int kb = k0 / 64, kj = k0 % 64;
+    for (int u = tid; u < nsplit * E * 2; u += RS_THREADS) {
+      const int half = u & 1, pe = u >> 1;
+      const int p = pe / E, e = pe % E;
+      const uint4 w = *reinterpret_cast<const uint4*>(planes + (int64_t)(h * E + e) * prow +
+                                                      (int64_t)(kb * nsplit + p) * 64 + kj + half * 8);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+      float* dst = gs + (p * EPAD + e) * (RS_KC + 1) + half * 8;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(w2[q]);
+        dst[2 * q] = f.x;
+        dst[2 * q + 1] = f.y;
+      }
+    }
+    __syncthreads();
+    for (int p = 0; p < nsplit; ++p) {
+#pragma unroll 4
+      for (int c = 0; c < RS_KC; ++c) {
+        float a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = xs[(warp * 4 + i) * (RS_KC + 1) + c];
+#pragma unroll
+        for (int j = 0; j < EP; ++j) {
+          const int e = lane + 32 * j;
+          const float b = e < E ? gs[(p * EPAD + e) * (RS_KC + 1) + c] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i][j] = __fmaf_rn(a[i], b, acc[i][j]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < EP; ++j) red[(warp * 4 + i) * EPAD + lane + 32 * j] = acc[i][j];
+  cluster_sync();                         // every partial tile written
+
+  if (rank == 0) {
+    // fixed-order sum of the eight partials (rank 0 first), plus the optional logit bias
+    const uint32_t red_s = smem_u32(red);
+    uint32_t remote[RS_SPLIT];
+#pragma unroll
+    for (int r = 0; r < RS_SPLIT; ++r) remote[r] = mapa_shared(red_s, (uint32_t)r);
+    for (int u = tid; u < RS_TOK * E; u += RS_THREADS) {
+      const int t = u / E, e = u % E;
+      const int o = t * EPAD + e;
+      float v = red[o];
+#pragma unroll
+      for (int r = 1; r < RS_SPLIT; ++r) v += ld_dsmem_f32(remote[r] + (uint32_t)o * 4u);
+      if (logit_bias) v = __fadd_rn(v, logit_bias[(int64_t)h * E + e]);
+      red[o] = v;
+    }
+  }
+  cluster_sync();                         // the leader has read every partial: the others may exit
+  if (rank != 0) return;
+  __syncthreads();
+
+  // scoring and top-k: one warp per token
+  for (int t = warp; t < RS_TOK; t += RS_THREADS / 32) {
+    const int s = s0 + t;
+    if (s >= S) break;
+    const int64_t row = (int64_t)h * S + s;
+    const float* lg = red + t * EPAD;
+    if (logits)
+      for (int e = lane; e < E; e += 32) logits[row * E + e] = lg[e];
+    float mx = -INFINITY, sum = 0.f;
+    if (score_func == 0) {
+      for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      for (int e = lane; e < E; e += 32) sum += expf(lg[e] - mx);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    float sc[EP], sel[EP];
+#pragma unroll
+    for (int j = 0; j < EP; ++j) {
+      const int e = lane + 32 * j;
+      sc[j] = 0.f;
+      sel[j] = -INFINITY;
+      if (e < E) {
+        const float l = lg[e];
+        sc[j] = score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
+        sel[j] = bias ? __fadd_rn(sc[j], bias[(int64_t)h * E + e]) : sc[j];
+      }
+    }
+    float my_p = 0.f;
+    int my_i = 0;
+    for (int k = 0; k < K; ++k) {
+      float v = -INFINITY;
+      int vi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < EP; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E && (sel[j] > v || (sel[j] == v && e < vi))) {
+          v = sel[j];
+          vi = e;
+        }
+      }
+      rs_argmax(v, vi);
+      if (vi >= E) vi = 0;                  // every remaining value is NaN: deterministic fallback
+      float p = 0.f;
+#pragma unroll
+      for (int j = 0; j < EP; ++j)
+        if (lane + 32 * j == vi) {
+          p = sc[j];
+          sel[j] = -INFINITY;               // taken (never selected again: -inf < any score)
+        }
+      p = __shfl_sync(0xffffffffu, p, vi & 31);
+      if (lane == k) {
+        my_p = p;
+        my_i = vi;
+      }
+    }
+    if (route_norm) {
+      float a = lane < K ? fabsf(my_p) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      my_p = __fdiv_rn(my_p, fmaxf(a, norm_eps));
+    }
+    if (lane < K) {
+      probs[row * K + lane] = __fmul_rn(my_p, route_scale);
+      idx[row * K + lane] = my_i;
+    }
+  }
+}
+
+bool router_small_supported(int S, int H, int dh, int E, int K) {
+  const int tc_tiles = H * ((S + 127) / 128);
+  return tc_tiles * 4 <= num_sms() && dh % (RS_SPLIT * RS_KC) == 0 && E <= 256 && K <= 32 && K <= E;
+}
+
+cudaError_t launch_router_small(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* planes, int nsplit,
+                                int S, int H, int dh, int E, int K, int score_func, const float* logit_bias,
+                                const float* bias, int route_norm, float norm_eps, float route_scale, float* probs,
+                                int64_t* idx, float* logits, cudaStream_t st) {
+  if (S == 0) return cudaSuccess;
+  const int ep0 = (E + 31) / 32;
+  const int ep = ep0 <= 1 ? 1 : ep0 <= 2 ? 2 : ep0 <= 4 ? 4 : 8;    // instantiated lane widths
+  const int epad = 32 * ep;
+  const size_t smem = sizeof(float) * ((size_t)RS_TOK * epad + RS_TOK * (RS_KC + 1) +
+                                       (size_t)nsplit * epad * (RS_KC + 1));
+  const int tiles = H * ((S + RS_TOK - 1) / RS_TOK);
+  const dim3 grid(tiles * RS_SPLIT);
+#define MHMOE_RS_CASE(N)                                                                                          \
+  case N: {                                                                                                       \
+    static PerDeviceOnce once;                                                                                    \
+    const cudaError_t a = once.run([](int) {                                                                      \
+      return cudaFuncSetAttribute(router_small_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+    });                                                                                                           \
+    if (a != cudaSuccess) return a;                                                                               \
+    MHMOE_LAUNCH_PDL(router_small_kernel<N>, grid, RS_THREADS, smem, st, x, sx_s, planes, nsplit, S, H, dh, E, K,  \
+                     score_func, logit_bias, bias, route_norm, norm_eps, route_scale, probs, idx, logits);       \
+    break;                                                                                                        \
+  }
+  switch (ep) {
+    MHMOE_RS_CASE(1)
+    MHMOE_RS_CASE(2)
+    MHMOE_RS_CASE(4)
+    MHMOE_RS_CASE(8)
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef MHMOE_RS_CASE
+  return cudaGetLastError();
+}
+
+}  // namespace mhmoe

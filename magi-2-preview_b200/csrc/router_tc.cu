@@ -24,6 +24,7 @@
 // merged in two rounds (group 1 into 0 and 3 into 2, then 2 into 0) — lower groups hold
 // lower experts, so the merge keeps the order (score desc, expert asc) of one sequential
 // pass.
+#include <cstdlib>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -380,6 +381,16 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
               int dh, int E, int K, int score_func, const float* logit_bias, const float* bias, int route_norm,
               float norm_eps, float route_scale, float* probs, int64_t* idx, float* logits, int* status,
               cudaStream_t st, cudaError_t* cerr) {
+  if (router_small_supported(S, H, dh, E, K) && !std::getenv("MHMOE_ROUTER_TC_ONLY")) {
+    // a batch of a few tiles: split the reduction over clusters of CTAs instead
+    const cudaError_t e = launch_router_small(x, sx_s, gate_planes, nsplit, S, H, dh, E, K, score_func, logit_bias,
+                                              bias, route_norm, norm_eps, route_scale, probs, idx, logits, st);
+    if (e != cudaSuccess) {
+      *cerr = e;
+      return MHMOE_ERR_LAUNCH;
+    }
+    return MHMOE_OK;
+  }
   const int Npad = std::max(16, (E + 15) / 16 * 16);
   CUtensorMap tx, tg;
   if (encode_bf16_2d(&tx, x, (uint64_t)H * dh, (uint64_t)S, (uint64_t)sx_s * 2, RT_BK, RT_BM) != cudaSuccess ||

@@ -101,8 +101,16 @@ FUSED = [
 ]
 
 
+@pytest.mark.parametrize("path", ["default", "tensor_core"])
 @pytest.mark.parametrize("S,H,dh,E,K,score,use_bias,scale,bf16_gate", FUSED)
-def test_fused_router_matches_reference(S, H, dh, E, K, score, use_bias, scale, bf16_gate):
+def test_fused_router_matches_reference(S, H, dh, E, K, score, use_bias, scale, bf16_gate, path, monkeypatch):
+    """Both router kernels: batches of a few 128-token tiles take the cluster split-K
+    router by default (route_small.cu); MHMOE_ROUTER_TC_ONLY=1 forces the tensor-core
+    router (router_tc.cu) the full-size batches use."""
+    if path == "tensor_core":
+        monkeypatch.setenv("MHMOE_ROUTER_TC_ONLY", "1")
+    else:
+        monkeypatch.delenv("MHMOE_ROUTER_TC_ONLY", raising=False)
     from flash_mh_moe.route import route_fused, router_prepare
     g = torch.Generator().manual_seed(S * 7 + E)
     x = torch.randn(S, H, dh, generator=g).to(torch.bfloat16)
