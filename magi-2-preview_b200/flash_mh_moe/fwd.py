@@ -90,9 +90,9 @@ def ffn_nvfp4(x_heads: torch.Tensor, gather_ids: torch.Tensor, probs: torch.Tens
     n = expert_offsets.numel() - 1
     if gu.num_experts != n or dn.num_experts != n:
         raise ValueError(f"weights hold {gu.num_experts}/{dn.num_experts} experts, expert_offsets {n}")
-    if gu.shape[1] != dh0 or dn.shape[2] != dh0 or gu.d_head != dn.d_head or gu.d_expert != dn.d_expert:
-        raise ValueError("weight shapes do not match x")
     dh, de = gu.d_head, gu.d_expert
+    if dh0 not in (gu.shape[1], dh) or gu.shape[1] != dn.shape[2] or dh != dn.d_head or de != dn.d_expert:
+        raise ValueError("weight shapes do not match x")
     assert dh % 256 == 0 and de % 256 == 0, "packed dimensions are multiples of 256"
     x = x_heads if x_heads.dtype == torch.bfloat16 else x_heads.to(torch.bfloat16)
     if dh != dh0:

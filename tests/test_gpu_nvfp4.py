@@ -50,8 +50,12 @@ def test_pack_weights_bit_exact(n, dh, de):
     Wg[0, :16, :16] = 0                          # an all-zero block
     gu = pack_gate_up(Wg.cuda(), Wu.cuda())
     dn = pack_down(Wd.cuda())
-    ref_gu = nv.pack_gate_up(Wg.float().numpy(), Wu.float().numpy())
-    ref_dn = nv.pack_down(Wd.float().numpy())
+    # sizes that are not multiples of 256 are packed zero-padded up to one
+    dhp, dep = (dh + 255) // 256 * 256, (de + 255) // 256 * 256
+    pad = lambda w, a, b: np.pad(w.float().numpy(), ((0, 0), (0, a - w.shape[1]), (0, b - w.shape[2])))
+    ref_gu = nv.pack_gate_up(pad(Wg, dhp, dep), pad(Wu, dhp, dep))
+    ref_dn = nv.pack_down(pad(Wd, dep, dhp))
+    assert gu.shape == (n, dh, de) and (gu.d_head, gu.d_expert) == (dhp, dep)
     np.testing.assert_array_equal(to_np(gu.gscale[0]), ref_gu["gscale_gate"])
     np.testing.assert_array_equal(to_np(gu.gscale[1]), ref_gu["gscale_up"])
     np.testing.assert_array_equal(to_np(gu.data), ref_gu["data"])
