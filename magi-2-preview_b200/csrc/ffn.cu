@@ -119,7 +119,7 @@ static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, con
   });
   if (attr_err != cudaSuccess) return attr_err;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), max_work));
-  MHMOE_LAUNCH_PDL(ffn_gemm_nvfp4_kernel<EPI>, grid, GEMM_THREADS, gemm_smem_bytes(EPI), st, ta, tb, tc, p);
+  MHMOE_LAUNCH_PDL(ffn_gemm_nvfp4_kernel<EPI>, grid, gemm_threads(EPI), gemm_smem_bytes(EPI), st, ta, tb, tc, p);
   return cudaGetLastError();
 }
 

@@ -6,16 +6,20 @@
 //
 //   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
 //
-// Warp roles (352 threads):
+// Warp roles (EPI_SWIGLU: 608 threads, 16 epilogue warps; other epilogues: 352 threads, 8):
 //   warp 0      TMA producer into a 4-stage (EPI_DOWN: 3-stage) shared-memory ring, one
 //               stage = 256 K-elements: A tile (128 x 256 FP4 = 16 KB) and B tile
 //               (256 x 256 FP4 = 32 KB), 128-B swizzle, plus their UE4M3 scale atoms
 //               (2 KB + 4 KB, untiled bulk copies).  The whole warp waits; lane 0 issues.
 //   warp 1      TMEM owner + MMA issuer: per stage, once the stage's scale factors are in
 //               TMEM, issues 4 x tcgen05.mma kind::mxf4nvf4 block16 (M128 N256 K64).
-//   warps 2-9   epilogue: drain the accumulator with tcgen05.ld into registers,
-//               release TMEM, then apply the fused epilogue and store.
-//   warp 10     scale-factor copier: per stage copies the 12 scale atoms into TMEM
+//   warps 2..    epilogue: drain the accumulator with tcgen05.ld into registers,
+//               release TMEM, then apply the fused epilogue and store.  Warp w reads TMEM
+//               lane quarter w % 4 and a 1024/EPW-column slice of the accumulator.  The
+//               SwiGLU epilogue's arithmetic per accumulator element is several times the
+//               MMA's at small K (d_head 256: one 256-K stage per tile), so that
+//               epilogue gets 16 warps.
+//   last warp   scale-factor copier: per stage copies the 12 scale atoms into TMEM
 //               (tcgen05.cp 32x128b.warpx4) and commits to the stage's sf-full barrier.
 //               The copies cost the tcgen05 pipe more than the MMAs do; issued from their
 //               own warp they run ahead of and beside the MMAs instead of between them.
@@ -50,7 +54,7 @@ enum { EPI_SWIGLU = 0, EPI_DOWN = 1, EPI_RAW = 2, EPI_DOWN_ATOMIC = 3 };
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
 constexpr int GEMM_BK = 256;          // FP4 elements per stage = 128 bytes per row
-constexpr int GEMM_THREADS = 352;          // single-CTA kernel: warps 0-9 + the scale-factor copier
+constexpr int GEMM_THREADS = 352;          // single-CTA kernel, 8 epilogue warps: warps 0-9 + the copier
 constexpr int GEMMP_THREADS = 320;         // CTA-pair kernel
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK / 2;          // 16384
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK / 2;          // 32768
@@ -64,6 +68,9 @@ constexpr int GEMM_SF_COL0 = 256;
 constexpr int GEMM_SF_COLS_PER_STAGE = 48;
 
 __host__ __device__ constexpr int gemm_stages(int epi) { return epi == EPI_DOWN ? 3 : 4; }
+// Epilogue warps (a multiple of 4: each lane quarter of TMEM is read by EPW/4 warps).
+__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_SWIGLU ? 16 : 8; }
+__host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (3 + gemm_epi_warps(epi)); }
 __host__ __device__ constexpr int gemm_smem_bytes(int epi) {
   return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
 }
@@ -115,16 +122,16 @@ struct FfnGemmParams {
 __device__ __forceinline__ float swiglu7(float g, float u) {
   g = fminf(g, 7.0f);
   u = fminf(fmaxf(u, -7.0f), 7.0f);
-  const float sig = __frcp_rn(1.0f + __expf(-1.702f * g));
+  const float sig = __fdividef(1.0f, 1.0f + __expf(-1.702f * g));
   return g * sig * (u + 1.0f);
 }
 
 // Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
-// accumulator columns [128*half, 128*half + 128) already in registers (r), TMEM released.
+// accumulator columns [NCOL*half, NCOL*half + NCOL) already in registers (r), TMEM released.
 // stg: this warp's 4 KB store staging (EPI_DOWN).
-template <int EPI>
+template <int EPI, int NCOL>
 __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const CUtensorMap* tmC,
-                                                   const uint32_t (&r)[128], int mt, int nt, int m, int q, int half,
+                                                   const uint32_t (&r)[NCOL], int mt, int nt, int m, int q, int half,
                                                    int lane, uint8_t* stg) {
   const int e = p.tile_expert[mt];
   const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
@@ -133,10 +140,11 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
     const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
     const float s_up = __fmul_rn(gr, p.gs_up[e]);
     const int hid_cols = p.N / 2;
-    uint32_t words[8];
+    constexpr int NB = NCOL / 32;            // SwiGLU blocks: 16 gate + 16 up columns -> 16 hidden
+    uint32_t words[2 * NB];
     uint32_t sfw = 0;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < NB; ++c) {
       float hv[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -150,12 +158,16 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
       words[2 * c + 1] = w2[1];
       sfw |= sf << (8 * c);
     }
-    const int hcol0 = nt * (GEMM_BN / 2) + half * 64;          // first hidden column of this thread
+    const int hcol0 = nt * (GEMM_BN / 2) + half * (NCOL / 2);  // first hidden column of this thread
     uint4* dst = reinterpret_cast<uint4*>(p.h_data + prow * (size_t)(hid_cols / 2) + hcol0 / 2);
-    dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-    dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-    *reinterpret_cast<uint32_t*>(p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols)) =
-        sfw;
+#pragma unroll
+    for (int v = 0; v < NB / 2; ++v)
+      dst[v] = make_uint4(words[4 * v], words[4 * v + 1], words[4 * v + 2], words[4 * v + 3]);
+    uint8_t* sfd = p.h_sf + sf_atom_offset(prow, (uint32_t)(hcol0 / 16), (uint32_t)hid_cols);
+    if constexpr (NB == 4)
+      *reinterpret_cast<uint32_t*>(sfd) = sfw;
+    else
+      *reinterpret_cast<uint16_t*>(sfd) = (uint16_t)sfw;
   } else if constexpr (EPI == EPI_DOWN) {
     const int nrows = p.tile_rows[mt];
     const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
@@ -222,12 +234,15 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
 // tmB: B operand [n_experts * N, K/2], box 128 x 256.
 // tmC: EPI_DOWN -> P [128 * n_mtiles, N] bf16, box 64 x 32 (store); unused otherwise.
 template <int EPI>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const FfnGemmParams p) {
   pdl_wait();
   pdl_trigger();
   constexpr int STAGES = gemm_stages(EPI);
+  constexpr int EPW = gemm_epi_warps(EPI);
+  constexpr int NCOL = 4 * GEMM_BN / EPW;           // accumulator columns per epilogue thread
+  constexpr int COPIER = 2 + EPW;                   // warp index of the scale-factor copier
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -254,7 +269,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     mbar_init(smem_u32(tfull_bar), 1);
-    mbar_init(smem_u32(tempty_bar), 8);
+    mbar_init(smem_u32(tempty_bar), EPW);
     mbar_init(smem_u32(drain_bar), 1);
     for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&sff_bar[s]), 1);
     mbar_init(smem_u32(drain2_bar), 1);
@@ -350,7 +365,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       acc_phase ^= 1;
     }
-  } else if (warp == 10) {
+  } else if (warp == COPIER) {
     // ───────── scale-factor copier (whole warp waits; lane 0 issues) ─────────
     int stage = 0;
     uint32_t phase = 0;
@@ -376,9 +391,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
-    // ───────── epilogue warps 2..9 ─────────
+    // ───────── epilogue warps 2 .. 2+EPW-1 ─────────
     const int q = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;       // accumulator columns [128*half, 128*half + 128)
+    const int half = (warp - 2) >> 2;       // accumulator columns [NCOL*half, NCOL*half + NCOL)
     const int m = q * 32 + lane;            // tile row owned by this thread
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -386,18 +401,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
-      uint32_t r[128];
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 128);
-      MHMOE_TMEM_LD_32x32b_X32(taddr + 0, (r + 0));
-      MHMOE_TMEM_LD_32x32b_X32(taddr + 32, (r + 32));
-      MHMOE_TMEM_LD_32x32b_X32(taddr + 64, (r + 64));
-      MHMOE_TMEM_LD_32x32b_X32(taddr + 96, (r + 96));
+      uint32_t r[NCOL];
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * NCOL);
+#pragma unroll
+      for (int c = 0; c < NCOL; c += 32) MHMOE_TMEM_LD_32x32b_X32(taddr + c, (r + c));
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
 
-      gemm_epilogue_tile<EPI>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, NCOL>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();     // stores complete before the CTA exits
@@ -410,7 +423,7 @@ done:
     tc_commit(smem_u32(drain_bar));
     mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
-  if (warp == 10 && lane == 0) {
+  if (warp == COPIER && lane == 0) {
     tc_commit(smem_u32(drain2_bar));
     mbar_wait(smem_u32(drain2_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
@@ -599,7 +612,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      gemm_epilogue_tile<EPI>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, 128>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();
