@@ -112,15 +112,20 @@ static cudaError_t launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb
 template <int EPI>
 static cudaError_t launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                                const FfnGemmParams& p, int64_t max_work, cudaStream_t st) {
-  static PerDeviceOnce once;
-  const cudaError_t attr_err = once.run([](int) {
-    return cudaFuncSetAttribute(ffn_gemm_nvfp4_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                gemm_smem_bytes(EPI));
-  });
-  if (attr_err != cudaSuccess) return attr_err;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), max_work));
-  MHMOE_LAUNCH_PDL(ffn_gemm_nvfp4_kernel<EPI>, grid, gemm_threads(EPI), gemm_smem_bytes(EPI), st, ta, tb, tc, p);
-  return cudaGetLastError();
+  static PerDeviceOnce once[2];
+  auto go = [&](auto kernel, int epw) -> cudaError_t {
+    const cudaError_t attr_err = once[epw == 16].run([&](int) {
+      return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(EPI));
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    MHMOE_LAUNCH_PDL(kernel, grid, 32 * (3 + epw), gemm_smem_bytes(EPI), st, ta, tb, tc, p);
+    return cudaGetLastError();
+  };
+  if constexpr (EPI == EPI_SWIGLU) {
+    if (gemm_epi_warps(EPI, p.K) == 16) return go(ffn_gemm_nvfp4_kernel<EPI, 16>, 16);
+  }
+  return go(ffn_gemm_nvfp4_kernel<EPI, 8>, 8);
 }
 
 // ───────────────────────────── workspace layout ─────────────────────────────

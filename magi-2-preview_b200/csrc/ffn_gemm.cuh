@@ -6,7 +6,8 @@
 //
 //   D[128 x 256] (fp32, TMEM) = sum_k (A[128 x k] .* SFA) (B_e[256 x k] .* SFB)^T
 //
-// Warp roles (EPI_SWIGLU: 608 threads, 16 epilogue warps; other epilogues: 352 threads, 8):
+// Warp roles (3 + EPW warps: EPW = 16 epilogue warps for the SwiGLU epilogue at K <= 1024,
+// else 8):
 //   warp 0      TMA producer into a 4-stage (EPI_DOWN: 3-stage) shared-memory ring, one
 //               stage = 256 K-elements: A tile (128 x 256 FP4 = 16 KB) and B tile
 //               (256 x 256 FP4 = 32 KB), 128-B swizzle, plus their UE4M3 scale atoms
@@ -17,8 +18,8 @@
 //               release TMEM, then apply the fused epilogue and store.  Warp w reads TMEM
 //               lane quarter w % 4 and a 1024/EPW-column slice of the accumulator.  The
 //               SwiGLU epilogue's arithmetic per accumulator element is several times the
-//               MMA's at small K (d_head 256: one 256-K stage per tile), so that
-//               epilogue gets 16 warps.
+//               MMA's at small K (d_head 256: one 256-K stage per tile), so there it
+//               gets 16 warps.
 //   last warp   scale-factor copier: per stage copies the 12 scale atoms into TMEM
 //               (tcgen05.cp 32x128b.warpx4) and commits to the stage's sf-full barrier.
 //               The copies cost the tcgen05 pipe more than the MMAs do; issued from their
@@ -68,9 +69,12 @@ constexpr int GEMM_SF_COL0 = 256;
 constexpr int GEMM_SF_COLS_PER_STAGE = 48;
 
 __host__ __device__ constexpr int gemm_stages(int epi) { return epi == EPI_DOWN ? 3 : 4; }
-// Epilogue warps (a multiple of 4: each lane quarter of TMEM is read by EPW/4 warps).
-__host__ __device__ constexpr int gemm_epi_warps(int epi) { return epi == EPI_SWIGLU ? 16 : 8; }
-__host__ __device__ constexpr int gemm_threads(int epi) { return 32 * (3 + gemm_epi_warps(epi)); }
+// Epilogue warps (a multiple of 4: each lane quarter of TMEM is read by EPW/4 warps): 16 for
+// the SwiGLU epilogue when the reduction is short (K <= 1024: few MMAs per tile to hide the
+// epilogue behind), else 8.
+__host__ __device__ constexpr int gemm_epi_warps(int epi, int K) {
+  return epi == EPI_SWIGLU && K <= 1024 ? 16 : 8;
+}
 __host__ __device__ constexpr int gemm_smem_bytes(int epi) {
   return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
 }
@@ -126,19 +130,46 @@ __device__ __forceinline__ float swiglu7(float g, float u) {
   return g * sig * (u + 1.0f);
 }
 
-// Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
-// accumulator columns [NCOL*half, NCOL*half + NCOL) already in registers (r), TMEM released.
-// stg: this warp's 4 KB store staging (EPI_DOWN).
-template <int EPI, int NCOL>
-__device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const CUtensorMap* tmC,
-                                                   const uint32_t (&r)[NCOL], int mt, int nt, int m, int q, int half,
-                                                   int lane, uint8_t* stg) {
-  const int e = p.tile_expert[mt];
-  const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
+// Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded before the thread
+// waits for the accumulator so their global-memory latency hides under the MMAs.
+struct EpiScalars {
+  float s0, s1, pr;   // SwiGLU: gate / up dequantisation scales; down: scale, prob
+  int64_t tok;        // atomic scatter: token of the row
+  int e, rows;
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiScalars epi_prefetch(const FfnGemmParams& p, int mt, int m) {
+  EpiScalars v{};
+  v.e = p.tile_expert[mt];
+  const size_t prow = (size_t)mt * GEMM_BM + m;
   if constexpr (EPI == EPI_SWIGLU) {
     const float gr = p.row_gscale[prow];
-    const float s_gate = __fmul_rn(gr, p.gs_gate[e]);
-    const float s_up = __fmul_rn(gr, p.gs_up[e]);
+    v.s0 = __fmul_rn(gr, p.gs_gate[v.e]);
+    v.s1 = __fmul_rn(gr, p.gs_up[v.e]);
+  } else if constexpr (EPI == EPI_DOWN || EPI == EPI_DOWN_ATOMIC) {
+    v.rows = p.tile_rows[mt];
+    v.s0 = __fmul_rn(HIDDEN_GSCALE, p.gs_down[v.e]);
+    const bool valid = m < v.rows;
+    const int64_t srow = (int64_t)p.tile_row0[mt] + m;
+    v.pr = valid ? p.probs[srow] : 0.0f;
+    if constexpr (EPI == EPI_DOWN_ATOMIC) v.tok = valid ? p.gather_ids[srow] : 0;
+  }
+  return v;
+}
+
+// Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
+// accumulator columns [NCOL*half, NCOL*half + NCOL) already in registers (r), TMEM released,
+// per-tile scalars in v.  stg: this warp's 4 KB store staging (EPI_DOWN).
+template <int EPI, int NCOL>
+__device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const CUtensorMap* tmC,
+                                                   const uint32_t (&r)[NCOL], const EpiScalars& v, int mt, int nt,
+                                                   int m, int q, int half, int lane, uint8_t* stg) {
+  const int e = v.e;
+  const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
+  if constexpr (EPI == EPI_SWIGLU) {
+    const float s_gate = v.s0;
+    const float s_up = v.s1;
     const int hid_cols = p.N / 2;
     constexpr int NB = NCOL / 32;            // SwiGLU blocks: 16 gate + 16 up columns -> 16 hidden
     uint32_t words[2 * NB];
@@ -169,9 +200,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
     else
       *reinterpret_cast<uint16_t*>(sfd) = (uint16_t)sfw;
   } else if constexpr (EPI == EPI_DOWN) {
-    const int nrows = p.tile_rows[mt];
-    const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
-    const float pr = m < nrows ? p.probs[p.tile_row0[mt] + m] : 0.0f;
+    const float s = v.s0;
+    const float pr = v.pr;
     const uint32_t stg_s = smem_u32(stg);
 #pragma unroll
     for (int box = 0; box < 2; ++box) {
@@ -200,11 +230,10 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
       }
     }
   } else if constexpr (EPI == EPI_DOWN_ATOMIC) {
-    if (m < p.tile_rows[mt]) {
-      const int64_t srow = (int64_t)p.tile_row0[mt] + m;
-      const float s = __fmul_rn(HIDDEN_GSCALE, p.gs_down[e]);
-      const float pr = p.probs[srow];
-      const int64_t tok = p.gather_ids[srow];
+    if (m < v.rows) {
+      const float s = v.s0;
+      const float pr = v.pr;
+      const int64_t tok = v.tok;
       const int h = e / p.experts_per_head;
       __nv_bfloat16* yrow = p.y + tok * p.sy_s + (int64_t)h * p.sy_h + nt * GEMM_BN + half * 128;
 #pragma unroll
@@ -233,14 +262,14 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
 // tmA: grouped A operand [128 * n_mtiles, K/2], box 128 x 128.
 // tmB: B operand [n_experts * N, K/2], box 128 x 256.
 // tmC: EPI_DOWN -> P [128 * n_mtiles, N] bf16, box 64 x 32 (store); unused otherwise.
-template <int EPI>
-__global__ void __launch_bounds__(gemm_threads(EPI), 1)
+template <int EPI, int EPW>
+__global__ void __launch_bounds__(32 * (3 + EPW), 1)
     ffn_gemm_nvfp4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmC, const FfnGemmParams p) {
   pdl_wait();
   pdl_trigger();
   constexpr int STAGES = gemm_stages(EPI);
-  constexpr int EPW = gemm_epi_warps(EPI);
+  static_assert(EPW == 8 || (EPW == 16 && EPI == EPI_SWIGLU), "16 epilogue warps: SwiGLU epilogue only");
   constexpr int NCOL = 4 * GEMM_BN / EPW;           // accumulator columns per epilogue thread
   constexpr int COPIER = 2 + EPW;                   // warp index of the scale-factor copier
   extern __shared__ uint8_t smem_raw[];
@@ -398,6 +427,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
+      const EpiScalars sc = epi_prefetch<EPI>(p, mt, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
@@ -410,7 +440,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
 
-      gemm_epilogue_tile<EPI, NCOL>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, NCOL>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();     // stores complete before the CTA exits
@@ -599,6 +629,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
     for (int t = cluster_id; t < total; t += n_clusters) {
       const int pt = t / n_ntiles, nt = t % n_ntiles;
       const int mt = 2 * pt + (int)crank;
+      const EpiScalars sc = epi_prefetch<EPI>(p, mt, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
@@ -612,7 +643,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      gemm_epilogue_tile<EPI, 128>(p, &tmC, r, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, 128>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();
