@@ -8,7 +8,8 @@
 // the whole gate through one SM (~50 us).  Here a cluster of 8 CTAs splits the reduction
 // dimension of a 32-token tile: CTA r accumulates x[:, r*dh/8 : (r+1)*dh/8] against the
 // same slice of the gate planes, on the CUDA cores, as exact products (bf16 x bf16 plane
-// values) added in fp32 — the arithmetic of the tensor-core router.  The leader CTA sums
+// values) added in fp32 — the arithmetic of the tensor-core router — with the slice
+// streamed through shared memory by asynchronous copies.  The leader CTA sums
 // the eight partial tiles through distributed shared memory in rank order (run-to-run
 // identical), then scores and selects, one warp per token.  No scratch memory.
 #include "kernels.cuh"
@@ -17,7 +18,7 @@ namespace mhmoe {
 
 constexpr int RS_TOK = 32;            // tokens per cluster tile
 constexpr int RS_SPLIT = 8;           // CTAs per cluster (reduction-dimension split)
-constexpr int RS_KC = 16;             // reduction elements per shared-memory chunk
+constexpr int RS_SMEM_MAX = 200 * 1024;
 constexpr int RS_THREADS = 256;
 
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
@@ -39,21 +40,33 @@ __device__ __forceinline__ void rs_argmax(float& v, int& i) {
   }
 }
 
-// EP = experts per lane (E <= 32 * EP).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// EP = experts per lane (E <= 32 * EP).  The CTA's reduction slice is streamed in chunks of
+// kch elements through two shared-memory buffers with asynchronous 16-B copies (the next
+// chunk loads while this one is consumed), kept as bf16: x [32][kch + 8] and the gate
+// planes [nsplit][32*EP][kch + 8].  The row pitch (kch + 8) * 2 B is 16 mod 128 B, so the
+// 16-B reads of eight consecutive experts hit distinct banks.
 template <int EP>
 __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1)
     router_small_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, const __nv_bfloat16* __restrict__ planes,
                         int nsplit, int S, int H, int dh, int E, int K, int score_func,
                         const float* __restrict__ logit_bias, const float* __restrict__ bias, int route_norm,
                         float norm_eps, float route_scale, float* __restrict__ probs, int64_t* __restrict__ idx,
-                        float* __restrict__ logits) {
+                        float* __restrict__ logits, int kch) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ float rs_smem[];
+  extern __shared__ __align__(16) float rs_smem[];
   constexpr int EPAD = 32 * EP;
   float* red = rs_smem;                                   // [RS_TOK][EPAD] partial (leader: final) logits
-  float* xs = red + RS_TOK * EPAD;                        // [RS_TOK][RS_KC + 1]
-  float* gs = xs + RS_TOK * (RS_KC + 1);                  // [nsplit * EPAD][RS_KC + 1]
+  const int pitch = kch + 8;                              // bf16 elements per buffered row
+  const int buf_elems = (RS_TOK + nsplit * EPAD) * pitch;
+  __nv_bfloat16* bufs = reinterpret_cast<__nv_bfloat16*>(red + RS_TOK * EPAD);   // 2 x [x rows | gate rows]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_ctarank();
   const int tiles_per_head = (S + RS_TOK - 1) / RS_TOK;
@@ -63,6 +76,33 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1
   const int kspan = dh / RS_SPLIT;
   const int k_begin = (int)rank * kspan;
   const int64_t prow = (int64_t)nsplit * dh;              // plane row pitch (elements)
+  const int nch = kspan / kch;
+  const int vpr = kch / 8;                                // 16-B pieces per buffered row
+
+  auto issue = [&](int c) {
+    __nv_bfloat16* buf = bufs + (size_t)(c & 1) * buf_elems;
+    const int k0 = k_begin + c * kch;
+    const int rows = RS_TOK + nsplit * E;
+    for (int u = tid; u < rows * vpr; u += RS_THREADS) {
+      const int row = u / vpr, v = u % vpr;
+      const int k = k0 + 8 * v;
+      const __nv_bfloat16* src;
+      uint32_t nbytes = 16;
+      __nv_bfloat16* dst;
+      if (row < RS_TOK) {                                  // x row of token s0 + row
+        const int s = s0 + row;
+        src = s < S ? x + (int64_t)s * sx_s + (int64_t)h * dh + k : x;
+        nbytes = s < S ? 16u : 0u;                         // zero-filled past the batch
+        dst = buf + (size_t)row * pitch + 8 * v;
+      } else {                                             // plane p of expert e
+        const int pe = row - RS_TOK, p = pe / E, e = pe % E;
+        src = planes + (int64_t)(h * E + e) * prow + (int64_t)((k / 64) * nsplit + p) * 64 + k % 64;
+        dst = buf + (size_t)(RS_TOK + p * EPAD + e) * pitch + 8 * v;
+      }
+      cp_async16(smem_u32(dst), src, nbytes);
+    }
+    cp_async_commit();
+  };
 
   float acc[4][EP];
 #pragma unroll
@@ -70,53 +110,49 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1
 #pragma unroll
     for (int j = 0; j < EP; ++j) acc[i][j] = 0.f;
 
-  for (int k0 = k_begin; k0 < k_begin + kspan; k0 += RS_KC) {
-    // x chunk: 32 tokens x 16 elements, one bf16 pair per thread
-    {
-      const int t = tid >> 3, c = (tid & 7) * 2;
-      const int s = s0 + t;
-      float2 v = make_float2(0.f, 0.f);
-      if (s < S) {
-        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(x + (int64_t)s * sx_s + (int64_t)h * dh +
-                                                                          k0 + c);
-        v = __bfloat1622float2(b);
-      }
-      xs[t * (RS_KC + 1) + c] = v.x;
-      xs[t * (RS_KC + 1) + c + 1] = v.y;
-    }
-    // gate planes chunk: nsplit x E rows of 16 elements (two 16-B loads per row)
-    const int kb = k0 / 64, kj = k0 % 64;
-    for (int u = tid; u < nsplit * E * 2; u += RS_THREADS) {
-      const int half = u & 1, pe = u >> 1;
-      const int p = pe / E, e = pe % E;
-      const uint4 w = *reinterpret_cast<const uint4*>(planes + (int64_t)(h * E + e) * prow +
-                                                      (int64_t)(kb * nsplit + p) * 64 + kj + half * 8);
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-      float* dst = gs + (p * EPAD + e) * (RS_KC + 1) + half * 8;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(w2[q]);
-        dst[2 * q] = f.x;
-        dst[2 * q + 1] = f.y;
-      }
+  issue(0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) {
+      issue(c + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    for (int p = 0; p < nsplit; ++p) {
-#pragma unroll 4
-      for (int c = 0; c < RS_KC; ++c) {
-        float a[4];
+    const __nv_bfloat16* buf = bufs + (size_t)(c & 1) * buf_elems;
+    for (int kk = 0; kk < kch; kk += 8) {
+      float xa[4][8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = xs[(warp * 4 + i) * (RS_KC + 1) + c];
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(buf + (size_t)(warp * 4 + i) * pitch + kk);
+        const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(r2[q]);
+          xa[i][2 * q] = f.x;
+          xa[i][2 * q + 1] = f.y;
+        }
+      }
+      for (int p = 0; p < nsplit; ++p) {
 #pragma unroll
         for (int j = 0; j < EP; ++j) {
           const int e = lane + 32 * j;
-          const float b = e < E ? gs[(p * EPAD + e) * (RS_KC + 1) + c] : 0.f;
+          if (e >= E) continue;
+          const uint4 raw = *reinterpret_cast<const uint4*>(buf + (size_t)(RS_TOK + p * EPAD + e) * pitch + kk);
+          const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[i][j] = __fmaf_rn(a[i], b, acc[i][j]);
+          for (int q = 0; q < 4; ++q) {
+            const float2 g = __bfloat1622float2(r2[q]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              acc[i][j] = __fmaf_rn(xa[i][2 * q], g.x, acc[i][j]);
+              acc[i][j] = __fmaf_rn(xa[i][2 * q + 1], g.y, acc[i][j]);
+            }
+          }
         }
       }
     }
-    __syncthreads();
+    __syncthreads();                        // this buffer is refilled by chunk c + 2
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -214,9 +250,26 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1
   }
 }
 
+// Largest chunk (a multiple of 16 dividing the CTA's slice) whose two buffers fit.
+static int rs_chunk(int dh, int E, int nsplit, size_t* smem) {
+  const int epad = E <= 32 ? 32 : E <= 64 ? 64 : E <= 128 ? 128 : 256;
+  const int kspan = dh / RS_SPLIT;
+  for (int kch = kspan; kch >= 16; kch -= 16) {
+    if (kspan % kch) continue;
+    const size_t bytes = sizeof(float) * RS_TOK * epad + 2 * sizeof(__nv_bfloat16) * (RS_TOK + (size_t)nsplit * epad) *
+                                                             (kch + 8);
+    if (bytes <= RS_SMEM_MAX) {
+      if (smem) *smem = bytes;
+      return kch;
+    }
+  }
+  return 0;
+}
+
 bool router_small_supported(int S, int H, int dh, int E, int K) {
   const int tc_tiles = H * ((S + 127) / 128);
-  return tc_tiles * 4 <= num_sms() && dh % (RS_SPLIT * RS_KC) == 0 && E <= 256 && K <= 32 && K <= E;
+  return tc_tiles * 4 <= num_sms() && dh % (RS_SPLIT * 16) == 0 && E <= 256 && K <= 32 && K <= E &&
+         rs_chunk(dh, E, 3, nullptr) > 0;
 }
 
 cudaError_t launch_router_small(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* planes, int nsplit,
@@ -226,20 +279,20 @@ cudaError_t launch_router_small(const __nv_bfloat16* x, int64_t sx_s, const __nv
   if (S == 0) return cudaSuccess;
   const int ep0 = (E + 31) / 32;
   const int ep = ep0 <= 1 ? 1 : ep0 <= 2 ? 2 : ep0 <= 4 ? 4 : 8;    // instantiated lane widths
-  const int epad = 32 * ep;
-  const size_t smem = sizeof(float) * ((size_t)RS_TOK * epad + RS_TOK * (RS_KC + 1) +
-                                       (size_t)nsplit * epad * (RS_KC + 1));
+  size_t smem = 0;
+  const int kch = rs_chunk(dh, E, nsplit, &smem);
+  if (kch == 0) return cudaErrorInvalidValue;
   const int tiles = H * ((S + RS_TOK - 1) / RS_TOK);
   const dim3 grid(tiles * RS_SPLIT);
 #define MHMOE_RS_CASE(N)                                                                                          \
   case N: {                                                                                                       \
     static PerDeviceOnce once;                                                                                    \
     const cudaError_t a = once.run([](int) {                                                                      \
-      return cudaFuncSetAttribute(router_small_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+      return cudaFuncSetAttribute(router_small_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, RS_SMEM_MAX); \
     });                                                                                                           \
     if (a != cudaSuccess) return a;                                                                               \
     MHMOE_LAUNCH_PDL(router_small_kernel<N>, grid, RS_THREADS, smem, st, x, sx_s, planes, nsplit, S, H, dh, E, K,  \
-                     score_func, logit_bias, bias, route_norm, norm_eps, route_scale, probs, idx, logits);       \
+                     score_func, logit_bias, bias, route_norm, norm_eps, route_scale, probs, idx, logits, kch);  \
     break;                                                                                                        \
   }
   switch (ep) {
