@@ -56,7 +56,7 @@ constexpr int GEMM_BM = 128;
 constexpr int GEMM_BN = 256;
 constexpr int GEMM_BK = 256;          // FP4 elements per stage = 128 bytes per row
 constexpr int GEMM_THREADS = 352;          // single-CTA kernel, 8 epilogue warps: warps 0-9 + the copier
-constexpr int GEMMP_THREADS = 320;         // CTA-pair kernel
+constexpr int GEMMP_THREADS = 352;         // CTA-pair kernel: warps 0-9 + the leader's scale-factor copier
 constexpr int GEMM_A_BYTES = GEMM_BM * GEMM_BK / 2;          // 16384
 constexpr int GEMM_B_BYTES = GEMM_BN * GEMM_BK / 2;          // 32768
 constexpr int GEMM_SFA_BYTES = GEMM_BM * GEMM_BK / 16;       // 2048
@@ -471,9 +471,11 @@ done:
 //   producer (both CTAs): TMA loads into its own shared memory (A rows, B rows
 //     [nt*256 + 128*r, +128), SFA, full SFB) that signal the LEADER's full barrier; the
 //     leader's producer posts the expected bytes of both CTAs.
-//   MMA (leader only): tcgen05.cp / tcgen05.mma with cta_group::2 (each CTA's shared memory
-//     at the same offsets -> its own TMEM), commits to the stage's empty barrier of both
-//     CTAs and, per tile, to both CTAs' accumulator-full barrier.
+//   copier (warp 10, leader only): tcgen05.cp with cta_group::2 (each CTA's shared memory at
+//     the same offsets -> its own TMEM), committed to the leader's sf-full barrier.
+//   MMA (leader only): tcgen05.mma with cta_group::2 once the stage's data and scale
+//     factors are in, commits to the stage's empty barrier of both CTAs and, per tile, to
+//     both CTAs' accumulator-full barrier.
 //   epilogue (both CTAs): its own 128 rows; releases the accumulator on the leader's
 //     barrier (16 arrivals per tile).
 // tmSFA / tmSFB: the SF atom arrays viewed as [bytes/256, 256] u8, box 256 x 8 (2 KB).
@@ -496,7 +498,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = tfull_bar + 1;            // (leader's is used)
   uint64_t* drain_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* sff_bar = tfull_bar + 3;               // [STAGES] scale factors of the stage in TMEM (leader's)
+  uint64_t* drain2_bar = sff_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain2_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -511,6 +515,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
     mbar_init(smem_u32(tfull_bar), 1);
     mbar_init(smem_u32(tempty_bar), 16);
     mbar_init(smem_u32(drain_bar), 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&sff_bar[s]), 1);
+    mbar_init(smem_u32(drain2_bar), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -586,18 +592,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
         tc_fence_after();
         for (int kb = 0; kb < n_kblk; ++kb) {
           if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          if (!mbar_wait(smem_u32(&sff_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
             const uint32_t tsfb = tsfa + 16;
-            const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
-            const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              tc_cp_32x128b_warpx4_pair(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
-              tc_cp_32x128b_warpx4_pair(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
-              tc_cp_32x128b_warpx4_pair(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
-            }
             const uint32_t a_s = smem_u32(sA + stage * GEMM_A_BYTES);
             const uint32_t b_s = smem_u32(sB + stage * GEMMP_B_BYTES);
 #pragma unroll
@@ -617,6 +616,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
         }
         __syncwarp();
         acc_phase ^= 1;
+      }
+    }
+  } else if (warp == 10) {
+    // ───────── scale-factor copier: the leader CTA only (pair copies reach both CTAs' TMEM) ─────────
+    // Slot s is rewritten only after full[s] of the next round, posted after empty[s], which
+    // the MMA warp commits after the MMAs that read slot s (as in the single-CTA kernel).
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = cluster_id; t < total; t += n_clusters) {
+        for (int kb = 0; kb < n_kblk; ++kb) {
+          if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) goto done;
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t tsfa = tmem_base + GEMM_SF_COL0 + stage * GEMM_SF_COLS_PER_STAGE;
+            const uint32_t tsfb = tsfa + 16;
+            const uint32_t sfa_s = smem_u32(sSFA + stage * GEMM_SFA_BYTES);
+            const uint32_t sfb_s = smem_u32(sSFB + stage * GEMM_SFB_BYTES);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              tc_cp_32x128b_warpx4_pair(tsfa + j * 4, sdesc_sf_chunk(sfa_s + j * 512));
+              tc_cp_32x128b_warpx4_pair(tsfb + j * 8, sdesc_sf_chunk(sfb_s + j * 512));
+              tc_cp_32x128b_warpx4_pair(tsfb + j * 8 + 4, sdesc_sf_chunk(sfb_s + 2048 + j * 512));
+            }
+            tc_commit_pair(mapa_shared(smem_u32(&sff_bar[stage]), 0));
+          }
+          __syncwarp();
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
       }
     }
   } else {
@@ -653,6 +681,10 @@ done:
   if (leader && warp == 1 && lane == 0) {
     tc_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
     mbar_wait(smem_u32(drain_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
+  }
+  if (leader && warp == 10 && lane == 0) {
+    tc_commit_pair(mapa_shared(smem_u32(drain2_bar), 0));
+    mbar_wait(smem_u32(drain2_bar), 0, nullptr, 0, MHMOE_DRAIN_NS);
   }
   tc_fence_before();
   cluster_sync();                                  // neither CTA leaves while the pair still uses it
