@@ -64,6 +64,7 @@ constexpr int GEMM_SFB_BYTES = GEMM_BN * GEMM_BK / 16;       // 4096
 constexpr int GEMM_STAGE_TX = GEMM_A_BYTES + GEMM_B_BYTES + GEMM_SFA_BYTES + GEMM_SFB_BYTES;
 constexpr int GEMM_STAGE_BYTES = GEMM_STAGE_TX;
 constexpr int GEMM_STG_BYTES = 8 * 32 * 128;                 // EPI_DOWN: 4 KB store staging per epilogue warp
+constexpr int GEMM_MISC_BYTES = 256 + 512;                    // mbarriers + TMEM slot, then the 128-float table
 constexpr int GEMM_TMEM_COLS = 512;
 constexpr int GEMM_SF_COL0 = 256;
 constexpr int GEMM_SF_COLS_PER_STAGE = 48;
@@ -76,7 +77,7 @@ __host__ __device__ constexpr int gemm_epi_warps(int epi, int K) {
   return epi == EPI_SWIGLU && K <= 1024 ? 16 : 8;
 }
 __host__ __device__ constexpr int gemm_smem_bytes(int epi) {
-  return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
+  return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + GEMM_MISC_BYTES + 1024;
 }
 
 // CTA-pair variant (cluster of 2, cta_group::2): M = 256 rows per pair (128 per CTA), each
@@ -87,7 +88,7 @@ constexpr int GEMMP_STAGE_TX = GEMM_A_BYTES + GEMMP_B_BYTES + GEMM_SFA_BYTES + G
 constexpr int GEMMP_STAGE_BYTES = GEMMP_STAGE_TX;
 __host__ __device__ constexpr int gemmp_stages(int epi) { return epi == EPI_DOWN ? 4 : 5; }
 __host__ __device__ constexpr int gemmp_smem_bytes(int epi) {
-  return gemmp_stages(epi) * GEMMP_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + 256 + 1024;
+  return gemmp_stages(epi) * GEMMP_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + GEMM_MISC_BYTES + 1024;
 }
 
 // Static second-level scale of the SwiGLU7 hidden: |swiglu7| <= 7 * 8 = 56, 56 / 2688.
@@ -123,11 +124,57 @@ struct FfnGemmParams {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ float swiglu7(float g, float u) {
-  g = fminf(g, 7.0f);
-  u = fminf(fmaxf(u, -7.0f), 7.0f);
-  const float sig = __fdividef(1.0f, 1.0f + __expf(-1.702f * g));
-  return g * sig * (u + 1.0f);
+// SwiGLU7 of two (gate, up) pairs at once: min(g, 7) * sigmoid(1.702 min(g, 7)) *
+// (clamp(u, -7, 7) + 1).  sigmoid(1.702 g) = 1 / (1 + 2^(g * -1.702 log2(e))): one scaled
+// 2^x and one reciprocal from the special-function unit, the products and sums as
+// two-lane fp32 (rounded like the scalar sequence (g * sig) * (u + 1)).
+constexpr float SWIGLU7_NEG_ALPHA_LOG2E = -1.702f * 1.44269504088896341f;
+__device__ __forceinline__ uint64_t swiglu7_x2(uint64_t g2, uint64_t u2) {
+  float g0, g1, u0, u1;
+  f2_unpack(g2, g0, g1);
+  f2_unpack(u2, u0, u1);
+  g0 = fminf(g0, 7.0f);
+  g1 = fminf(g1, 7.0f);
+  u0 = fminf(fmaxf(u0, -7.0f), 7.0f);
+  u1 = fminf(fmaxf(u1, -7.0f), 7.0f);
+  const uint64_t gc = f2_pack(g0, g1);
+  float a0, a1;
+  f2_unpack(f2_mul(gc, f2_pack(SWIGLU7_NEG_ALPHA_LOG2E, SWIGLU7_NEG_ALPHA_LOG2E)), a0, a1);
+  float d0, d1;
+  f2_unpack(f2_add(f2_pack(ex2_approx(a0), ex2_approx(a1)), f2_pack(1.0f, 1.0f)), d0, d1);
+  const uint64_t gs = f2_mul(gc, f2_pack(rcp_approx(d0), rcp_approx(d1)));
+  return f2_mul(gs, f2_add(f2_pack(u0, u1), f2_pack(1.0f, 1.0f)));
+}
+
+// 1 / (e4m3(sf) * HIDDEN_GSCALE) for every E4M3 scale byte (0 for sf = 0): the per-block
+// factor of the hidden's quantisation, filled once per CTA into a 128-entry table.
+__device__ __forceinline__ float hidden_inv_scale(uint32_t sf) {
+  return sf ? __fdiv_rn(1.0f, __fmul_rn(e4m3_to_f32(sf), HIDDEN_GSCALE)) : 0.0f;
+}
+
+// NVFP4 quantisation of 16 hidden values (8 pairs) with the static second-level scale,
+// the same results as quant_block16(v, HIDDEN_GSCALE): there the block scale is
+// amax / (6 * HIDDEN_GSCALE), and 6 * HIDDEN_GSCALE rounds to exactly 0.125 in fp32, so the
+// division is the exact amax * 8; the reciprocal comes from the table.
+__device__ __forceinline__ uint32_t quant_hidden16(const uint64_t (&h2)[8], const float* inv_tab, uint32_t out[2]) {
+  float h[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f2_unpack(h2[i], h[2 * i], h[2 * i + 1]);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+  const uint32_t sf = cvt_e4m3(amax * 8.0f);
+  const float inv = inv_tab[sf];
+  const uint64_t inv2 = f2_pack(inv, inv);
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f2_unpack(f2_mul(h2[4 * w + i], inv2), s[2 * i], s[2 * i + 1]);
+    const uint32_t word = cvt_e2m1x8(s[0], s[1], s[2], s[3], s[4], s[5], s[6], s[7]);
+    out[w] = sf ? word : 0u;
+  }
+  return sf;
 }
 
 // Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded before the thread
@@ -160,31 +207,34 @@ __device__ __forceinline__ EpiScalars epi_prefetch(const FfnGemmParams& p, int m
 
 // Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
 // accumulator columns [NCOL*half, NCOL*half + NCOL) already in registers (r), TMEM released,
-// per-tile scalars in v.  stg: this warp's 4 KB store staging (EPI_DOWN).
+// per-tile scalars in v.  stg: this warp's 4 KB store staging (EPI_DOWN); inv_tab: the
+// hidden's reciprocal block scales (EPI_SWIGLU, hidden_inv_scale, in shared memory).
 template <int EPI, int NCOL>
 __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const CUtensorMap* tmC,
                                                    const uint32_t (&r)[NCOL], const EpiScalars& v, int mt, int nt,
-                                                   int m, int q, int half, int lane, uint8_t* stg) {
+                                                   int m, int q, int half, int lane, uint8_t* stg,
+                                                   const float* inv_tab) {
   const int e = v.e;
   const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
   if constexpr (EPI == EPI_SWIGLU) {
-    const float s_gate = v.s0;
-    const float s_up = v.s1;
+    const uint64_t s_gate2 = f2_pack(v.s0, v.s0);
+    const uint64_t s_up2 = f2_pack(v.s1, v.s1);
     const int hid_cols = p.N / 2;
     constexpr int NB = NCOL / 32;            // SwiGLU blocks: 16 gate + 16 up columns -> 16 hidden
     uint32_t words[2 * NB];
     uint32_t sfw = 0;
 #pragma unroll
     for (int c = 0; c < NB; ++c) {
-      float hv[16];
+      uint64_t h2[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float g = __fmul_rn(__uint_as_float(r[c * 32 + i]), s_gate);
-        const float u = __fmul_rn(__uint_as_float(r[c * 32 + 16 + i]), s_up);
-        hv[i] = swiglu7(g, u);
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t* rg = r + c * 32 + 2 * i;
+        const uint64_t g2 = f2_mul(f2_pack(__uint_as_float(rg[0]), __uint_as_float(rg[1])), s_gate2);
+        const uint64_t u2 = f2_mul(f2_pack(__uint_as_float(rg[16]), __uint_as_float(rg[17])), s_up2);
+        h2[i] = swiglu7_x2(g2, u2);
       }
       uint32_t w2[2];
-      const uint32_t sf = quant_block16(hv, HIDDEN_GSCALE, w2);
+      const uint32_t sf = quant_hidden16(h2, inv_tab, w2);
       words[2 * c] = w2[0];
       words[2 * c + 1] = w2[1];
       sfw |= sf << (8 * c);
@@ -200,8 +250,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
     else
       *reinterpret_cast<uint16_t*>(sfd) = (uint16_t)sfw;
   } else if constexpr (EPI == EPI_DOWN) {
-    const float s = v.s0;
-    const float pr = v.pr;
+    const uint64_t s2 = f2_pack(v.s0, v.s0);
+    const uint64_t pr2 = f2_pack(v.pr, v.pr);
     const uint32_t stg_s = smem_u32(stg);
 #pragma unroll
     for (int box = 0; box < 2; ++box) {
@@ -214,8 +264,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int col = box * 64 + c * 8 + 2 * j;
-          const float a = __fmul_rn(__fmul_rn(__uint_as_float(r[col]), s), pr);
-          const float b = __fmul_rn(__fmul_rn(__uint_as_float(r[col + 1]), s), pr);
+          float a, b;   // (acc * s) * prob, rounded per step
+          f2_unpack(f2_mul(f2_mul(f2_pack(__uint_as_float(r[col]), __uint_as_float(r[col + 1])), s2), pr2), a, b);
           __nv_bfloat162 h2 = __floats2bfloat162_rn(a, b);
           w[j] = *reinterpret_cast<uint32_t*>(&h2);
         }
@@ -288,9 +338,11 @@ __global__ void __launch_bounds__(32 * (3 + EPW), 1)
   uint64_t* sff_bar = tfull_bar + 3;               // [STAGES] scale factors of the stage in TMEM
   uint64_t* drain2_bar = sff_bar + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain2_bar + 1);
+  float* sInv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // [128] hidden_inv_scale
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (EPI == EPI_SWIGLU && threadIdx.x < 128) sInv[threadIdx.x] = hidden_inv_scale(threadIdx.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -440,7 +492,7 @@ __global__ void __launch_bounds__(32 * (3 + EPW), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar));
 
-      gemm_epilogue_tile<EPI, NCOL>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, NCOL>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128), sInv);
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();     // stores complete before the CTA exits
@@ -501,9 +553,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
   uint64_t* sff_bar = tfull_bar + 3;               // [STAGES] scale factors of the stage in TMEM (leader's)
   uint64_t* drain2_bar = sff_bar + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain2_bar + 1);
+  float* sInv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // [128] hidden_inv_scale
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (EPI == EPI_SWIGLU && threadIdx.x < 128) sInv[threadIdx.x] = hidden_inv_scale(threadIdx.x);
   const uint32_t crank = cluster_ctarank();
   const bool leader = crank == 0;
 
@@ -671,7 +725,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      gemm_epilogue_tile<EPI, 128>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128));
+      gemm_epilogue_tile<EPI, 128>(p, &tmC, r, sc, mt, nt, m, q, half, lane, sSTG + (warp - 2) * (32 * 128), sInv);
     }
     if constexpr (EPI == EPI_DOWN) {
       if (lane == 0) bulk_wait_all();

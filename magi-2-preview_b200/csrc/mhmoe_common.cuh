@@ -372,6 +372,39 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// ───────────────────────────── two-lane fp32 (sm_100 packed FP32) ─────────────────────────────
+// One instruction for two IEEE round-to-nearest operations (no flush): lane-for-lane the
+// same results as __fmul_rn / __fadd_rn, half the issue slots.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// 2^x and 1/x from the special-function unit (approximate; flush subnormal results to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // ───────────────────────────── NVFP4 conversions ─────────────────────────────
 
 // RNE + saturate of eight fp32 values to E2M1, packed little-endian: value i goes to
@@ -379,8 +412,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
 __device__ __forceinline__ uint32_t cvt_e2m1x8(float a0, float a1, float a2, float a3, float a4, float a5,
                                                float a6, float a7) {
   uint32_t out;
-  asm volatile(
-      "{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
       "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
@@ -394,7 +426,7 @@ __device__ __forceinline__ uint32_t cvt_e2m1x8(float a0, float a1, float a2, flo
 // RNE + saturate (448) of a non-negative fp32 to E4M3; returns the byte.
 __device__ __forceinline__ uint32_t cvt_e4m3(float a) {
   uint16_t out;
-  asm volatile("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(out) : "f"(a), "f"(0.0f));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(out) : "f"(a), "f"(0.0f));
   return out & 0xFFu;
 }
 

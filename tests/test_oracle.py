@@ -126,6 +126,16 @@ def test_block_quant_known_answer():
     np.testing.assert_allclose(nv.dequantize(codes, sf), v)
 
 
+def test_hidden_block_scale_is_amax_times_8():
+    """The gate/up epilogue computes the hidden's block scale as amax * 8: exact because
+    6 * HIDDEN_GLOBAL rounds to 0.125 in fp32, so amax / (6 * g) is a power-of-two scaling."""
+    g = nv.HIDDEN_GLOBAL
+    assert np.float32(np.float32(6.0) * g) == np.float32(0.125)
+    amax = np.random.default_rng(0).uniform(0, 60, 4096).astype(np.float32)
+    amax[:4] = [0.0, 1e-40, 3.4e37, 7.0]
+    np.testing.assert_array_equal((amax / (np.float32(6.0) * g)).astype(np.float32), amax * np.float32(8.0))
+
+
 def test_sf_atom_layout():
     M, K = 256, 128
     sf = np.arange(M * K // 16, dtype=np.int64).reshape(M, K // 16) % 251
