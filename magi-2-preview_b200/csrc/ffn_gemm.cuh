@@ -177,8 +177,8 @@ __device__ __forceinline__ uint32_t quant_hidden16(const uint64_t (&h2)[8], cons
   return sf;
 }
 
-// Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded before the thread
-// waits for the accumulator so their global-memory latency hides under the MMAs.
+// Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded one tile ahead of
+// their use so their global-memory latency hides under the MMAs or the previous epilogue.
 struct EpiScalars {
   float s0, s1, pr;   // SwiGLU: gate / up dequantisation scales; down: scale, prob
   int64_t tok;        // atomic scatter: token of the row
@@ -477,9 +477,14 @@ __global__ void __launch_bounds__(32 * (3 + EPW), 1)
     const int half = (warp - 2) >> 2;       // accumulator columns [NCOL*half, NCOL*half + NCOL)
     const int m = q * 32 + lane;            // tile row owned by this thread
     uint32_t acc_phase = 0;
+    // The per-tile scalars are loaded one tile ahead: their global-memory latency hides under
+    // the current tile's epilogue, which matters when the epilogue is the bottleneck.
+    EpiScalars sc_next{};
+    if (blockIdx.x < total) sc_next = epi_prefetch<EPI>(p, (int)blockIdx.x / n_ntiles, m);
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
-      const EpiScalars sc = epi_prefetch<EPI>(p, mt, m);
+      const EpiScalars sc = sc_next;
+      if (t + (int)gridDim.x < total) sc_next = epi_prefetch<EPI>(p, (t + (int)gridDim.x) / n_ntiles, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
@@ -708,10 +713,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
     const int m = q * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty_bar), 0);
     uint32_t acc_phase = 0;
+    EpiScalars sc_next{};                    // per-tile scalars, loaded one tile ahead
+    if (cluster_id < total) sc_next = epi_prefetch<EPI>(p, 2 * (cluster_id / n_ntiles) + (int)crank, m);
     for (int t = cluster_id; t < total; t += n_clusters) {
       const int pt = t / n_ntiles, nt = t % n_ntiles;
       const int mt = 2 * pt + (int)crank;
-      const EpiScalars sc = epi_prefetch<EPI>(p, mt, m);
+      const EpiScalars sc = sc_next;
+      if (t + n_clusters < total) sc_next = epi_prefetch<EPI>(p, 2 * ((t + n_clusters) / n_ntiles) + (int)crank, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
