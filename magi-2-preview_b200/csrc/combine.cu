@@ -138,46 +138,57 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
               srt[warp]);
 }
 
-// Expert-parallel receiver: key = received record slot src * cap + slot.  The record's sum goes straight into the source rank's return area, row
-// (source's send position of the record) = meta offset + slot, over NVLink; slots past
-// the source's count are skipped.  The last CTA to finish raises the return flag of
-// this rank in every peer (system-scope release after every CTA's stores).
-// bulk != 0: the sum is built in shared memory and sent with one bulk copy per record
-// (dynamic shared memory: COMBINE_WARPS * dh bf16); else stored directly from registers.
+// Expert-parallel receiver: key = received record slot src * cap + slot.  The record's sum
+// goes into the source rank's return area, row (source's send position of the record) =
+// meta offset + slot, over NVLink; slots past the source's count are skipped.  The last CTA
+// to finish raises the return flag of this rank in every peer (system-scope release after
+// every CTA's stores).
+// Work item w -> source (w + me) % n, slot w / n: consecutive warps write to different
+// ranks, so all links carry the returns at once (no rank is the target of everyone).
+// Warps walk the items grid-stride.
+// bulk != 0: each sum is built in one of two shared-memory buffers of the warp and sent
+// with one bulk copy; a buffer is rewritten once its previous copy has been read out
+// (wait_group.read), so a warp keeps a copy in flight while it sums the next record, and
+// waits for completion once, before the flag.  bulk == 0: stored from registers.
 __global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
                                       int dh, const int32_t* __restrict__ tok_rows, int k_fixed, int64_t R,
                                       int64_t P_rows, const EpReturn r, int bulk) {
   __shared__ int srt[COMBINE_WARPS][32];
   extern __shared__ __align__(128) uint8_t stage_raw[];
   const int warp = threadIdx.x >> 5;
-  // work item w -> source (w + me) % n, slot w / n: consecutive warps write to different
-  // ranks, so all links carry the returns at once (no rank is the target of everyone)
-  const int64_t w = (int64_t)blockIdx.x * COMBINE_WARPS + warp;
+  const int lane = threadIdx.x & 31;
   const int64_t slots = (int64_t)r.n * r.cap;
-  if (w < slots && ld_volatile_i32(r.status) == 0) {
+  const int64_t* meta = reinterpret_cast<const int64_t*>(r.local + r.layout.off_meta);
+  int issued = 0;
+  for (int64_t w = (int64_t)blockIdx.x * COMBINE_WARPS + warp; w < slots; w += (int64_t)gridDim.x * COMBINE_WARPS) {
+    if (ld_volatile_i32(r.status) != 0) break;
     const int src = (int)((w + r.me) % r.n);
     const int64_t slot = w / r.n;
     const int64_t key = (int64_t)src * r.cap + slot;
-    const int64_t* meta = reinterpret_cast<const int64_t*>(r.local + r.layout.off_meta);
     const int64_t cnt = meta[2 * src], off = meta[2 * src + 1];
-    if (slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots) {
-      __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
-      if (bulk) {
-        __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(stage_raw) + (size_t)warp * dh;
-        combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, srow, srt[warp]);
-        fence_proxy_async_shared();
+    if (!(slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots)) continue;
+    __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
+    if (bulk) {
+      __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(stage_raw) + ((size_t)warp * 2 + (issued & 1)) * dh;
+      if (issued >= 2) {
+        if (lane == 0) bulk_wait_read_1();      // the copy that last used this buffer has read it
         __syncwarp();
-        if ((threadIdx.x & 31) == 0) {
-          bulk_store(yrow, smem_u32(srow), (uint32_t)dh * 2);
-          bulk_commit();
-          bulk_wait_all();                 // written at the destination before the flag release
-          fence_proxy_async_global();
-        }
-        __syncwarp();
-      } else {
-        combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
       }
+      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, srow, srt[warp]);
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        bulk_store(yrow, smem_u32(srow), (uint32_t)dh * 2);
+        bulk_commit();
+      }
+      ++issued;
+    } else {
+      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
     }
+  }
+  if (bulk && lane == 0 && issued > 0) {
+    bulk_wait_all();                            // written at the destinations before the flag release
+    fence_proxy_async_global();
   }
   if (ep_last_cta(reinterpret_cast<int*>(r.local + r.layout.off_done) + 1) && threadIdx.x == 0) {
     for (int d = 0; d < r.n; ++d)
@@ -222,11 +233,22 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
                                   const int32_t* tok_rows, int k_fixed, int64_t R, int64_t P_rows, const EpReturn& r,
                                   cudaStream_t st) {
   const int64_t keys = (int64_t)r.n * r.cap;
-  const int64_t blocks = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
-  // bulk copies when MHMOE_EP_BULK=1 and a row is at most 8 KB
+  // bulk copies when MHMOE_EP_BULK=1, for rows of at most 8 KB (two 8 KB buffers per warp);
+  // measured slower than stores from registers at 2 GPUs (the default)
   const char* env = std::getenv("MHMOE_EP_BULK");
   const int bulk = (env && env[0] == '1') && dh * 2 <= 8192 ? 1 : 0;
-  const size_t smem = bulk ? (size_t)COMBINE_WARPS * dh * 2 : 0;
+  const size_t smem = bulk ? (size_t)COMBINE_WARPS * 2 * dh * 2 : 0;
+  if (bulk) {
+    static PerDeviceOnce once;
+    const cudaError_t e = once.run([](int) {
+      return cudaFuncSetAttribute(combine_return_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  COMBINE_WARPS * 2 * 8192);
+    });
+    if (e != cudaSuccess) return e;
+  }
+  // warps walk the records grid-stride: a few CTAs per SM keep copies in flight on every link
+  const int64_t want = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
+  const int64_t blocks = std::min<int64_t>(want, (int64_t)(bulk ? 3 : 8) * num_sms());
   combine_return_kernel<<<(unsigned)blocks, COMBINE_WARPS * 32, smem, st>>>(P, pad_of_row, dh, tok_rows, k_fixed, R,
                                                                             P_rows, r, bulk);
   return cudaGetLastError();

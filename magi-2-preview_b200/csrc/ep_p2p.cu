@@ -23,6 +23,8 @@
 // raises after every kernel that reads rx/meta for call t; a destination writes a
 // source's back area for call t+1 only after receiving the source's call-t+1 records,
 // which the source sends after its combine of call t has read back.
+#include <cstdlib>
+
 #include "kernels.cuh"
 
 namespace mhmoe {
@@ -34,9 +36,11 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
                                        int E_loc, const int32_t* __restrict__ send_key,
                                        const int64_t* __restrict__ send_offsets, int n, int me, int64_t cap,
                                        int64_t row_bytes, const EpPeers peers, EpLayout L, uint8_t* local,
-                                       int* status) {
+                                       int* status, int bulk) {
+  extern __shared__ __align__(128) uint8_t rec_stage[];
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
+  int issued = 0;
   // Work item w -> destination d = (w + me) % n, its k = w / n-th row: consecutive warps
   // write to different ranks (and each rank starts at a different one), so every link
   // carries traffic at once instead of all ranks filling one destination after another.
@@ -54,7 +58,17 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
     const int64_t t = send_key[j];                                      // h*S + s
     const int h = (int)(t / S), s = (int)(t % S);
     const int64_t q = (int64_t)s * H + h;                               // quantised token row
-    uint8_t* row = peers.base[d] + L.off_rx + ((int64_t)me * cap + slot) * row_bytes;
+    uint8_t* const dst_row = peers.base[d] + L.off_rx + ((int64_t)me * cap + slot) * row_bytes;
+    // bulk: the record is built in one of the warp's two shared-memory buffers and sent with
+    // one bulk copy (the buffer's previous copy must have read it out first)
+    uint8_t* row = dst_row;
+    if (bulk) {
+      row = rec_stage + ((size_t)(threadIdx.x >> 5) * 2 + (issued & 1)) * row_bytes;
+      if (issued >= 2) {
+        if (lane == 0) bulk_wait_read_1();
+        __syncwarp();
+      }
+    }
     const uint4* src = reinterpret_cast<const uint4*>(xq + q * (dh / 2));
     uint4* dst = reinterpret_cast<uint4*>(row);
     for (int i = lane; i < dh / 32; i += 32) dst[i] = src[i];
@@ -81,6 +95,19 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
     if (lane >= c && lane < K) pairs[lane] = make_int2(-1, 0);
     if (lane == 0)
       *reinterpret_cast<float4*>(row + dh / 2 + dh / 16) = make_float4(xg[q], __int_as_float(c), 0.f, 0.f);
+    if (bulk) {
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        bulk_store(dst_row, smem_u32(row), (uint32_t)row_bytes);
+        bulk_commit();
+      }
+      ++issued;
+    }
+  }
+  if (bulk && lane == 0 && issued > 0) {
+    bulk_wait_all();                 // records written at the destinations before the flag release
+    fence_proxy_async_global();
   }
   if (ep_last_cta(reinterpret_cast<int*>(local + L.off_done)) && threadIdx.x == 0) {
     for (int d = 0; d < n; ++d) {
@@ -135,8 +162,21 @@ cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const 
   const EpLayout L = ep_layout(n, cap, dh, rb);
   const int64_t items = (int64_t)n * cap;
   const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, 4 * num_sms()));
-  ep_send_records_kernel<<<(unsigned)blocks, 256, 0, st>>>(xq, xsf, xg, H, S, dh, idx, probs, K, E, E_loc, send_key,
-                                                           send_offsets, n, me, cap, rb, peers, L, local, status);
+  // bulk copies when MHMOE_EP_BULK=1 (two record buffers per warp, at most 6 KB each); the
+  // default stores from registers measured as fast at 2 GPUs
+  const char* env = std::getenv("MHMOE_EP_BULK");
+  const int bulk = (env && env[0] == '1') && rb <= 6144 ? 1 : 0;
+  const size_t smem = bulk ? (size_t)8 * 2 * rb : 0;
+  if (bulk) {
+    static PerDeviceOnce once;
+    const cudaError_t e = once.run([](int) {
+      return cudaFuncSetAttribute(ep_send_records_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 6144);
+    });
+    if (e != cudaSuccess) return e;
+  }
+  ep_send_records_kernel<<<(unsigned)blocks, 256, smem, st>>>(xq, xsf, xg, H, S, dh, idx, probs, K, E, E_loc,
+                                                              send_key, send_offsets, n, me, cap, rb, peers, L, local,
+                                                              status, bulk);
   return cudaGetLastError();
 }
 

@@ -250,6 +250,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
     else
       *reinterpret_cast<uint16_t*>(sfd) = (uint16_t)sfw;
   } else if constexpr (EPI == EPI_DOWN) {
+    // this warp's 32 rows are all expert padding: nothing reads them, store nothing
+    if (q * 32 >= v.rows) return;
     const uint64_t s2 = f2_pack(v.s0, v.s0);
     const uint64_t pr2 = f2_pack(v.pr, v.pr);
     const uint32_t stg_s = smem_u32(stg);

@@ -61,9 +61,11 @@ __device__ __forceinline__ void warp_quant_row(const __nv_bfloat16* src, int K, 
   }
 }
 
-// Grouped A operand of the gate/up GEMM: one warp per padded row of the expert-grouped
-// row space copies its token's NVFP4 row (per-token quantised x: data, row-major scales,
-// row scale) into place, scales into the SF-atom layout.  Padding rows are zeroed.
+// Grouped A operand of the gate/up GEMM: warps walk the padded rows of the expert-grouped
+// row space (grid-stride, up to the device's tile count: the grid is sized for the rows
+// actually present, not for the host's upper bound); each copies its token's NVFP4 row
+// (per-token quantised x: data, row-major scales, row scale) into place, scales into the
+// SF-atom layout.  Padding rows are zeroed.
 __global__ void group_rows_kernel(const uint8_t* __restrict__ xq, int64_t xq_pitch, const uint8_t* __restrict__ xsf,
                                   int64_t xsf_pitch, const uint8_t* __restrict__ xg, int64_t xg_pitch, int64_t T,
                                   int dh, int H, int E_per_head,
@@ -75,28 +77,30 @@ __global__ void group_rows_kernel(const uint8_t* __restrict__ xq, int64_t xq_pit
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
-  const int64_t prow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int mt = (int)(prow >> 7);
-  if (mt >= cu_tiles[HE]) return;
-  const int m = (int)(prow & 127);
-  int64_t t = -1;
-  if (m < tile_rows[mt]) {
-    const int s = gather_ids[tile_row0[mt] + m];
-    t = (int64_t)s * H + tile_expert[mt] / E_per_head;
-    if (s < 0 || t >= T) {
-      if (lane == 0) record_error(status, MHMOE_ERR_ARGS);
-      t = -1;
+  const int64_t n_rows = (int64_t)cu_tiles[HE] * 128;
+  const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t prow = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); prow < n_rows; prow += stride) {
+    const int mt = (int)(prow >> 7);
+    const int m = (int)(prow & 127);
+    int64_t t = -1;
+    if (m < tile_rows[mt]) {
+      const int s = gather_ids[tile_row0[mt] + m];
+      t = (int64_t)s * H + tile_expert[mt] / E_per_head;
+      if (s < 0 || t >= T) {
+        if (lane == 0) record_error(status, MHMOE_ERR_ARGS);
+        t = -1;
+      }
     }
+    uint4* dst = reinterpret_cast<uint4*>(a_data + prow * (dh / 2));
+    const uint4* src = t >= 0 ? reinterpret_cast<const uint4*>(xq + t * xq_pitch) : nullptr;
+    for (int i = lane; i < dh / 32; i += 32) dst[i] = src ? src[i] : make_uint4(0, 0, 0, 0);
+    const uint32_t* ssrc = t >= 0 ? reinterpret_cast<const uint32_t*>(xsf + t * xsf_pitch) : nullptr;
+    for (int w = lane; w < dh / 64; w += 32) {
+      const uint32_t v = ssrc ? ssrc[w] : 0u;
+      *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)(4 * w), (uint32_t)dh)) = v;
+    }
+    if (lane == 0) a_gscale[prow] = t >= 0 ? *reinterpret_cast<const float*>(xg + t * xg_pitch) : 1.0f;
   }
-  uint4* dst = reinterpret_cast<uint4*>(a_data + prow * (dh / 2));
-  const uint4* src = t >= 0 ? reinterpret_cast<const uint4*>(xq + t * xq_pitch) : nullptr;
-  for (int i = lane; i < dh / 32; i += 32) dst[i] = src ? src[i] : make_uint4(0, 0, 0, 0);
-  const uint32_t* ssrc = t >= 0 ? reinterpret_cast<const uint32_t*>(xsf + t * xsf_pitch) : nullptr;
-  for (int w = lane; w < dh / 64; w += 32) {
-    const uint32_t v = ssrc ? ssrc[w] : 0u;
-    *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)(4 * w), (uint32_t)dh)) = v;
-  }
-  if (lane == 0) a_gscale[prow] = t >= 0 ? *reinterpret_cast<const float*>(xg + t * xg_pitch) : 1.0f;
 }
 
 // Per-token quantisation: row t = s * H + h of x [S, H, dh]; scales row-major [T, dh/16].
@@ -296,7 +300,8 @@ cudaError_t launch_group_rows(const uint8_t* xq, int64_t xq_pitch, const uint8_t
                               const int* tile_expert, const int* tile_row0, const int* tile_rows, uint8_t* a_data,
                               uint8_t* a_sf, float* a_gscale, int* status, cudaStream_t st) {
   const int64_t rows = max_mtiles * 128;
-  MHMOE_LAUNCH_PDL(group_rows_kernel, (unsigned)(rows / 8), 256, 0, st, xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T,
+  const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(rows / 8, (int64_t)16 * num_sms()));
+  MHMOE_LAUNCH_PDL(group_rows_kernel, (unsigned)blocks, 256, 0, st, xq, xq_pitch, xsf, xsf_pitch, xg, xg_pitch, T,
                    dh, H, E_per_head, gather_ids, cu_tiles, HE, tile_expert, tile_row0, tile_rows, a_data, a_sf,
                    a_gscale, status);
   return cudaGetLastError();
