@@ -26,7 +26,8 @@ __global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const 
 }
 
 // Sum of one key's rows (cnt ids at tok_rows[begin..]) into yrow, one warp.
-// srt: this warp's 32-entry shared scratch.
+// srt: this warp's 32-entry shared scratch.  U: row loads issued together.
+template <int U = 8>
 __device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
                                             int dh, const int32_t* __restrict__ tok_rows, int64_t begin, int cnt,
                                             int64_t R, int64_t P_rows, __nv_bfloat16* yrow, int* srt) {
@@ -52,14 +53,14 @@ __device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P,
     for (int j = 0; j < cnt; ++j) nvalid += srt[j] != 0x7fffffff;
     for (int c = lane; c < nvec; c += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j0 = 0; j0 < nvalid; j0 += 8) {
-        // issue up to 8 independent row loads before accumulating (in ascending row order)
-        uint4 u[8];
+      for (int j0 = 0; j0 < nvalid; j0 += U) {
+        // issue up to U independent row loads before accumulating (in ascending row order)
+        uint4 u[U];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj)
+        for (int jj = 0; jj < U; ++jj)
           if (j0 + jj < nvalid) u[jj] = *reinterpret_cast<const uint4*>(P + (int64_t)srt[j0 + jj] * dh + c * 8);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < U; ++jj) {
           if (j0 + jj < nvalid) {
             const uint32_t w[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
 #pragma unroll
@@ -150,17 +151,19 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
 // with one bulk copy; a buffer is rewritten once its previous copy has been read out
 // (wait_group.read), so a warp keeps a copy in flight while it sums the next record, and
 // waits for completion once, before the flag.  bulk == 0: stored from registers.
-__global__ void combine_return_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
-                                      int dh, const int32_t* __restrict__ tok_rows, int k_fixed, int64_t R,
-                                      int64_t P_rows, const EpReturn r, int bulk) {
-  __shared__ int srt[COMBINE_WARPS][32];
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+    combine_return_kernel(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row, int dh,
+                          const int32_t* __restrict__ tok_rows, int k_fixed, int64_t R, int64_t P_rows,
+                          const EpReturn r, int bulk) {
+  __shared__ int srt[WARPS][32];
   extern __shared__ __align__(128) uint8_t stage_raw[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t slots = (int64_t)r.n * r.cap;
   const int64_t* meta = reinterpret_cast<const int64_t*>(r.local + r.layout.off_meta);
   int issued = 0;
-  for (int64_t w = (int64_t)blockIdx.x * COMBINE_WARPS + warp; w < slots; w += (int64_t)gridDim.x * COMBINE_WARPS) {
+  for (int64_t w = (int64_t)blockIdx.x * WARPS + warp; w < slots; w += (int64_t)gridDim.x * WARPS) {
     if (ld_volatile_i32(r.status) != 0) break;
     const int src = (int)((w + r.me) % r.n);
     const int64_t slot = w / r.n;
@@ -241,7 +244,7 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
   if (bulk) {
     static PerDeviceOnce once;
     const cudaError_t e = once.run([](int) {
-      return cudaFuncSetAttribute(combine_return_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      return cudaFuncSetAttribute(combine_return_kernel<COMBINE_WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   COMBINE_WARPS * 2 * 8192);
     });
     if (e != cudaSuccess) return e;
@@ -249,8 +252,8 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
   // warps walk the records grid-stride: a few CTAs per SM keep copies in flight on every link
   const int64_t want = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
   const int64_t blocks = std::min<int64_t>(want, (int64_t)(bulk ? 3 : 8) * num_sms());
-  combine_return_kernel<<<(unsigned)blocks, COMBINE_WARPS * 32, smem, st>>>(P, pad_of_row, dh, tok_rows, k_fixed, R,
-                                                                            P_rows, r, bulk);
+  combine_return_kernel<COMBINE_WARPS><<<(unsigned)blocks, COMBINE_WARPS * 32, smem, st>>>(
+      P, pad_of_row, dh, tok_rows, k_fixed, R, P_rows, r, bulk);
   return cudaGetLastError();
 }
 

@@ -170,13 +170,14 @@ cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const 
   if (bulk) {
     static PerDeviceOnce once;
     const cudaError_t e = once.run([](int) {
-      return cudaFuncSetAttribute(ep_send_records_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 6144);
+      return cudaFuncSetAttribute(ep_send_records_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  8 * 2 * 6144);
     });
     if (e != cudaSuccess) return e;
   }
   ep_send_records_kernel<<<(unsigned)blocks, 256, smem, st>>>(xq, xsf, xg, H, S, dh, idx, probs, K, E, E_loc,
-                                                              send_key, send_offsets, n, me, cap, rb, peers, L, local,
-                                                              status, bulk);
+                                                                     send_key, send_offsets, n, me, cap, rb, peers, L,
+                                                                     local, status, bulk);
   return cudaGetLastError();
 }
 

@@ -122,7 +122,7 @@ __device__ __forceinline__ bool ep_last_cta(int* done) {
 // permute.cu
 // Sort chunks hold at least min_chunk flat entries (256 by default; larger chunks shrink the
 // histogram scratch).
-int sort_chunk_size(int64_t R, int min_chunk = 256);
+int sort_chunk_size(int64_t R, int64_t HE, int min_chunk = 256);
 size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk = 256);
 cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, int S, int K, int E, void* ws,
                                int32_t* gather_ids, float* probs_sorted, int64_t* expert_offsets,

@@ -418,8 +418,12 @@ __global__ void tok_fill_kernel(const int32_t* __restrict__ gather_ids, const in
 
 // Chunk of flat entries per histogram row: 256 entries (8 warp steps in the scatter) up to
 // 2048 chunks, larger chunks beyond that so the histogram stays <= 2048 x H*E ints.
-int sort_chunk_size(int64_t R, int min_chunk) {
-  int64_t c = (R + 2047) / 2048;
+// Entries per chunk: at most ~2048 chunks, and chunks x keys at most 2^21 histogram
+// counters (the column scan reads each counter once per key-warp step; with thousands of
+// keys, as in the production head split's 12 x 256, many small chunks made that scan the
+// slowest step of the sort).
+int sort_chunk_size(int64_t R, int64_t HE, int min_chunk) {
+  int64_t c = std::max<int64_t>((R + 2047) / 2048, (R * std::max<int64_t>(HE, 1) + (1 << 21) - 1) >> 21);
   c = (c + 31) / 32 * 32;
   return (int)std::max<int64_t>(min_chunk, c);
 }
@@ -429,7 +433,7 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
                                int32_t* row_of_flat, int* status, cudaStream_t st, int min_chunk) {
   const int64_t R = (int64_t)H * S * K;
   const int HE = H * E;
-  const int chunk = sort_chunk_size(R, min_chunk);
+  const int chunk = sort_chunk_size(R, HE, min_chunk);
   const int nchunks = (int)((R + chunk - 1) / chunk);
   const int64_t mt = mtiles_upper_bound(R, HE);
   int* hist = static_cast<int*>(ws);
@@ -460,7 +464,7 @@ cudaError_t launch_global_sort(const float* probs, const int64_t* idx, int H, in
 
 size_t global_sort_ws_bytes(int H, int S, int K, int E, int min_chunk) {
   const int64_t R = (int64_t)H * S * K;
-  const int chunk = sort_chunk_size(R, min_chunk);
+  const int chunk = sort_chunk_size(R, (int64_t)H * E, min_chunk);
   const int64_t nchunks = (R + chunk - 1) / chunk;
   const int64_t mt = mtiles_upper_bound(R, (int64_t)H * E);
   return ((size_t)(nchunks + 2) * (size_t)(H * E) + 1 + 3 * (size_t)mt) * sizeof(int) + 256;

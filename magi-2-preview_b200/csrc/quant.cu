@@ -225,6 +225,82 @@ __global__ void __launch_bounds__(256, MAXNB <= 3 ? 4 : 2)
   }
 }
 
+// The same fused quantise + group for short head rows (dh = 16 * LPK: 256 or 512): LPK
+// lanes per key, one 16-element block per lane, 32 / LPK keys per warp, so every lane has a
+// block (the warp-pair kernel above leaves most lanes idle at dh = 256).  Same op sequence
+// and outputs.  Lanes of a warp loop over the largest destination count of its keys, so the
+// shuffles always see the whole warp.
+template <int LPK>
+__global__ void __launch_bounds__(256)
+    quant_scatter_short_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx_s, int64_t sx_h, int S, int H,
+                               const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
+                               int k_fixed, int64_t R, const int32_t* __restrict__ pad_of_row, int64_t rows,
+                               uint8_t* __restrict__ a_data, uint8_t* __restrict__ a_sf, float* __restrict__ a_gscale,
+                               int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int dh = 16 * LPK;
+  constexpr int KPW = 32 / LPK;                                  // keys per warp
+  const int lane = threadIdx.x & 31;
+  const int sl = lane % LPK;                                     // block of this lane
+  const int gbase = lane - sl;                                   // first lane of this key's group
+  const int64_t key = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * KPW + lane / LPK;
+  const bool live = key < (int64_t)H * S;
+  const int64_t h = live ? key / S : 0, s = live ? key % S : 0;
+  int64_t begin = 0;
+  int cnt = 0;
+  if (live) {
+    if (tok_offsets) {
+      begin = tok_offsets[key];
+      cnt = tok_offsets[key + 1] - (int)begin;
+    } else {
+      begin = key * k_fixed;
+      cnt = k_fixed;
+    }
+  }
+  float f[16];
+  if (live) {
+    const __nv_bfloat16* src = x + s * sx_s + h * sx_h + 16 * sl;
+    load8_bf16(src, f);
+    load8_bf16(src + 8, f + 8);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) f[j] = 0.f;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(f[j]));
+#pragma unroll
+  for (int o = LPK / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float g = amax > 0.f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+  uint32_t codes[2];
+  uint32_t sfw = quant_block16(f, g, codes);
+  // lane 4c collects the scales of lanes 4c..4c+3 (bytes 0..3 of the chunk's word)
+  sfw |= __shfl_down_sync(0xffffffffu, sfw, 1) << 8;
+  sfw |= __shfl_down_sync(0xffffffffu, sfw, 2) << 16;
+  int maxcnt = cnt;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) maxcnt = max(maxcnt, __shfl_xor_sync(0xffffffffu, maxcnt, o));
+  for (int j0 = 0; j0 < maxcnt; j0 += LPK) {
+    int64_t mine = -1;                                           // padded row of destination j0 + sl
+    if (j0 + sl < cnt) {
+      const int r = tok_rows[begin + j0 + sl];
+      const int32_t pr = r >= 0 && r < R ? pad_of_row[r] : -1;
+      if (pr >= 0 && pr < rows) mine = pr;
+      else record_error(status, MHMOE_ERR_ARGS);
+    }
+    const int n = min(LPK, maxcnt - j0);
+    for (int j = 0; j < n; ++j) {
+      const int64_t prow = __shfl_sync(0xffffffffu, mine, gbase + j);
+      if (j0 + j >= cnt || prow < 0) continue;
+      *reinterpret_cast<uint2*>(a_data + prow * (int64_t)(dh / 2) + 8 * sl) = make_uint2(codes[0], codes[1]);
+      if ((sl & 3) == 0)
+        *reinterpret_cast<uint32_t*>(a_sf + sf_atom_offset((uint64_t)prow, (uint32_t)sl, (uint32_t)dh)) = sfw;
+      if (sl == 0) a_gscale[prow] = g;
+    }
+  }
+}
+
 __global__ void quantize_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t pitch, int64_t M, int K,
                                      uint8_t* __restrict__ data, uint8_t* __restrict__ sf,
                                      float* __restrict__ gscale) {
@@ -321,6 +397,18 @@ cudaError_t launch_quant_scatter(const __nv_bfloat16* x, int64_t sx_s, int64_t s
                                  const int32_t* pad_of_row, int64_t rows, uint8_t* a_data, uint8_t* a_sf,
                                  float* a_gscale, int* status, cudaStream_t st) {
   const int64_t keys = (int64_t)S * H;
+  if (dh == 256 || dh == 512) {                          // short rows: LPK lanes per key, 8 warps per block
+    const int lpk = dh / 16;
+    const int64_t warps = (keys + 32 / lpk - 1) / (32 / lpk);
+    const unsigned g2 = (unsigned)((warps + 7) / 8);
+    if (lpk == 16)
+      MHMOE_LAUNCH_PDL(quant_scatter_short_kernel<16>, g2, 256, 0, st, x, sx_s, sx_h, S, H, tok_rows, tok_offsets,
+                       k_fixed, R, pad_of_row, rows, a_data, a_sf, a_gscale, status);
+    else
+      MHMOE_LAUNCH_PDL(quant_scatter_short_kernel<32>, g2, 256, 0, st, x, sx_s, sx_h, S, H, tok_rows, tok_offsets,
+                       k_fixed, R, pad_of_row, rows, a_data, a_sf, a_gscale, status);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((keys + 3) / 4);      // 4 keys (warp pairs) per 256-thread block
   const int nb = (dh / 16 + 63) / 64;                    // blocks per lane
 #define MHMOE_QS(NB)                                                                                       \

@@ -325,7 +325,7 @@ def _ep_timeout_ns() -> int:
 
 def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn,
                       group, stage_events=None, comm_events=None, slot: int = 0,
-                      out: torch.Tensor | None = None) -> torch.Tensor:
+                      out: torch.Tensor | None = None, ffn_after=None, gemms_done=None) -> torch.Tensor:
     """Token -> expert EP forward with the exchange fused into the kernels (peer memory).
 
     Same records and result as ``ep_moe_layer``; the record kernel stores into the
@@ -333,7 +333,10 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     source's buffer, each followed by a device-side arrival flag, so there is no count
     exchange and no host synchronisation.  comm_events (optional, 4): around the record
     send + wait, and around the wait for the returns.  slot: which exchange buffer
-    (pipeline chunk) to use; out: optional [S, H, dh] bf16 destination.
+    (pipeline chunk) to use; out: optional [S, H, dh] bf16 destination.  ffn_after: an event
+    the expert GEMMs wait for (the previous chunk's GEMMs); gemms_done: an event recorded once
+    this call's expert GEMMs are done (its returns still move); with stage_events, their
+    fourth event marks that point instead.
     """
     be = CudaBackend()
     L = _lib.lib()
@@ -383,11 +386,16 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
     R = slots * K
     ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, slots, 1, dh, gu.d_expert, E_loc)), dtype=torch.uint8,
                      device=dev)
+    if ffn_after is not None:
+        torch.cuda.current_stream(dev).wait_event(ffn_after)
+    evs = list(stage_events) if stage_events else None
+    if gemms_done is not None and not evs:
+        evs = [None, None, None, gemms_done, None]   # recorded after the down GEMM
     _lib.check(L.mhmoe_ep_ffn_return(px.local, ep, px.me, px.cap, dh, gu.d_expert, K, E_loc, R, lg.data_ptr(),
                                      lps.data_ptr(), loffs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(),
                                      gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(),
                                      dn.gscale.data_ptr(), linv.data_ptr(), ws.data_ptr(), px.peer_bases, status, 0,
-                                     _events(stage_events), st), "ep_ffn_return")
+                                     _events(evs), st), "ep_ffn_return")
     if comm_events:
         comm_events[2].record()
     _lib.check(L.mhmoe_ep_wait(px.local, 1, ep, px.epoch, timeout, status, st), "ep_wait(returns)")
@@ -414,9 +422,11 @@ def ep_moe_layer_peer_pipelined(x_heads: torch.Tensor, probs: torch.Tensor, idx:
                                 gu, dn, group, chunks: int = 2, stage_events=None,
                                 comm_events=None) -> torch.Tensor:
     """The peer-memory EP layer over ``chunks`` token chunks, each on its own stream with its
-    own exchange buffer: one chunk's returns (link-bound) overlap the next chunk's expert
-    GEMMs (tensor-bound).  Each token's result is computed exactly as unchunked (the same
-    records, experts and summation order).  Events, if given, time chunk 0.
+    own exchange buffer.  Chunk c's expert GEMMs start after chunk c-1's (an event after its
+    down GEMM), so the GEMMs do not compete for the SMs, while chunk c-1's returns and chunk
+    c+1's records (link-bound) could move beside them.  Each token's result is
+    computed exactly as unchunked (the same records, experts and summation order).  Events,
+    if given, time chunk 0.
     """
     S, H, dh = x_heads.shape
     if chunks <= 1 or S < 2 * chunks:
@@ -431,16 +441,20 @@ def ep_moe_layer_peer_pipelined(x_heads: torch.Tensor, probs: torch.Tensor, idx:
     ready.record(main)
     bounds = [(S * c) // chunks for c in range(chunks + 1)]
     done = []
+    prev_gemms = None
     for c in range(chunks):
         a, b = bounds[c], bounds[c + 1]
         s = streams[c]
         s.wait_event(ready)
+        ev_stage = stage_events if c == 0 else None
+        gemms = None if ev_stage else torch.cuda.Event()
         with torch.cuda.stream(s):
             ep_moe_layer_peer(x_heads[a:b], probs[:, a:b].contiguous(), idx[:, a:b].contiguous(), num_experts, gu,
-                              dn, group, stage_events if c == 0 else None, comm_events if c == 0 else None,
-                              slot=c, out=y[a:b])
+                              dn, group, ev_stage, comm_events if c == 0 else None, slot=c, out=y[a:b],
+                              ffn_after=prev_gemms, gemms_done=gemms)
             ev = torch.cuda.Event()
             ev.record(s)
+        prev_gemms = ev_stage[3] if ev_stage else gemms
         done.append(ev)
     for ev in done:
         main.wait_event(ev)

@@ -140,6 +140,8 @@ def _events(evs):
     import ctypes
     arr = (ctypes.c_void_p * 5)()
     for i, e in enumerate(evs):
+        if e is None:         # no event at this stage boundary
+            continue
         e.record()            # torch creates the CUDA event lazily; the library re-records it in place
         arr[i] = e.cuda_event
     return ctypes.cast(arr, ctypes.c_void_p)
