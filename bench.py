@@ -306,7 +306,11 @@ def step_ep(m, x, ev):
     probs, idx = m._route(x_heads)
     ev[1].record()
     gu, dn = m.packed_weights()
-    if ep_transport(m) == "peer":
+    if ep_transport(m) == "copy":
+        from flash_mh_moe.ep import ep_moe_layer_copy
+        y = ep_moe_layer_copy(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, chunks=ep_chunks(2),
+                              stage_events=ev[2:7], comm_events=ev[8:12])
+    elif ep_transport(m) == "peer":
         y = ep_moe_layer_peer_pipelined(x_heads, probs, idx, m.num_experts, gu, dn, m.ep_group, chunks=ep_chunks(),
                                         stage_events=ev[2:7], comm_events=ev[8:12])
     else:

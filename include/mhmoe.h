@@ -285,6 +285,26 @@ MHMOE_API int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const
                                     const int32_t* send_key, const int64_t* send_offsets, int n_ranks, int rank,
                                     int64_t cap, void* const* peer_bases, int* dev_status, void* stream);
 
+/* Copy-engine transport, step 1: the same records as mhmoe_ep_send_records, written into this
+ * rank's own slab (one cap-row slab per destination, send order within it) with the
+ * per-destination {count, offset} beside it; nothing crosses NVLink and no flag is raised.
+ * Replaces, like mhmoe_ep_send_records, the dispatch all_to_all of
+ * inference/model/magi2_preview.py:3277-3299. */
+MHMOE_API int mhmoe_ep_stage_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                                     const int64_t* topk_idx, const float* topk_probs, int K, int E,
+                                     const int32_t* send_key, const int64_t* send_offsets, int n_ranks, int rank,
+                                     int64_t cap, void* const* peer_bases, int* dev_status, void* stream);
+
+/* Copy-engine transport, step 2: one cudaMemcpyAsync per peer on `stream` (whole cap-row
+ * slabs: the counts stay on the device) and then this rank's flag of `kind` in every peer.
+ * kind 0: staged records -> each destination's receive area (+ their counts);
+ * kind 1: staged sums (mhmoe_ep_ffn_stage) -> each source's return area, row d*cap + slot.
+ * Only copies and a one-warp flag kernel: run it on a stream of its own to overlap the
+ * transfer with compute.  Replaces the all_to_all calls of
+ * inference/model/magi2_preview.py:3277-3327. */
+MHMOE_API int mhmoe_ep_push(void* local_base, int kind, int n_ranks, int rank, int64_t cap, int dh, int K,
+                            void* const* peer_bases, void* stream);
+
 /* Wait on the device until every source's flag of `kind` (0 records, 1 returns) in this
  * rank's buffer reaches `epoch`; gives up after timeout_ns with MHMOE_ERR_PEER in
  * dev_status.  Later work on the stream runs after it. */
@@ -307,6 +327,17 @@ MHMOE_API int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank,
                                   const float* dn_gscale, const int32_t* row_of_flat, void* workspace,
                                   void* const* peer_bases, int* dev_status, uint64_t timeout_ns,
                                   void* const* stage_events, void* stream);
+
+/* Copy-engine transport, step 3: mhmoe_ep_ffn_return with each record's sum written into this
+ * rank's own stage area (source s's records at s*cap + slot) instead of the source's memory;
+ * mhmoe_ep_push(kind 1) moves them.  Same arguments. */
+MHMOE_API int mhmoe_ep_ffn_stage(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K,
+                                 int E_loc, int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                                 const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                                 const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf,
+                                 const float* dn_gscale, const int32_t* row_of_flat, void* workspace,
+                                 void* const* peer_bases, int* dev_status, uint64_t timeout_ns,
+                                 void* const* stage_events, void* stream);
 
 /* ───────────────────────── MoE layer around the routed core ───────────────────────── */
 

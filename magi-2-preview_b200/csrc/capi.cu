@@ -462,10 +462,10 @@ static bool fill_peers(void* const* peer_bases, int n, EpPeers* peers) {
   return true;
 }
 
-int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
-                          const int64_t* idx, const float* probs, int K, int E, const int32_t* send_key,
-                          const int64_t* send_offsets, int n_ranks, int rank, int64_t cap, void* const* peer_bases,
-                          int* dev_status, void* stream) {
+static int ep_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh, const int64_t* idx,
+                      const float* probs, int K, int E, const int32_t* send_key, const int64_t* send_offsets,
+                      int n_ranks, int rank, int64_t cap, void* const* peer_bases, int* dev_status, void* stream,
+                      bool stage) {
   MHMOE_REQUIRE(xq && xsf && xg && idx && probs && send_key && send_offsets && peer_bases && dev_status);
   MHMOE_REQUIRE(H > 0 && S >= 0 && dh > 0 && dh % 256 == 0 && K > 0 && K <= 16 && E > 0);
   MHMOE_REQUIRE(n_ranks > 0 && n_ranks <= EP_MAX_RANKS && rank >= 0 && rank < n_ranks && (H * E) % n_ranks == 0);
@@ -475,8 +475,38 @@ int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg
   MHMOE_REQUIRE(fill_peers(peer_bases, n_ranks, &peers));
   const cudaError_t e = launch_ep_send_records(xq, xsf, xg, H, S, dh, idx, probs, K, E, H * E / n_ranks, send_key,
                                                send_offsets, n_ranks, rank, cap, peers, peers.base[rank], dev_status,
-                                               static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_send_records");
+                                               static_cast<cudaStream_t>(stream), stage);
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, stage ? "ep_stage_records" : "ep_send_records");
+}
+
+int mhmoe_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                          const int64_t* idx, const float* probs, int K, int E, const int32_t* send_key,
+                          const int64_t* send_offsets, int n_ranks, int rank, int64_t cap, void* const* peer_bases,
+                          int* dev_status, void* stream) {
+  return ep_records(xq, xsf, xg, H, S, dh, idx, probs, K, E, send_key, send_offsets, n_ranks, rank, cap, peer_bases,
+                    dev_status, stream, false);
+}
+
+int mhmoe_ep_stage_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
+                           const int64_t* idx, const float* probs, int K, int E, const int32_t* send_key,
+                           const int64_t* send_offsets, int n_ranks, int rank, int64_t cap, void* const* peer_bases,
+                           int* dev_status, void* stream) {
+  return ep_records(xq, xsf, xg, H, S, dh, idx, probs, K, E, send_key, send_offsets, n_ranks, rank, cap, peer_bases,
+                    dev_status, stream, true);
+}
+
+int mhmoe_ep_push(void* local_base, int kind, int n_ranks, int rank, int64_t cap, int dh, int K,
+                  void* const* peer_bases, void* stream) {
+  MHMOE_REQUIRE(local_base && peer_bases && (kind == 0 || kind == 1));
+  MHMOE_REQUIRE(n_ranks > 0 && n_ranks <= EP_MAX_RANKS && rank >= 0 && rank < n_ranks && cap >= 0);
+  MHMOE_REQUIRE(dh > 0 && dh % 256 == 0 && K > 0 && K <= 16);
+  MHMOE_CHECK_ARCH();
+  EpPeers peers;
+  MHMOE_REQUIRE(fill_peers(peer_bases, n_ranks, &peers));
+  MHMOE_REQUIRE(peers.base[rank] == local_base);
+  const cudaError_t e = launch_ep_push(static_cast<uint8_t*>(local_base), kind, n_ranks, rank, cap, dh, K, peers,
+                                       static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_push");
 }
 
 int mhmoe_ep_wait(const void* local_base, int kind, int n_ranks, int epoch, uint64_t timeout_ns, int* dev_status,
@@ -500,12 +530,12 @@ int mhmoe_ep_unpack_slots(const void* local_base, int n_ranks, int64_t cap, int 
   return e == cudaSuccess ? MHMOE_OK : fail_cuda(e, "ep_unpack_slots");
 }
 
-int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K, int E_loc,
-                        int64_t R, const int32_t* gather_ids, const float* probs_sorted,
-                        const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
-                        const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
-                        const int32_t* row_of_flat, void* workspace, void* const* peer_bases, int* dev_status,
-                        uint64_t timeout_ns, void* const* stage_events, void* stream) {
+static int ep_ffn(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K, int E_loc, int64_t R,
+                  const int32_t* gather_ids, const float* probs_sorted, const int64_t* expert_offsets,
+                  const uint8_t* gu_data, const uint8_t* gu_sf, const float* gu_gscale, const uint8_t* dn_data,
+                  const uint8_t* dn_sf, const float* dn_gscale, const int32_t* row_of_flat, void* workspace,
+                  void* const* peer_bases, int* dev_status, uint64_t timeout_ns, void* const* stage_events,
+                  void* stream, int stage) {
   MHMOE_REQUIRE(local_base && gather_ids && probs_sorted && expert_offsets && gu_data && gu_sf && gu_gscale &&
                 dn_data && dn_sf && dn_gscale && row_of_flat && workspace && peer_bases && dev_status);
   MHMOE_REQUIRE(n_ranks > 0 && n_ranks <= EP_MAX_RANKS && rank >= 0 && rank < n_ranks && cap > 0);
@@ -524,6 +554,7 @@ int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t c
   ret.n = n_ranks;
   ret.me = rank;
   ret.status = dev_status;
+  ret.stage = stage;
   const uint8_t* rx = ret.local + ret.layout.off_rx;
   const int64_t T = (int64_t)n_ranks * cap;
   MHMOE_REQUIRE(T <= 0x7fffffff);
@@ -533,9 +564,31 @@ int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t c
                            nullptr, dh, dh, dev_status, timeout_ns,
                            reinterpret_cast<cudaEvent_t const*>(stage_events), static_cast<cudaStream_t>(stream), &ce,
                            rx, rx + dh / 2, rx + dh / 2 + dh / 16, rb, rb, rb, &ret);
-  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, "ep_ffn_return");
+  if (rc == MHMOE_ERR_LAUNCH) return fail_cuda(ce, stage ? "ep_ffn_stage" : "ep_ffn_return");
   if (rc == MHMOE_ERR_DRIVER) g_last_error = "cuTensorMapEncodeTiled failed";
   return rc;
+}
+
+int mhmoe_ep_ffn_return(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K, int E_loc,
+                        int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                        const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                        const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                        const int32_t* row_of_flat, void* workspace, void* const* peer_bases, int* dev_status,
+                        uint64_t timeout_ns, void* const* stage_events, void* stream) {
+  return ep_ffn(local_base, n_ranks, rank, cap, dh, de, K, E_loc, R, gather_ids, probs_sorted, expert_offsets, gu_data,
+                gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, row_of_flat, workspace, peer_bases, dev_status, timeout_ns,
+                stage_events, stream, 0);
+}
+
+int mhmoe_ep_ffn_stage(const void* local_base, int n_ranks, int rank, int64_t cap, int dh, int de, int K, int E_loc,
+                       int64_t R, const int32_t* gather_ids, const float* probs_sorted,
+                       const int64_t* expert_offsets, const uint8_t* gu_data, const uint8_t* gu_sf,
+                       const float* gu_gscale, const uint8_t* dn_data, const uint8_t* dn_sf, const float* dn_gscale,
+                       const int32_t* row_of_flat, void* workspace, void* const* peer_bases, int* dev_status,
+                       uint64_t timeout_ns, void* const* stage_events, void* stream) {
+  return ep_ffn(local_base, n_ranks, rank, cap, dh, de, K, E_loc, R, gather_ids, probs_sorted, expert_offsets, gu_data,
+                gu_sf, gu_gscale, dn_data, dn_sf, dn_gscale, row_of_flat, workspace, peer_bases, dev_status, timeout_ns,
+                stage_events, stream, 1);
 }
 
 }  // extern "C"

@@ -170,7 +170,9 @@ __global__ void __launch_bounds__(WARPS * 32)
     const int64_t key = (int64_t)src * r.cap + slot;
     const int64_t cnt = meta[2 * src], off = meta[2 * src + 1];
     if (!(slot < cnt && cnt <= r.cap && off >= 0 && off + cnt <= slots)) continue;
-    __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
+    __nv_bfloat16* yrow =
+        r.stage ? reinterpret_cast<__nv_bfloat16*>(r.local + r.layout.off_stage) + key * dh   // copied by the push
+                : reinterpret_cast<__nv_bfloat16*>(r.peers.base[src] + r.layout.off_back) + (off + slot) * dh;
     if (bulk) {
       __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(stage_raw) + ((size_t)warp * 2 + (issued & 1)) * dh;
       if (issued >= 2) {
@@ -193,6 +195,7 @@ __global__ void __launch_bounds__(WARPS * 32)
     bulk_wait_all();                            // written at the destinations before the flag release
     fence_proxy_async_global();
   }
+  if (r.stage) return;                          // the push raises the flags after its copies
   if (ep_last_cta(reinterpret_cast<int*>(r.local + r.layout.off_done) + 1) && threadIdx.x == 0) {
     for (int d = 0; d < r.n; ++d)
       red_release_sys_add(reinterpret_cast<int*>(r.peers.base[d] + r.layout.off_flags) + 32 + r.me, 1);

@@ -36,7 +36,7 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
                                        int E_loc, const int32_t* __restrict__ send_key,
                                        const int64_t* __restrict__ send_offsets, int n, int me, int64_t cap,
                                        int64_t row_bytes, const EpPeers peers, EpLayout L, uint8_t* local,
-                                       int* status, int bulk) {
+                                       int* status, int bulk, int stage) {
   extern __shared__ __align__(128) uint8_t rec_stage[];
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
@@ -58,7 +58,9 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
     const int64_t t = send_key[j];                                      // h*S + s
     const int h = (int)(t / S), s = (int)(t % S);
     const int64_t q = (int64_t)s * H + h;                               // quantised token row
-    uint8_t* const dst_row = peers.base[d] + L.off_rx + ((int64_t)me * cap + slot) * row_bytes;
+    // stage: into this rank's slab for destination d (moved later by the copy engines)
+    uint8_t* const dst_row = stage ? local + L.off_slab + ((int64_t)d * cap + slot) * row_bytes
+                                   : peers.base[d] + L.off_rx + ((int64_t)me * cap + slot) * row_bytes;
     // bulk: the record is built in one of the warp's two shared-memory buffers and sent with
     // one bulk copy (the buffer's previous copy must have read it out first)
     uint8_t* row = dst_row;
@@ -109,6 +111,15 @@ __global__ void ep_send_records_kernel(const uint8_t* __restrict__ xq, const uin
     bulk_wait_all();                 // records written at the destinations before the flag release
     fence_proxy_async_global();
   }
+  if (stage) {                        // counts for the copies; no flags (the push raises them)
+    if (blockIdx.x == 0)
+      for (int d = threadIdx.x; d < n; d += blockDim.x) {
+        int64_t* mo = reinterpret_cast<int64_t*>(local + L.off_mout) + 2 * d;
+        mo[0] = send_offsets[d + 1] - send_offsets[d];
+        mo[1] = send_offsets[d];
+      }
+    return;
+  }
   if (ep_last_cta(reinterpret_cast<int*>(local + L.off_done)) && threadIdx.x == 0) {
     for (int d = 0; d < n; ++d) {
       int64_t* meta = reinterpret_cast<int64_t*>(peers.base[d] + L.off_meta) + 2 * me;
@@ -157,7 +168,7 @@ __global__ void ep_unpack_slots_kernel(const uint8_t* __restrict__ local, EpLayo
 cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
                                    const int64_t* idx, const float* probs, int K, int E, int E_loc,
                                    const int32_t* send_key, const int64_t* send_offsets, int n, int me, int64_t cap,
-                                   const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st) {
+                                   const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st, bool stage) {
   const int64_t rb = ep_row_bytes(dh, K);
   const EpLayout L = ep_layout(n, cap, dh, rb);
   const int64_t items = (int64_t)n * cap;
@@ -177,7 +188,44 @@ cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const 
   }
   ep_send_records_kernel<<<(unsigned)blocks, 256, smem, st>>>(xq, xsf, xg, H, S, dh, idx, probs, K, E, E_loc,
                                                                      send_key, send_offsets, n, me, cap, rb, peers, L,
-                                                                     local, status, bulk);
+                                                                     local, status, bulk, stage ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// Raise this rank's flag of `kind` in every peer (after the copies before it in the stream).
+__global__ void ep_flag_kernel(const EpPeers peers, int64_t off_flags, int kind, int n, int me) {
+  const int d = threadIdx.x;
+  if (d >= n) return;
+  __threadfence_system();
+  red_release_sys_add(reinterpret_cast<int*>(peers.base[d] + off_flags) + 32 * kind + me, 1);
+}
+
+// Copy-engine transport: one cudaMemcpyAsync per peer (whole slabs: the counts live on the
+// device, the receiver reads them from the copied meta), then the flags.
+//   kind 0: slab[d] -> d's rx[me], mout[d] -> d's meta[me]
+//   kind 1: stage[s] -> s's back[me]
+cudaError_t launch_ep_push(uint8_t* local, int kind, int n, int me, int64_t cap, int dh, int K, const EpPeers& peers,
+                           cudaStream_t st) {
+  const int64_t rb = ep_row_bytes(dh, K);
+  const EpLayout L = ep_layout(n, cap, dh, rb);
+  for (int i = 0; i < n; ++i) {
+    const int d = (me + 1 + i) % n;        // every rank starts with a different peer
+    cudaError_t e;
+    if (kind == 0) {
+      e = cudaMemcpyAsync(peers.base[d] + L.off_rx + (int64_t)me * cap * rb, local + L.off_slab + (int64_t)d * cap * rb,
+                          (size_t)(cap * rb), cudaMemcpyDeviceToDevice, st);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(peers.base[d] + L.off_meta + 16 * me, local + L.off_mout + 16 * d, 16,
+                            cudaMemcpyDeviceToDevice, st);
+    } else {
+      const int64_t rowb = (int64_t)dh * 2;
+      e = cudaMemcpyAsync(peers.base[d] + L.off_back + (int64_t)me * cap * rowb,
+                          local + L.off_stage + (int64_t)d * cap * rowb, (size_t)(cap * rowb), cudaMemcpyDeviceToDevice,
+                          st);
+    }
+    if (e != cudaSuccess) return e;
+  }
+  ep_flag_kernel<<<1, 32, 0, st>>>(peers, L.off_flags, kind, n, me);
   return cudaGetLastError();
 }
 

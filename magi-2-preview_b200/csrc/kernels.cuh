@@ -73,10 +73,15 @@ struct PerDeviceOnce {
 //                         offset of this rank's group in s's send order}
 //   done   int32 [8]      this rank's own last-CTA counters
 //   rx     [n][cap][row_bytes]  records from source s at slot s*cap + j
-//   back   [n*cap][dh] bf16     returned sums, row = this rank's send position
+//   back   [n*cap][dh] bf16     returned sums: row = this rank's send position (stores
+//                               from the kernels), or d*cap + slot (copy-engine transport)
+//   copy-engine transport only (local staging, moved by cudaMemcpyAsync):
+//   slab   [n][cap][row_bytes]  this rank's records for destination d at d*cap + slot
+//   mout   int64 [32][2]        {count, send offset} for destination d
+//   stage  [n][cap][dh] bf16    sums of the records received from source s at s*cap + slot
 constexpr int EP_MAX_RANKS = 32;
 struct EpLayout {
-  int64_t off_flags, off_meta, off_done, off_rx, off_back, bytes;
+  int64_t off_flags, off_meta, off_done, off_rx, off_back, off_slab, off_mout, off_stage, bytes;
 };
 inline EpLayout ep_layout(int n, int64_t cap, int dh, int64_t row_bytes) {
   auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
@@ -86,7 +91,10 @@ inline EpLayout ep_layout(int n, int64_t cap, int dh, int64_t row_bytes) {
   L.off_done = 768;
   L.off_rx = 1024;
   L.off_back = L.off_rx + up((int64_t)n * cap * row_bytes);
-  L.bytes = L.off_back + up((int64_t)n * cap * dh * 2);
+  L.off_slab = L.off_back + up((int64_t)n * cap * dh * 2);
+  L.off_mout = L.off_slab + up((int64_t)n * cap * row_bytes);
+  L.off_stage = L.off_mout + 512;
+  L.bytes = L.off_stage + up((int64_t)n * cap * dh * 2);
   return L;
 }
 struct EpPeers {
@@ -99,6 +107,7 @@ struct EpReturn {
   int64_t cap;
   int n, me;
   int* status;
+  int stage;         // 1: sums into this rank's stage area (copy-engine transport), no flags
 };
 
 // Last-CTA detection: every thread's stores (peer stores included) are ordered at system
@@ -198,7 +207,10 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
 cudaError_t launch_ep_send_records(const uint8_t* xq, const uint8_t* xsf, const float* xg, int H, int S, int dh,
                                    const int64_t* idx, const float* probs, int K, int E, int E_loc,
                                    const int32_t* send_key, const int64_t* send_offsets, int n, int me, int64_t cap,
-                                   const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st);
+                                   const EpPeers& peers, uint8_t* local, int* status, cudaStream_t st,
+                                   bool stage = false);
+cudaError_t launch_ep_push(uint8_t* local, int kind, int n, int me, int64_t cap, int dh, int K, const EpPeers& peers,
+                           cudaStream_t st);
 cudaError_t launch_ep_wait(const uint8_t* local, int kind, int n, int target, uint64_t timeout_ns, int* status,
                            cudaStream_t st);
 cudaError_t launch_ep_unpack_slots(const uint8_t* local, int n, int64_t cap, int dh, int K, int E_loc,

@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_rmsnorm": (i32, [vp, i64, vp, vp, i32, i64, i32, f32, f32, vp, i64, vp]),
     "mhmoe_ffn_nvfp4_atomic": (i32, [vp, i64, i64, i32, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                      vp, vp, i64, i64, vp, u64, vp, vp]),
+    "mhmoe_ep_stage_records": (i32, [vp, vp, vp, i32, i32, i32, vp, vp, i32, i32, vp, vp, i32, i32, i64, vp, vp,
+                                      vp]),
+    "mhmoe_ep_push": (i32, [vp, i32, i32, i32, i64, i32, i32, vp, vp]),
     "mhmoe_ep_sym_bytes": (sz, [i32, i64, i32, i32]),
     "mhmoe_ep_sym_offsets": (i32, [i32, i64, i32, i32, vp]),
     "mhmoe_ep_sym_alloc": (i32, [sz, vp, vp]),
@@ -64,6 +67,8 @@ SIGNATURES: dict[str, tuple] = {
     "mhmoe_ep_unpack_slots": (i32, [vp, i32, i64, i32, i32, i32, vp, vp, vp, vp]),
     "mhmoe_ep_ffn_return": (i32, [vp, i32, i32, i64, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                   vp, vp, vp, vp, u64, vp, vp]),
+    "mhmoe_ep_ffn_stage": (i32, [vp, i32, i32, i64, i32, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
+                                 vp, vp, vp, vp, u64, vp, vp]),
 }
 
 _lib = None

@@ -286,6 +286,7 @@ class PeerExchange:
         _lib.check(L.mhmoe_ep_sym_offsets(self.n, self.cap, dh, K, offs), "ep_sym_offsets")
         self.off_back = int(offs[3])
         self.epoch = 0
+        self.push_done = [None, None]   # copy-engine transport: last push of records / returns
         dist.barrier(group=group)
 
     @classmethod
@@ -411,11 +412,11 @@ def ep_moe_layer_peer(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Ten
 _side_streams: dict = {}
 
 
-def ep_chunks() -> int:
-    """Pipeline depth of the peer-memory EP layer (``MHMOE_EP_CHUNKS``, default 1: at 2 GPUs two
-    chunks measured slower, 15.7 M vs 17.3 M tokens/s)."""
+def ep_chunks(default: int = 1) -> int:
+    """Pipeline depth of the EP layer (``MHMOE_EP_CHUNKS``; default 1 for the kernel-store
+    transport, where two chunks measured slower at 2 GPUs, and 2 for the copy-engine one)."""
     import os
-    return max(1, int(os.environ.get("MHMOE_EP_CHUNKS", "1")))
+    return max(1, int(os.environ.get("MHMOE_EP_CHUNKS", str(default))))
 
 
 def ep_moe_layer_peer_pipelined(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int,
@@ -461,12 +462,124 @@ def ep_moe_layer_peer_pipelined(x_heads: torch.Tensor, probs: torch.Tensor, idx:
     return y
 
 
+_copy_streams: dict = {}
+
+
+def ep_moe_layer_copy(x_heads: torch.Tensor, probs: torch.Tensor, idx: torch.Tensor, num_experts: int, gu, dn,
+                      group, chunks: int = 2, stage_events=None, comm_events=None) -> torch.Tensor:
+    """Token -> expert EP forward whose NVLink transfers run on the copy engines.
+
+    The same records, experts and summation order as ``ep_moe_layer_peer`` (so the same
+    result), but the kernels only write this rank's own memory: each chunk's records are
+    staged into per-destination slabs and moved with one ``cudaMemcpyAsync`` per peer on a
+    copy stream (``mhmoe_ep_push``), and each chunk's per-record sums are staged per source and
+    pushed back the same way.  The SMs stay on compute while the copy engines move data, so
+    with ``chunks`` >= 2 chunk c+1's records and chunk c-1's returns cross the links during
+    chunk c's expert GEMMs.  Whole cap-row slabs move (the counts stay on the device), so at
+    n ranks a record slab carries ~(1 - (1 - 1/n)^K) rows in use per row moved.
+    stage_events (7, optional) time chunk 0; comm_events (4): around chunk 0's record wait
+    and return wait.
+    """
+    be = CudaBackend()
+    L = _lib.lib()
+    ep = dist.get_world_size(group)
+    S, H, dh = x_heads.shape
+    K = idx.shape[-1]
+    E = int(num_experts)
+    HE = H * E
+    if HE % ep:
+        raise ValueError(f"H*E ({HE}) must be divisible by ep_size ({ep})")
+    E_loc = HE // ep
+    dev = x_heads.device
+    chunks = max(1, min(int(chunks), S))
+    main = torch.cuda.current_stream(dev)
+    if dev.index not in _copy_streams:
+        _copy_streams[dev.index] = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+    rec_stream, ret_stream = _copy_streams[dev.index]
+    st = _lib.stream_ptr(dev)
+    status = _lib.device_status(dev).data_ptr()
+    timeout = _ep_timeout_ns()
+    y = torch.empty(S, H, dh, dtype=torch.bfloat16, device=dev)
+    bounds = [(S * c) // chunks for c in range(chunks + 1)]
+    state = []
+    # 1. every chunk's records: quantise, group by destination, stage, push on the copy stream
+    for c in range(chunks):
+        a, b = bounds[c], bounds[c + 1]
+        T = H * (b - a)
+        px = PeerExchange.get(group, dev, T, dh, K, 16 + c)
+        px.epoch += 1
+        if px.push_done[0] is not None:
+            main.wait_event(px.push_done[0])          # the previous push has read the slabs
+        idx_c, probs_c = idx[:, a:b].contiguous(), probs[:, a:b].contiguous()
+        xq, xsf, xg = be.quant_tokens(x_heads[a:b])
+        dest = be.dest(idx_c, E, ep)
+        zeros = torch.zeros(1, T, ep, dtype=torch.float32, device=dev)
+        send_key, _, send_offs, send_slot = be.sort(zeros, dest.view(1, T, ep), ep)
+        _lib.check(L.mhmoe_ep_stage_records(xq.data_ptr(), xsf.data_ptr(), xg.data_ptr(), H, b - a, dh,
+                                            idx_c.data_ptr(), probs_c.data_ptr(), K, E, send_key.data_ptr(),
+                                            send_offs.data_ptr(), ep, px.me, px.cap, px.peer_bases, status, st),
+                   "ep_stage_records")
+        staged = torch.cuda.Event()
+        staged.record(main)
+        rec_stream.wait_event(staged)
+        _lib.check(L.mhmoe_ep_push(px.local, 0, ep, px.me, px.cap, dh, K, px.peer_bases,
+                                   rec_stream.cuda_stream), "ep_push(records)")
+        px.push_done[0] = torch.cuda.Event()
+        px.push_done[0].record(rec_stream)
+        state.append((px, a, b, T, send_offs, send_slot))
+    # 2. every chunk: wait for its records, expert FFN, stage the sums, push them back
+    for c, (px, a, b, T, send_offs, send_slot) in enumerate(state):
+        if comm_events and c == 0:
+            comm_events[0].record()
+        _lib.check(L.mhmoe_ep_wait(px.local, 0, ep, px.epoch, timeout, status, st), "ep_wait(records)")
+        if comm_events and c == 0:
+            comm_events[1].record()
+        slots = ep * px.cap
+        lidx = torch.empty(slots, K, dtype=torch.int64, device=dev)
+        lprobs = torch.empty(slots, K, dtype=torch.float32, device=dev)
+        _lib.check(L.mhmoe_ep_unpack_slots(px.local, ep, px.cap, dh, K, E_loc, lidx.data_ptr(), lprobs.data_ptr(),
+                                           status, st), "ep_unpack_slots")
+        lg, lps, loffs, linv = be.sort(lprobs.view(1, slots, K), lidx.view(1, slots, K), E_loc)
+        R = slots * K
+        ws = torch.empty(max(1, L.mhmoe_ffn_workspace_bytes(R, slots, 1, dh, gu.d_expert, E_loc)),
+                         dtype=torch.uint8, device=dev)
+        if px.push_done[1] is not None:
+            main.wait_event(px.push_done[1])          # the previous push has read the stage area
+        _lib.check(L.mhmoe_ep_ffn_stage(px.local, ep, px.me, px.cap, dh, gu.d_expert, K, E_loc, R, lg.data_ptr(),
+                                        lps.data_ptr(), loffs.data_ptr(), gu.data.data_ptr(), gu.sf.data_ptr(),
+                                        gu.gscale.data_ptr(), dn.data.data_ptr(), dn.sf.data_ptr(),
+                                        dn.gscale.data_ptr(), linv.data_ptr(), ws.data_ptr(), px.peer_bases, status,
+                                        0, _events(stage_events if c == 0 else None), st), "ep_ffn_stage")
+        summed = torch.cuda.Event()
+        summed.record(main)
+        ret_stream.wait_event(summed)
+        _lib.check(L.mhmoe_ep_push(px.local, 1, ep, px.me, px.cap, dh, K, px.peer_bases,
+                                   ret_stream.cuda_stream), "ep_push(returns)")
+        px.push_done[1] = torch.cuda.Event()
+        px.push_done[1].record(ret_stream)
+    LAST_STATS.update(transport="copy")
+    # 3. every chunk: wait for the returns, sum each (head, token)'s rows in ascending rank order
+    for c, (px, a, b, T, send_offs, send_slot) in enumerate(state):
+        if comm_events and c == 0:
+            comm_events[2].record()
+        _lib.check(L.mhmoe_ep_wait(px.local, 1, ep, px.epoch, timeout, status, st), "ep_wait(returns)")
+        if comm_events and c == 0:
+            comm_events[3].record()
+        # send row j of destination d landed at back row d*cap + (j - send_offsets[d])
+        d = torch.arange(T * ep, device=dev) % ep
+        j = send_slot.to(torch.int64)
+        back_rows = torch.where(j >= 0, d * px.cap + j - send_offs[d], -1).to(torch.int32)
+        _lib.check(L.mhmoe_combine(px.local + px.off_back, ep * px.cap, None, dh, b - a, H, back_rows.data_ptr(), None,
+                                   ep, ep * px.cap, y[a:b].data_ptr(), y.stride(0), y.stride(1), st), "combine")
+    return y
+
+
 def ep_transport(module) -> str:
-    """'peer' (default when every rank has its own GPU of one node) or 'nccl'
-    (``MHMOE_EP_TRANSPORT=nccl`` or peer buffers unavailable)."""
+    """'peer' (kernels store over NVLink; the default), 'copy' (copy engines move staged
+    slabs, ``MHMOE_EP_TRANSPORT=copy``) or 'nccl' (``MHMOE_EP_TRANSPORT=nccl``)."""
     import os
     want = getattr(module, "ep_transport", None) or os.environ.get("MHMOE_EP_TRANSPORT", "peer")
-    return "nccl" if want == "nccl" else "peer"
+    return want if want in ("nccl", "copy") else "peer"
 
 
 def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None, comm_events=None) -> torch.Tensor:
@@ -476,6 +589,9 @@ def ep_moe_forward(module, x_heads: torch.Tensor, stage_events=None, comm_events
     if gu.d_head != x_heads.shape[-1]:
         raise NotImplementedError(f"expert parallelism takes d_head multiples of 256 (got {x_heads.shape[-1]}): "
                                   "its records carry the unpadded NVFP4 rows")
+    if ep_transport(module) == "copy":
+        return ep_moe_layer_copy(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
+                                 chunks=ep_chunks(2), stage_events=stage_events, comm_events=comm_events)
     if ep_transport(module) == "peer":
         return ep_moe_layer_peer_pipelined(x_heads, probs, idx, module.num_experts, gu, dn, module.ep_group,
                                            chunks=ep_chunks(), stage_events=stage_events, comm_events=comm_events)

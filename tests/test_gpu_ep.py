@@ -65,7 +65,7 @@ def _worker(rank, world, port, q, transport, chunks):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("transport,chunks", [("peer", 1), ("peer", 2), ("nccl", 1)])
+@pytest.mark.parametrize("transport,chunks", [("peer", 1), ("peer", 2), ("copy", 1), ("copy", 2), ("nccl", 1)])
 def test_ep_module_matches_single_gpu(transport, chunks):
     world = 2
     ctx = mp.get_context("spawn")
