@@ -463,9 +463,11 @@ def _e2e(args, m, x_host, dev, world):
     loop feeds the layer); serial = copy in, compute, copy out on one stream."""
     import torch
     import torch.distributed as dist
+    from flash_mh_moe.host import near_gpu, pinned_like
     comp = torch.cuda.current_stream(dev)
-    xh = [x_host.pin_memory(), x_host.clone().pin_memory()]
-    yh = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    # pinned buffers on the GPU's NUMA node, as a serving loop would hold them
+    xh = [pinned_like(x_host, dev, copy=True), pinned_like(x_host.clone(), dev, copy=True)]
+    yh = [pinned_like(x_host, dev) for _ in range(2)]
     xd = [torch.empty_like(x_host, device=dev) for _ in range(2)]
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
@@ -496,21 +498,22 @@ def _e2e(args, m, x_host, dev, world):
 
     out = []
     for fn in (overlapped, serial):
-        fn(max(1, args.warmup))
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(comp)
-        fn(args.steps)
-        e1.record(comp)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        out.append(ms)
+        with near_gpu(dev):
+            fn(max(1, args.warmup))
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(comp)
+            fn(args.steps)
+            e1.record(comp)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            out.append(ms)
     return out[0], out[1]
 
 
