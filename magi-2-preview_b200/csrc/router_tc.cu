@@ -214,9 +214,11 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
       const float* lb = p.logit_bias ? p.logit_bias + (int64_t)h * p.E : nullptr;
       uint32_t r[32];
-      // pass 1: row max over this group's columns (and the optional logits output)
+      // pass 1: row max over this group's columns (and the optional logits output); the
+      // sigmoid scores need neither, so without a logits output the pass is skipped
       float mx = -INFINITY;
-      for (int c = c0; c < c1; ++c) {
+      const bool pass1 = p.score_func == 0 || p.logits;
+      for (int c = c0; pass1 && c < c1; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
@@ -229,9 +231,11 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           }
         }
       }
-      red_max[g * 128 + m] = mx;
-      if (!quarter_sync()) break;
-      mx = fmaxf(fmaxf(red_max[m], red_max[128 + m]), fmaxf(red_max[256 + m], red_max[384 + m]));
+      if (p.score_func == 0) {
+        red_max[g * 128 + m] = mx;
+        if (!quarter_sync()) break;
+        mx = fmaxf(fmaxf(red_max[m], red_max[128 + m]), fmaxf(red_max[256 + m], red_max[384 + m]));
+      }
       // pass 2: softmax denominator, ascending experts within the group, groups in order
       float sum = 0.f;
       if (p.score_func == 0) {

@@ -57,7 +57,8 @@ def test_global_sort_matches_reference(name):
     np.testing.assert_array_equal(to_np(o), d[name + "/expert_offsets"])
 
 
-@pytest.mark.parametrize("H,S,K,E", [(1, 16384, 8, 128), (12, 2048, 6, 256), (1, 1, 2, 8), (3, 777, 5, 40)])
+@pytest.mark.parametrize("H,S,K,E", [(1, 16384, 8, 128), (12, 2048, 6, 256), (1, 1, 2, 8), (3, 777, 5, 40),
+                                     (2, 16000, 8, 120), (1, 32768, 8, 256), (12, 16384, 6, 256)])
 def test_global_sort_large_matches_oracle(H, S, K, E):
     from flash_mh_moe.route import flash_mh_moe_global_sort_with_inverse
     rng = np.random.default_rng(H * 1000 + S)
