@@ -239,7 +239,8 @@ int ffn_nvfp4(const __nv_bfloat16* x, int64_t sx_s, int64_t sx_h, int S, int H, 
   }
   // Local tokens are quantised once and written straight into their grouped rows; tokens
   // that arrive pre-quantised (expert-parallel receive) are grouped by copy.
-  const bool fused = !prequant && dh <= quant_scatter_max_dh();
+  const char* qenv = std::getenv("MHMOE_QUANT_FUSED");
+  const bool fused = !prequant && dh <= quant_scatter_max_dh() && !(qenv && qenv[0] == '0');
   // (the A operand's padding rows stay unwritten: each row's GEMM results depend on that row
   // alone, and nothing reads a padding row's hidden or partial output)
   MHMOE_TRY(launch_pad_rows(w.cu_tiles, HE, max_mt, w.tile_row0, w.tile_rows, w.pad_of_row, st));

@@ -86,3 +86,21 @@ def test_ffn_deterministic_and_empty(scatter, monkeypatch):
                          torch.empty(0, device="cuda"), torch.zeros(E + 1, dtype=torch.int64, device="cuda"),
                          *args[4:])
     assert torch.count_nonzero(z) == 0
+
+
+@pytest.mark.parametrize("S,H,dh,de,E,K,seed,skew", [CASES[2], CASES[4], CASES[5]])
+def test_ffn_quantise_paths_identical(S, H, dh, de, E, K, seed, skew, monkeypatch):
+    """The A operand is the same bytes whichever way it is built: quantise + scatter in one
+    kernel (the default for local tokens), or per-token quantisation then grouping by row
+    (the path of expert-parallel records; MHMOE_QUANT_FUSED=0 selects it for local tokens)."""
+    from flash_mh_moe import flash_mh_moe_fwd
+    x, gate, Wg, Wu, Wd = seeded_moe(S, H, dh, de, E, K, seed)
+    gids, ps, offs = _route(x, gate, S, H, dh, E, K, skew)
+    args = (bf16_tensor(x.reshape(S, H, dh)), torch.from_numpy(gids).cuda(), torch.from_numpy(ps).cuda(),
+            torch.from_numpy(offs).cuda(), bf16_tensor(Wg), bf16_tensor(Wu), bf16_tensor(Wd))
+    outs = []
+    for fused in ("1", "0"):
+        monkeypatch.setenv("MHMOE_QUANT_FUSED", fused)
+        outs.append(flash_mh_moe_fwd(*args))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
