@@ -26,13 +26,17 @@ __global__ void pad_rows_kernel(const int* __restrict__ cu_tiles, int HE, const 
 }
 
 // Sum of one key's rows (cnt ids at tok_rows[begin..]) into yrow, one warp.
-// srt: this warp's 32-entry shared scratch.  U: row loads issued together.
+// srt: this warp's 32-entry shared scratch.  U: row loads issued together.  The warp sums
+// the 8-column groups part, part + parts, ... (lane-strided): parts > 1 lets several warps
+// share one key's row when there are few keys.
 template <int U = 8>
 __device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P, const int32_t* __restrict__ pad_of_row,
                                             int dh, const int32_t* __restrict__ tok_rows, int64_t begin, int cnt,
-                                            int64_t R, int64_t P_rows, __nv_bfloat16* yrow, int* srt) {
+                                            int64_t R, int64_t P_rows, __nv_bfloat16* yrow, int* srt, int part = 0,
+                                            int parts = 1) {
   const int lane = threadIdx.x & 31;
   const int nvec = dh / 8;
+  const int c_first = part * 32 + lane, c_step = 32 * parts;
   if (cnt <= 32) {
     // rank sort of <= 32 row ids (ascending; ids are distinct)
     int r = lane < cnt ? tok_rows[begin + lane] : 0x7fffffff;
@@ -51,7 +55,7 @@ __device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P,
     __syncwarp();
     int nvalid = 0;
     for (int j = 0; j < cnt; ++j) nvalid += srt[j] != 0x7fffffff;
-    for (int c = lane; c < nvec; c += 32) {
+    for (int c = c_first; c < nvec; c += c_step) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int j0 = 0; j0 < nvalid; j0 += U) {
         // issue up to U independent row loads before accumulating (in ascending row order)
@@ -82,7 +86,7 @@ __device__ __forceinline__ void combine_key(const __nv_bfloat16* __restrict__ P,
     __syncwarp();
   } else {
     // rare long lists: ascending selection, one row at a time
-    for (int c = lane; c < nvec; c += 32) {
+    for (int c = c_first; c < nvec; c += c_step) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       int last = -1;
       for (int it = 0; it < cnt; ++it) {
@@ -118,12 +122,14 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
                                int S, int H,
                                const int32_t* __restrict__ tok_rows, const int32_t* __restrict__ tok_offsets,
                                int k_fixed, int64_t R, int64_t P_rows, __nv_bfloat16* __restrict__ y, int64_t sy_s,
-                               int64_t sy_h) {
+                               int64_t sy_h, int parts) {
   pdl_wait();
   pdl_trigger();
   __shared__ int srt[COMBINE_WARPS][32];
   const int warp = threadIdx.x >> 5;
-  const int64_t key = (int64_t)blockIdx.x * COMBINE_WARPS + warp;   // key = h * S + s
+  const int64_t w = (int64_t)blockIdx.x * COMBINE_WARPS + warp;
+  const int64_t key = w / parts;                                      // key = h * S + s
+  const int part = (int)(w % parts);
   if (key >= (int64_t)H * S) return;
   const int h = (int)(key / S), s = (int)(key % S);
   int64_t begin;
@@ -136,7 +142,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ P, const int32_
     cnt = k_fixed;
   }
   combine_key(P, pad_of_row, dh, tok_rows, begin, cnt, R, P_rows, y + (int64_t)s * sy_s + (int64_t)h * sy_h,
-              srt[warp]);
+              srt[warp], part, parts);
 }
 
 // Expert-parallel receiver: key = received record slot src * cap + slot.  The record's sum
@@ -230,8 +236,14 @@ cudaError_t launch_combine(const __nv_bfloat16* P, const int32_t* pad_of_row, in
                            const int32_t* tok_rows, const int32_t* tok_offsets, int k_fixed, int64_t R,
                            int64_t P_rows, __nv_bfloat16* y, int64_t sy_s, int64_t sy_h, cudaStream_t st) {
   const int64_t keys = (int64_t)H * S;
-  MHMOE_LAUNCH_PDL(combine_kernel, (unsigned)((keys + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st,
-                   P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h);
+  // few keys (small batches): several warps per key, each a share of the row's columns, so
+  // that the launch still has ~16 warps per SM
+  const int64_t want = 16 * (int64_t)num_sms();
+  const int parts = (int)std::max<int64_t>(1, std::min<int64_t>((want + keys - 1) / std::max<int64_t>(keys, 1),
+                                                                 (dh / 8 + 31) / 32));
+  const int64_t warps = keys * parts;
+  MHMOE_LAUNCH_PDL(combine_kernel, (unsigned)((warps + COMBINE_WARPS - 1) / COMBINE_WARPS), COMBINE_WARPS * 32, 0, st,
+                   P, pad_of_row, dh, S, H, tok_rows, tok_offsets, k_fixed, R, P_rows, y, sy_s, sy_h, parts);
   return cudaGetLastError();
 }
 

@@ -7,9 +7,11 @@
 // At 256 tokens the tensor-core router runs two CTAs, each streaming 128 x dh of x and
 // the whole gate through one SM (~50 us).  Here a cluster of 8 CTAs splits the reduction
 // dimension of a 32-token tile: CTA r accumulates x[:, r*dh/8 : (r+1)*dh/8] against the
-// same slice of the gate planes, on the CUDA cores, as exact products (bf16 x bf16 plane
-// values) added in fp32 — the arithmetic of the tensor-core router — with the slice
-// streamed through shared memory by asynchronous copies.  The leader CTA sums
+// same slice of the gate, on the CUDA cores, as an fp32 FMA chain in ascending k of the
+// bf16 x values and the fp32 gate (rebuilt exactly from its bf16 planes: their sum is the
+// fp32 weight, each partial sum representable), with the slice streamed through shared
+// memory by asynchronous copies.  One FMA per (token, expert, k) whatever the number of
+// planes; the result is the fp32 dot product to rounding.  The leader CTA sums
 // the eight partial tiles through distributed shared memory in rank order (run-to-run
 // identical), then scores and selects, one warp per token.  No scratch memory.
 #include "kernels.cuh"
@@ -133,23 +135,26 @@ __global__ void __cluster_dims__(RS_SPLIT, 1, 1) __launch_bounds__(RS_THREADS, 1
           xa[i][2 * q + 1] = f.y;
         }
       }
-      for (int p = 0; p < nsplit; ++p) {
 #pragma unroll
-        for (int j = 0; j < EP; ++j) {
-          const int e = lane + 32 * j;
-          if (e >= E) continue;
+      for (int j = 0; j < EP; ++j) {
+        const int e = lane + 32 * j;
+        if (e >= E) continue;
+        // the fp32 gate weights k .. k+7 of expert e: the sum of its planes, plane by plane
+        float gv[8];
+        for (int p = 0; p < nsplit; ++p) {
           const uint4 raw = *reinterpret_cast<const uint4*>(buf + (size_t)(RS_TOK + p * EPAD + e) * pitch + kk);
           const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float2 g = __bfloat1622float2(r2[q]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              acc[i][j] = __fmaf_rn(xa[i][2 * q], g.x, acc[i][j]);
-              acc[i][j] = __fmaf_rn(xa[i][2 * q + 1], g.y, acc[i][j]);
-            }
+            gv[2 * q] = p ? __fadd_rn(gv[2 * q], g.x) : g.x;
+            gv[2 * q + 1] = p ? __fadd_rn(gv[2 * q + 1], g.y) : g.y;
           }
         }
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i][j] = __fmaf_rn(xa[i][q], gv[q], acc[i][j]);
       }
     }
     __syncthreads();                        // this buffer is refilled by chunk c + 2
