@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(WARPS * 32)
         if (lane == 0) bulk_wait_read_1();      // the copy that last used this buffer has read it
         __syncwarp();
       }
-      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, srow, srt[warp]);
+      combine_key<4>(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, srow, srt[warp]);
       fence_proxy_async_shared();
       __syncwarp();
       if (lane == 0) {
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(WARPS * 32)
       }
       ++issued;
     } else {
-      combine_key(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
+      combine_key<4>(P, pad_of_row, dh, tok_rows, key * k_fixed, k_fixed, R, P_rows, yrow, srt[warp]);
     }
   }
   if (bulk && lane == 0 && issued > 0) {
@@ -266,7 +266,7 @@ cudaError_t launch_combine_return(const __nv_bfloat16* P, const int32_t* pad_of_
   }
   // warps walk the records grid-stride: a few CTAs per SM keep copies in flight on every link
   const int64_t want = std::max<int64_t>(1, (keys + COMBINE_WARPS - 1) / COMBINE_WARPS);
-  const int64_t blocks = std::min<int64_t>(want, (int64_t)(bulk ? 3 : 8) * num_sms());
+  const int64_t blocks = std::min<int64_t>(want, (int64_t)(bulk ? 3 : 16) * num_sms());
   combine_return_kernel<COMBINE_WARPS><<<(unsigned)blocks, COMBINE_WARPS * 32, smem, st>>>(
       P, pad_of_row, dh, tok_rows, k_fixed, R, P_rows, r, bulk);
   return cudaGetLastError();
