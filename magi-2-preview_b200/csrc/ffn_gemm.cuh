@@ -76,8 +76,9 @@ __host__ __device__ constexpr int gemm_stages(int epi) { return epi == EPI_DOWN 
 __host__ __device__ constexpr int gemm_epi_warps(int epi, int K) {
   return epi == EPI_SWIGLU && K <= 1024 ? 16 : 8;
 }
+__host__ __device__ constexpr int gemm_stg_bytes(int epi) { return epi == EPI_DOWN ? GEMM_STG_BYTES : 0; }
 __host__ __device__ constexpr int gemm_smem_bytes(int epi) {
-  return gemm_stages(epi) * GEMM_STAGE_BYTES + (epi == EPI_DOWN ? GEMM_STG_BYTES : 0) + GEMM_MISC_BYTES + 1024;
+  return gemm_stages(epi) * GEMM_STAGE_BYTES + gemm_stg_bytes(epi) + GEMM_MISC_BYTES + 1024;
 }
 
 // CTA-pair variant (cluster of 2, cta_group::2): M = 256 rows per pair (128 per CTA), each
@@ -177,33 +178,73 @@ __device__ __forceinline__ uint32_t quant_hidden16(const uint64_t (&h2)[8], cons
   return sf;
 }
 
-// Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded one tile ahead of
-// their use so their global-memory latency hides under the MMAs or the previous epilogue.
+// Per-tile scalars of one epilogue thread (row m of m-tile mt), loaded ahead of their use
+// in two steps so that no load waits on another inside the tile loop: the loads indexed by
+// the tile alone (expert, row scale, row range) two tiles ahead, the loads indexed by
+// those (per-expert scales, probabilities) one tile ahead.  Products are formed at use.
+struct EpiIndex {
+  float gr;           // SwiGLU: second-level scale of the A row
+  int e, rows, row0;  // expert; down: valid rows and first sorted row of the tile
+};
 struct EpiScalars {
-  float s0, s1, pr;   // SwiGLU: gate / up dequantisation scales; down: scale, prob
+  float gr, s0, s1;   // SwiGLU: row scale, gate / up weight scales; down: s0 = weight scale
+  float pr;           // down: routing probability of the row
   int64_t tok;        // atomic scatter: token of the row
   int e, rows;
 };
 
 template <int EPI>
-__device__ __forceinline__ EpiScalars epi_prefetch(const FfnGemmParams& p, int mt, int m) {
-  EpiScalars v{};
-  v.e = p.tile_expert[mt];
-  const size_t prow = (size_t)mt * GEMM_BM + m;
+__device__ __forceinline__ EpiIndex epi_load_index(const FfnGemmParams& p, int mt, int m) {
+  EpiIndex x{};
+  x.e = p.tile_expert[mt];
   if constexpr (EPI == EPI_SWIGLU) {
-    const float gr = p.row_gscale[prow];
-    v.s0 = __fmul_rn(gr, p.gs_gate[v.e]);
-    v.s1 = __fmul_rn(gr, p.gs_up[v.e]);
+    x.gr = p.row_gscale[(size_t)mt * GEMM_BM + m];
   } else if constexpr (EPI == EPI_DOWN || EPI == EPI_DOWN_ATOMIC) {
-    v.rows = p.tile_rows[mt];
-    v.s0 = __fmul_rn(HIDDEN_GSCALE, p.gs_down[v.e]);
-    const bool valid = m < v.rows;
-    const int64_t srow = (int64_t)p.tile_row0[mt] + m;
+    x.rows = p.tile_rows[mt];
+    x.row0 = p.tile_row0[mt];
+  }
+  return x;
+}
+
+template <int EPI>
+__device__ __forceinline__ EpiScalars epi_load_scalars(const FfnGemmParams& p, const EpiIndex& x, int m) {
+  EpiScalars v{};
+  v.e = x.e;
+  if constexpr (EPI == EPI_SWIGLU) {
+    v.gr = x.gr;
+    v.s0 = p.gs_gate[x.e];
+    v.s1 = p.gs_up[x.e];
+  } else if constexpr (EPI == EPI_DOWN || EPI == EPI_DOWN_ATOMIC) {
+    v.rows = x.rows;
+    v.s0 = p.gs_down[x.e];
+    const bool valid = m < x.rows;
+    const int64_t srow = (int64_t)x.row0 + m;
     v.pr = valid ? p.probs[srow] : 0.0f;
     if constexpr (EPI == EPI_DOWN_ATOMIC) v.tok = valid ? p.gather_ids[srow] : 0;
   }
   return v;
 }
+
+// The two-step prefetch of one epilogue thread over the tiles t0, t0 + step, ... (m-tile of
+// tile t: mtile_of(t)).  next() returns the scalars of the current tile and issues the loads
+// of the following two.
+template <int EPI, class MtileOf>
+struct EpiPrefetch {
+  EpiScalars cur;
+  EpiIndex ahead;     // index loads of the tile after the next
+  __device__ __forceinline__ EpiPrefetch(const FfnGemmParams& p, MtileOf mtile_of, int t0, int step, int total, int m) {
+    cur = EpiScalars{};
+    ahead = EpiIndex{};
+    if (t0 < total) cur = epi_load_scalars<EPI>(p, epi_load_index<EPI>(p, mtile_of(t0), m), m);
+    if (t0 + step < total) ahead = epi_load_index<EPI>(p, mtile_of(t0 + step), m);
+  }
+  __device__ __forceinline__ EpiScalars next(const FfnGemmParams& p, MtileOf mtile_of, int t, int step, int total, int m) {
+    const EpiScalars v = cur;
+    if (t + step < total) cur = epi_load_scalars<EPI>(p, ahead, m);
+    if (t + 2 * step < total) ahead = epi_load_index<EPI>(p, mtile_of(t + 2 * step), m);
+    return v;
+  }
+};
 
 // Fused epilogue of one 128 x 256 accumulator tile for one thread: row m of m-tile mt,
 // accumulator columns [NCOL*half, NCOL*half + NCOL) already in registers (r), TMEM released,
@@ -217,8 +258,9 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
   const int e = v.e;
   const size_t prow = (size_t)mt * GEMM_BM + m;   // padded row
   if constexpr (EPI == EPI_SWIGLU) {
-    const uint64_t s_gate2 = f2_pack(v.s0, v.s0);
-    const uint64_t s_up2 = f2_pack(v.s1, v.s1);
+    const float s_gate = __fmul_rn(v.gr, v.s0), s_up = __fmul_rn(v.gr, v.s1);
+    const uint64_t s_gate2 = f2_pack(s_gate, s_gate);
+    const uint64_t s_up2 = f2_pack(s_up, s_up);
     const int hid_cols = p.N / 2;
     constexpr int NB = NCOL / 32;            // SwiGLU blocks: 16 gate + 16 up columns -> 16 hidden
     uint32_t words[2 * NB];
@@ -252,7 +294,8 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
   } else if constexpr (EPI == EPI_DOWN) {
     // this warp's 32 rows are all expert padding: nothing reads them, store nothing
     if (q * 32 >= v.rows) return;
-    const uint64_t s2 = f2_pack(v.s0, v.s0);
+    const float s = __fmul_rn(HIDDEN_GSCALE, v.s0);
+    const uint64_t s2 = f2_pack(s, s);
     const uint64_t pr2 = f2_pack(v.pr, v.pr);
     const uint32_t stg_s = smem_u32(stg);
 #pragma unroll
@@ -283,7 +326,7 @@ __device__ __forceinline__ void gemm_epilogue_tile(const FfnGemmParams& p, const
     }
   } else if constexpr (EPI == EPI_DOWN_ATOMIC) {
     if (m < v.rows) {
-      const float s = v.s0;
+      const float s = __fmul_rn(HIDDEN_GSCALE, v.s0);
       const float pr = v.pr;
       const int64_t tok = v.tok;
       const int h = e / p.experts_per_head;
@@ -330,8 +373,8 @@ __global__ void __launch_bounds__(32 * (3 + EPW), 1)
   uint8_t* sB = sA + STAGES * GEMM_A_BYTES;
   uint8_t* sSFA = sB + STAGES * GEMM_B_BYTES;
   uint8_t* sSFB = sSFA + STAGES * GEMM_SFA_BYTES;
-  uint8_t* sSTG = sSFB + STAGES * GEMM_SFB_BYTES;                     // EPI_DOWN staging (1024-aligned)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sSTG + (EPI == EPI_DOWN ? GEMM_STG_BYTES : 0));
+  uint8_t* sSTG = sSFB + STAGES * GEMM_SFB_BYTES;                     // store staging (1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sSTG + gemm_stg_bytes(EPI));
   uint64_t* full_bar = bars;                       // [STAGES]
   uint64_t* empty_bar = bars + STAGES;             // [STAGES]
   uint64_t* tfull_bar = bars + 2 * STAGES;         // accumulator ready
@@ -479,14 +522,13 @@ __global__ void __launch_bounds__(32 * (3 + EPW), 1)
     const int half = (warp - 2) >> 2;       // accumulator columns [NCOL*half, NCOL*half + NCOL)
     const int m = q * 32 + lane;            // tile row owned by this thread
     uint32_t acc_phase = 0;
-    // The per-tile scalars are loaded one tile ahead: their global-memory latency hides under
-    // the current tile's epilogue, which matters when the epilogue is the bottleneck.
-    EpiScalars sc_next{};
-    if (blockIdx.x < total) sc_next = epi_prefetch<EPI>(p, (int)blockIdx.x / n_ntiles, m);
+    // Per-tile scalars arrive ahead of their tile (EpiPrefetch): their global-memory latency
+    // hides under the epilogues before, which matters when the epilogue is the bottleneck.
+    const auto mtile_of = [n_ntiles](int t) { return t / n_ntiles; };
+    EpiPrefetch<EPI, decltype(mtile_of)> pf(p, mtile_of, (int)blockIdx.x, (int)gridDim.x, total, m);
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const int mt = t / n_ntiles, nt = t % n_ntiles;
-      const EpiScalars sc = sc_next;
-      if (t + (int)gridDim.x < total) sc_next = epi_prefetch<EPI>(p, (t + (int)gridDim.x) / n_ntiles, m);
+      const EpiScalars sc = pf.next(p, mtile_of, t, (int)gridDim.x, total, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
@@ -715,13 +757,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMMP_THREADS, 1)
     const int m = q * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty_bar), 0);
     uint32_t acc_phase = 0;
-    EpiScalars sc_next{};                    // per-tile scalars, loaded one tile ahead
-    if (cluster_id < total) sc_next = epi_prefetch<EPI>(p, 2 * (cluster_id / n_ntiles) + (int)crank, m);
+    const int crank_i = (int)crank;
+    const auto mtile_of = [n_ntiles, crank_i](int t) { return 2 * (t / n_ntiles) + crank_i; };
+    EpiPrefetch<EPI, decltype(mtile_of)> pf(p, mtile_of, cluster_id, n_clusters, total, m);   // per-tile scalars
     for (int t = cluster_id; t < total; t += n_clusters) {
       const int pt = t / n_ntiles, nt = t % n_ntiles;
       const int mt = 2 * pt + (int)crank;
-      const EpiScalars sc = sc_next;
-      if (t + n_clusters < total) sc_next = epi_prefetch<EPI>(p, 2 * ((t + n_clusters) / n_ntiles) + (int)crank, m);
+      const EpiScalars sc = pf.next(p, mtile_of, t, n_clusters, total, m);
       if (!mbar_wait(smem_u32(tfull_bar), acc_phase, p.status, MHMOE_ERR_TIMEOUT, timeout)) break;
       acc_phase ^= 1;
       tc_fence_after();
