@@ -75,7 +75,9 @@ __device__ __forceinline__ void topk_insert(float v, int e, float sc, float (&tv
   ts[0] = top ? sc : ts[0];
 }
 
-template <int KM>
+// SF: the score function (0 softmax, 1 sigmoid), fixed per instantiation so the per-score
+// code carries no branch on it.
+template <int KM, int SF>
 __global__ void __launch_bounds__(RT_THREADS, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmG,
                      const RouterParams p) {
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       // pass 1: row max over this group's columns (and the optional logits output); the
       // sigmoid scores need neither, so without a logits output the pass is skipped
       float mx = -INFINITY;
-      const bool pass1 = p.score_func == 0 || p.logits;
+      const bool pass1 = SF == 0 || p.logits;
       for (int c = c0; pass1 && c < c1; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
@@ -231,14 +233,14 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           }
         }
       }
-      if (p.score_func == 0) {
+      if (SF == 0) {
         red_max[g * 128 + m] = mx;
         if (!quarter_sync()) break;
         mx = fmaxf(fmaxf(red_max[m], red_max[128 + m]), fmaxf(red_max[256 + m], red_max[384 + m]));
       }
       // pass 2: softmax denominator, ascending experts within the group, groups in order
       float sum = 0.f;
-      if (p.score_func == 0) {
+      if (SF == 0) {
         float part = 0.f;
         for (int c = c0; c < c1; ++c) {
           MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
@@ -265,16 +267,34 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         ts[j] = 0.f;
         ti[j] = 0;
       }
+      // score of logit l: softmax exp(l - max) / sum, or sigmoid 1 / (1 + exp(-l)) (the
+      // correctly rounded reciprocal equals the correctly rounded quotient 1 / y)
+      auto score_of = [&](float l) -> float {
+        if constexpr (SF == 0) return __fdiv_rn(expf(l - mx), sum);
+        else return __frcp_rn(1.0f + expf(-l));
+      };
+      // without logit or selection bias the selection value is the score: a loop with no
+      // per-score branches
+      const bool plain = lb == nullptr && p.bias == nullptr;
       for (int c = c0; c < c1; ++c) {
         MHMOE_TMEM_LD_32x32b_X32(taddr + c * 32, r);
         tmem_wait_ld();
+        if (plain) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int e = c * 32 + i;
+            const float sc = score_of(__uint_as_float(r[i]));
+            topk_insert<KM>(e < p.E ? sc : -INFINITY, e, sc, tv, ti, ts);
+          }
+          continue;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int e = c * 32 + i;
           float v = -INFINITY, sc = 0.f;
           if (e < p.E) {
             const float l = lb ? __fadd_rn(__uint_as_float(r[i]), lb[e]) : __uint_as_float(r[i]);
-            sc = p.score_func == 0 ? __fdiv_rn(expf(l - mx), sum) : __fdiv_rn(1.0f, 1.0f + expf(-l));
+            sc = score_of(l);
             v = p.bias ? __fadd_rn(sc, p.bias[(int64_t)h * p.E + e]) : sc;
           }
           topk_insert<KM>(v, e, sc, tv, ti, ts);
@@ -424,12 +444,13 @@ int router_tc(const __nv_bfloat16* x, int64_t sx_s, const __nv_bfloat16* gate_pl
   p.stages = std::min(RT_MAX_STAGES, (227 * 1024 - fixed) / stage_bytes);
   const int smem = p.stages * stage_bytes + fixed;
   // top-K lists of 8 entries cover K <= 8; 16 entries otherwise (K <= 16)
-  auto kernel = K <= 8 ? router_tc_kernel<8> : router_tc_kernel<16>;
+  auto kernel = K <= 8 ? (score_func == 0 ? router_tc_kernel<8, 0> : router_tc_kernel<8, 1>)
+                       : (score_func == 0 ? router_tc_kernel<16, 0> : router_tc_kernel<16, 1>);
   static PerDeviceOnce once;
   const cudaError_t attr = once.run([](int) {
-    cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(router_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaSuccess;
+    for (auto k : {router_tc_kernel<8, 0>, router_tc_kernel<8, 1>, router_tc_kernel<16, 0>, router_tc_kernel<16, 1>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     return e;
   });
   if (attr != cudaSuccess) {
